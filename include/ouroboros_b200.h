@@ -1,0 +1,174 @@
+/*
+ * ouroboros_b200.h — C ABI of libouroboros_b200.so
+ *
+ * The drop-in boundary for paged block attention on B200 (sm_100a):
+ *   1. the native KV-block allocator and its page-table export, which replace
+ *      the reference's pybind11 module `ouroboros_cpp` (src/cpp/bindings.cpp:26-86)
+ *      and the Python page-table builders (src/block_table.py:187-222);
+ *   2. the attention launchers, which replace the Triton kernel launched by
+ *      src/kernels/block_attention.py:368-527.
+ *
+ * Conventions
+ *   - Every entry point returns an int status: OURO_OK (0) or a negative
+ *     OURO_E* code. ouro_last_error() returns a thread-local message for the
+ *     most recent failure on the calling thread (the reference raises
+ *     RuntimeError with the same texts).
+ *   - Tensor arguments are raw device pointers plus sizes; nothing here knows
+ *     about torch. Launchers are asynchronous on the given cudaStream_t
+ *     (passed as void*; NULL = legacy default stream) and never synchronise.
+ *   - Layouts (all row-major, contiguous):
+ *       k_cache / v_cache / q_cache  [n_phys, H, 64, D]
+ *       page_table                   [S, max_blocks] int32, -1 past the chain
+ *       cos / sin                    [max_positions, D/2] fp32
+ */
+#ifndef OUROBOROS_B200_H_
+#define OUROBOROS_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+  OURO_OK = 0,
+  OURO_EINVAL = -1,      /* bad argument: shape, size, null pointer */
+  OURO_EALLOC = -2,      /* allocator rule violated (message says which) */
+  OURO_EUNSUPPORTED = -3,/* dtype / head_dim / group size not built */
+  OURO_ECUDA = -4,       /* a CUDA runtime call failed */
+  OURO_EPAGETABLE = -5   /* page-table entry out of range or not PAD past the chain */
+};
+
+enum { OURO_F32 = 0, OURO_F16 = 1, OURO_BF16 = 2 };
+
+#define OURO_BLOCK_TOKENS 64
+#define OURO_PAD_ID (-1)
+
+/* Message for the last failure on this thread ("" if none). */
+const char* ouro_last_error(void);
+/* Library version string. */
+const char* ouro_version(void);
+
+/* ------------------------------------------------------------------------
+ * KV-block allocator.  Replaces ouroboros::BlockTable
+ * (src/cpp/block_table.h:23-80, src/cpp/block_table.cpp:16-166) and the
+ * Python twin src/block_table.py:59-209 with identical allocation order,
+ * all-or-nothing chains and error texts.
+ * ---------------------------------------------------------------------- */
+typedef struct ouro_block_table ouro_block_table;
+
+/* BlockTable(max_blocks)                       block_table.py:67-74 */
+int ouro_bt_create(int32_t max_blocks, ouro_block_table** out);
+void ouro_bt_destroy(ouro_block_table* bt);
+int32_t ouro_bt_max_blocks(const ouro_block_table* bt);
+/* num_free                                     block_table.py:207-209 */
+int32_t ouro_bt_num_free(const ouro_block_table* bt);
+/* is_allocated                                 block_table.h:30 */
+int32_t ouro_bt_is_allocated(const ouro_block_table* bt, int32_t id);
+/* allocate_block                               block_table.py:76-87 */
+int ouro_bt_allocate_block(ouro_block_table* bt, int32_t* out_id);
+/* free_block                                   block_table.py:89-94 */
+int ouro_bt_free_block(ouro_block_table* bt, int32_t id);
+/* link                                         block_table.py:101-105 */
+int ouro_bt_link(ouro_block_table* bt, int32_t prev_id, int32_t next_id);
+/* allocate_chain                               block_table.py:112-130 */
+int ouro_bt_allocate_chain(ouro_block_table* bt, int32_t n_blocks, int32_t* out_head);
+/* expand_chain                                 block_table.py:152-165 */
+int ouro_bt_expand_chain(ouro_block_table* bt, int32_t tail, int32_t* out_new_tail);
+/* chain_len                                    block_table.py:147-150 */
+int ouro_bt_chain_len(const ouro_block_table* bt, int32_t head, int32_t* out_len);
+/* Last block of the chain (no reference counterpart; serving.py:194-197 walks for it). */
+int ouro_bt_chain_tail(const ouro_block_table* bt, int32_t head, int32_t* out_tail);
+/* walk: writes up to `cap` ids, *out_len = chain length   block_table.py:132-145 */
+int ouro_bt_walk(const ouro_block_table* bt, int32_t head, int32_t* out_ids, int32_t cap,
+                 int32_t* out_len);
+/* resolve_block                                block_table.py:167-185 */
+int ouro_bt_resolve_block(const ouro_block_table* bt, int32_t head, int32_t logical_idx,
+                          int32_t* out_id);
+/* Frees a whole chain (serving.py:159-169 does this walk-then-free in Python). */
+int ouro_bt_free_chain(ouro_block_table* bt, int32_t head, int32_t* out_freed);
+/* build_page_table(table, heads, pad_to) into one [n_heads, pad_to] int32
+ * buffer (host memory; pin it for an async H2D copy).  block_table.py:187-222 */
+int ouro_bt_export_page_table(const ouro_block_table* bt, const int32_t* heads,
+                              int32_t n_heads, int32_t pad_to, int32_t* out);
+/* next_ptr[id] of an allocated block          block_table.cpp:166-169 */
+int ouro_bt_next(const ouro_block_table* bt, int32_t id, int32_t* out_next);
+/* Whole-state snapshots (the bindings' next_ptr view, bindings.cpp:59-67):
+ * next_out[max_blocks] (-1 for free slots), live_out[max_blocks] 0/1,
+ * free_out[num_free] bottom-to-top of the LIFO stack. Any may be NULL. */
+int ouro_bt_snapshot(const ouro_block_table* bt, int32_t* next_out, uint8_t* live_out,
+                     int32_t* free_out);
+/* Live pointer to the 64 payload cells of an allocated block (get_block,
+ * block_table.py:96-99). Valid until the block is freed or the table destroyed. */
+int ouro_bt_payload(ouro_block_table* bt, int32_t id, int32_t** out_cells);
+
+/* ------------------------------------------------------------------------
+ * Paged decode: one query token per sequence over its paged K/V.
+ *
+ * Replaces the decode use of the Triton kernel launched at
+ * src/kernels/block_attention.py:503-526 (the reference computes every row
+ * of the self-attention; a decode step needs the last one) and the
+ * host-side checks of block_attention.py:433-470.  Adds GQA, explicit query
+ * positions, split-K and the token-granular Table-1 scope.
+ *
+ * Semantics, per sequence s with L = seq_lens[s] and p = positions[s]
+ * (default L - 1):
+ *   keys j in [0, L) (j <= p when causal), skipped when the block mask
+ *   element (s, p / 64, j / 64) is 0 or, with a scope, when
+ *   !(scope_tags[s, j] || span_lo <= j < span_hi);
+ *   RoPE (half-split pairs d, d + D/2) at position p on q and j on k_j;
+ *   out[s, h] = softmax_j(q_h . k_j * scale) @ v_j  with KV head h / (Hq / Hkv).
+ * A sequence with no allowed key gets a zero row.
+ * ---------------------------------------------------------------------- */
+typedef struct ouro_decode_args {
+  const void* q;              /* [S, Hq, D], dtype */
+  const void* k_cache;        /* [n_phys, Hkv, 64, D], dtype */
+  const void* v_cache;        /* [n_phys, Hkv, 64, D], dtype */
+  const int32_t* page_table;  /* [S, max_blocks], -1 past the chain */
+  const int32_t* seq_lens;    /* [S] */
+  const int32_t* positions;   /* [S] query positions, or NULL for seq_len - 1 */
+  const float* cos;           /* [max_positions, D/2] */
+  const float* sin;           /* [max_positions, D/2] */
+  const int8_t* block_mask;   /* optional; element (s, qb, kb) at the given strides */
+  int64_t mask_stride_s, mask_stride_q, mask_stride_k;
+  const uint8_t* scope_tags;  /* optional [S, scope_stride], 1 = GLOBAL token;
+                                 16-byte aligned with scope_stride % 16 == 0 for the
+                                 tensor-core kernel */
+  int64_t scope_stride;
+  const int32_t* scope_span;  /* optional [S, 2]: the query's LOCAL span [lo, hi) */
+  void* out;                  /* [S, Hq, D], dtype */
+  void* workspace;            /* split-K partials, >= ouro_decode_plan's bytes, 16-B aligned */
+  size_t workspace_bytes;
+  int32_t* status;            /* optional device int32: bit 1 bad page entry,
+                                 bit 2 wait timeout, bit 4 position outside the tables */
+  int32_t num_seqs, num_q_heads, num_kv_heads, head_dim;
+  int32_t max_blocks, num_phys_blocks, max_positions;
+  int32_t dtype;              /* OURO_F32 / OURO_F16 / OURO_BF16 */
+  int32_t split_blocks;       /* blocks per split-K chunk; 0 = chosen from the SM count */
+  int32_t causal;             /* 1: keys j <= positions[s] only */
+  int32_t kernel;             /* 0 auto, 1 CUDA cores, 2 tensor cores */
+  float softmax_scale;        /* <= 0: 1/sqrt(D) */
+} ouro_decode_args;
+
+/* Split-K plan for these arguments: blocks per chunk, chunks per sequence
+ * (upper bound), workspace bytes the caller must provide, kernel choice. */
+int ouro_decode_plan(const ouro_decode_args* args, int32_t* split_blocks, int32_t* max_splits,
+                     size_t* workspace_bytes, int32_t* uses_tensor_cores);
+/* Launches decode (+ the combine kernel when a sequence spans >1 chunk). */
+int ouro_paged_decode(const ouro_decode_args* args, void* stream);
+
+/* Device-side page-table check (the reference's host loop,
+ * block_attention.py:445-466): `report` is one device uint64 that ends as
+ * UINT64_MAX when every entry is valid, else (flat_index << 2 | code) of the
+ * lowest bad entry, code 1 = out of [0, n_phys), 2 = not PAD past the chain,
+ * 3 = sequence longer than the table or negative length. */
+int ouro_validate_page_table(const int32_t* page_table, const int32_t* seq_lens,
+                             int32_t num_seqs, int32_t max_blocks, int32_t num_phys_blocks,
+                             void* report, void* stream);
+
+#ifdef __cplusplus
+}  /* extern "C" */
+#endif
+
+#endif  /* OUROBOROS_B200_H_ */

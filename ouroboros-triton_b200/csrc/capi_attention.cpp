@@ -1,0 +1,198 @@
+// extern "C" launchers for the paged-attention kernels (include/ouroboros_b200.h).
+// Validates sizes and pointers, picks the kernel and split-K plan, launches on
+// the caller's stream. No synchronisation and no allocation happen here: the
+// split-K workspace is passed in by the caller (sized by ouro_decode_plan).
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <string>
+
+#include "attention.hpp"
+#include "block_table.hpp"
+#include "capi_common.hpp"
+
+using ouro::fail;
+
+namespace {
+
+int dtype_bytes(int dtype) {
+  switch (dtype) {
+    case OURO_F32: return 4;
+    case OURO_F16: return 2;
+    case OURO_BF16: return 2;
+    default: return 0;
+  }
+}
+
+void check_cuda(cudaError_t e, const char* what) {
+  if (e != cudaSuccess) {
+    cudaGetLastError();  // clear the sticky-free error state for the next call
+    fail(OURO_ECUDA, std::string(what) + ": " + cudaGetErrorString(e));
+  }
+}
+
+int num_sms() {
+  int dev = 0, n = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess) {
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) n = 148;
+  }
+  cudaGetLastError();
+  return n > 0 ? n : 148;
+}
+
+int hpc_of(int hkv) {
+  for (int h : {8, 4, 2, 1})
+    if (hkv % h == 0) return h;
+  return 1;
+}
+
+// Fills a DecodeParams from the C struct (no split plan yet).
+ouro::DecodeParams to_params(const ouro_decode_args* a) {
+  if (a == nullptr) fail(OURO_EINVAL, "null decode args");
+  ouro::DecodeParams p{};
+  p.q = a->q;
+  p.k = a->k_cache;
+  p.v = a->v_cache;
+  p.page_table = a->page_table;
+  p.seq_lens = a->seq_lens;
+  p.positions = a->positions;
+  p.cos = a->cos;
+  p.sin = a->sin;
+  p.block_mask = a->block_mask;
+  p.mask_s = a->mask_stride_s;
+  p.mask_q = a->mask_stride_q;
+  p.mask_k = a->mask_stride_k;
+  p.scope_tags = a->scope_tags;
+  p.scope_stride = a->scope_stride;
+  p.scope_span = a->scope_span;
+  p.out = a->out;
+  p.status = a->status;
+  p.S = a->num_seqs;
+  p.Hq = a->num_q_heads;
+  p.Hkv = a->num_kv_heads;
+  p.D = a->head_dim;
+  p.max_blocks = a->max_blocks;
+  p.n_phys = a->num_phys_blocks;
+  p.max_pos = a->max_positions;
+  p.causal = a->causal ? 1 : 0;
+  const float scale = a->softmax_scale > 0.f ? a->softmax_scale
+                                             : 1.0f / std::sqrt(static_cast<float>(a->head_dim));
+  p.scale_log2 = scale * ouro::kLog2e;
+
+  if (dtype_bytes(a->dtype) == 0) fail(OURO_EUNSUPPORTED, "unsupported dtype code");
+  if (p.S < 0) fail(OURO_EINVAL, "num_seqs must be >= 0");
+  if (p.Hq <= 0 || p.Hkv <= 0 || p.Hq % p.Hkv != 0)
+    fail(OURO_EINVAL, "num_q_heads must be a positive multiple of num_kv_heads, got " +
+                          std::to_string(p.Hq) + " and " + std::to_string(p.Hkv));
+  p.G = p.Hq / p.Hkv;
+  if (p.D < 2 || p.D % 2 != 0 || p.D > 256)
+    fail(OURO_EUNSUPPORTED, "head dim must be even and in [2, 256], got " + std::to_string(p.D));
+  if (p.max_blocks < 0 || p.n_phys <= 0 || p.max_pos <= 0)
+    fail(OURO_EINVAL, "max_blocks, num_phys_blocks and max_positions must be positive");
+  if (p.S > 0 && (!p.q || !p.k || !p.v || !p.page_table || !p.seq_lens || !p.cos || !p.sin ||
+                  !p.out))
+    fail(OURO_EINVAL, "null tensor pointer in decode args");
+  if (p.scope_tags && p.scope_stride < 1) fail(OURO_EINVAL, "scope_stride must be >= 1");
+  return p;
+}
+
+int choose_split(const ouro::DecodeParams& p, bool tc, int waves) {
+  const int hpc = tc ? hpc_of(p.Hkv) : 1;
+  const int64_t groups = tc ? p.Hkv / hpc : static_cast<int64_t>(p.Hkv) * ((p.G + 7) / 8);
+  const int64_t work = static_cast<int64_t>(p.S) * groups * std::max(p.max_blocks, 1);
+  const int64_t target = static_cast<int64_t>(num_sms()) * std::max(waves, 1);
+  int64_t split = (work + target - 1) / std::max<int64_t>(target, 1);
+  split = std::max<int64_t>(split, 4);
+  split = std::min<int64_t>(split, std::max(p.max_blocks, 1));
+  split = std::min<int64_t>(split, 1024);
+  return static_cast<int>(std::max<int64_t>(split, 1));
+}
+
+// Completes the plan: kernel choice, split size, max splits, workspace bytes.
+void plan(ouro::DecodeParams& p, const ouro_decode_args* a, bool* use_tc, size_t* ws_bytes) {
+  const bool tc_ok = ouro::decode_tc_supported(
+      [&] {
+        ouro::DecodeParams t = p;
+        t.split_blocks = 1;
+        return t;
+      }(),
+      a->dtype);
+  bool tc = false;
+  if (a->kernel == 0) tc = tc_ok;
+  else if (a->kernel == 2) {
+    if (!tc_ok) fail(OURO_EUNSUPPORTED, "tensor-core decode not built for this dtype/head_dim/group");
+    tc = true;
+  } else if (a->kernel != 1) {
+    fail(OURO_EINVAL, "kernel selector must be 0 (auto), 1 (cuda cores) or 2 (tensor cores)");
+  }
+  int split = a->split_blocks > 0 ? a->split_blocks : choose_split(p, tc, 16);
+  split = std::min(split, std::max(p.max_blocks, 1));
+  if (tc) split = std::min(split, 1024);
+  p.split_blocks = split;
+  p.max_splits = std::max(1, (p.max_blocks + split - 1) / split);
+  *use_tc = tc;
+  *ws_bytes = p.max_splits > 1
+                  ? static_cast<size_t>(p.S) * p.Hq * p.max_splits * (p.D + 2) * sizeof(float)
+                  : 0;
+}
+
+}  // namespace
+
+extern "C" {
+
+int ouro_decode_plan(const ouro_decode_args* args, int32_t* split_blocks, int32_t* max_splits,
+                     size_t* workspace_bytes, int32_t* uses_tensor_cores) {
+  OURO_CAPI_GUARD({
+    ouro::DecodeParams p = to_params(args);
+    bool tc = false;
+    size_t ws = 0;
+    plan(p, args, &tc, &ws);
+    if (split_blocks) *split_blocks = p.split_blocks;
+    if (max_splits) *max_splits = p.max_splits;
+    if (workspace_bytes) *workspace_bytes = ws;
+    if (uses_tensor_cores) *uses_tensor_cores = tc ? 1 : 0;
+  })
+}
+
+int ouro_paged_decode(const ouro_decode_args* args, void* stream) {
+  OURO_CAPI_GUARD({
+    ouro::DecodeParams p = to_params(args);
+    bool tc = false;
+    size_t ws = 0;
+    plan(p, args, &tc, &ws);
+    if (p.S == 0) return OURO_OK;
+    if (ws > 0) {
+      if (args->workspace == nullptr || args->workspace_bytes < ws)
+        fail(OURO_EINVAL, "decode workspace too small: need " + std::to_string(ws) + " bytes");
+      if ((reinterpret_cast<uintptr_t>(args->workspace) & 15u) != 0)
+        fail(OURO_EINVAL, "decode workspace must be 16-byte aligned");
+      p.ws_o = static_cast<float*>(args->workspace);
+      p.ws_ml = p.ws_o + static_cast<size_t>(p.S) * p.Hq * p.max_splits * p.D;
+    }
+    auto st = static_cast<cudaStream_t>(stream);
+    if (tc) check_cuda(ouro::launch_decode_tc(p, args->dtype, st), "decode (tensor cores)");
+    else check_cuda(ouro::launch_decode_simt_dtype(p, args->dtype, st), "decode (cuda cores)");
+    if (p.max_splits > 1)
+      check_cuda(ouro::launch_decode_combine_dtype(p, args->dtype, st), "decode combine");
+  })
+}
+
+int ouro_validate_page_table(const int32_t* page_table, const int32_t* seq_lens, int32_t num_seqs,
+                             int32_t max_blocks, int32_t num_phys_blocks, void* report,
+                             void* stream) {
+  OURO_CAPI_GUARD({
+    if (num_seqs < 0 || max_blocks < 0) fail(OURO_EINVAL, "negative page-table size");
+    if (report == nullptr) fail(OURO_EINVAL, "null report pointer");
+    auto st = static_cast<cudaStream_t>(stream);
+    check_cuda(cudaMemsetAsync(report, 0xff, sizeof(unsigned long long), st), "report reset");
+    if (static_cast<int64_t>(num_seqs) * max_blocks == 0) return OURO_OK;
+    if (!page_table || !seq_lens) fail(OURO_EINVAL, "null page table or seq_lens");
+    check_cuda(ouro::launch_validate_page_table(page_table, seq_lens, num_seqs, max_blocks,
+                                                num_phys_blocks,
+                                                static_cast<unsigned long long*>(report), st),
+               "page-table check");
+  })
+}
+
+}  // extern "C"

@@ -1,0 +1,382 @@
+"""Paged block attention on B200: the drop-in for the reference module
+``src/kernels/block_attention.py``.
+
+Entry points
+  * :func:`block_attention_decode` — one query token per sequence (the decode
+    step) over its paged K/V: GQA, explicit positions, split-K, fused RoPE,
+    block mask and token-granular Table-1 scope. sm_100a kernels in
+    ``csrc/decode_tc.cu`` (tensor cores) and ``csrc/decode_simt.cu``.
+  * :func:`validate_bias_shape`, :func:`validate_mask_shape`,
+    :func:`_broadcast_strides` — the reference's pure-Python helpers
+    (block_attention.py:90-178), same rules and messages.
+
+Every launcher calls the native library through its C ABI
+(``include/ouroboros_b200.h``). There is no Triton and no CPU path: without a
+CUDA device, or without the built library, calls raise RuntimeError.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from typing import Sequence
+
+try:  # import safety, as in the reference (block_attention.py:55-71)
+    import torch
+
+    HAS_TORCH = True
+except ImportError:  # pragma: no cover
+    torch = None  # type: ignore[assignment]
+    HAS_TORCH = False
+
+from .. import _native
+from ..block_table import BLOCK_SIZE, PAD_ID
+from . import _capi
+
+#: The reference's flag for its Triton backend. This implementation never uses
+#: Triton; the flag stays for import compatibility and is always False.
+HAS_TRITON = False
+
+__all__ = [
+    "HAS_TRITON",
+    "HAS_TORCH",
+    "block_attention_decode",
+    "decode_plan",
+    "validate_bias_shape",
+    "validate_mask_shape",
+    "validate_page_table",
+]
+
+_KERNELS = {"auto": 0, "simt": 1, "cuda_cores": 1, "tensor_cores": 2, "tc": 2}
+
+
+# ---------------------------------------------------------------------------
+# Shape helpers (reference block_attention.py:90-178)
+# ---------------------------------------------------------------------------
+
+
+def validate_bias_shape(bias_shape: Sequence[int], *, num_heads: int, q_len: int, kv_len: int,
+                        num_seqs: int | None = None) -> None:
+    """Bias must broadcast to [S, H, Q, K] (right-aligned, dims equal or 1)."""
+    shape = tuple(int(d) for d in bias_shape)
+    targets = (num_seqs if num_seqs is not None else 1, num_heads, q_len, kv_len)
+    if len(shape) > 4:
+        raise RuntimeError(f"bias rank {len(shape)} > 4, cannot broadcast to [S, H, Q, K]")
+    padded = (1,) * (4 - len(shape)) + shape
+    for got, want in zip(padded, targets):
+        if got != 1 and got != want:
+            raise RuntimeError(
+                f"bias dim {got} incompatible with expected {want} "
+                f"(shape {shape} vs [S={targets[0]}, H={num_heads}, Q={q_len}, K={kv_len}])")
+
+
+def validate_mask_shape(mask_shape: Sequence[int], *, num_q_blocks: int, num_kv_blocks: int,
+                        num_seqs: int | None = None) -> None:
+    """Block mask must broadcast to [S, QB, KB]; a rank-1 mask is per KV block."""
+    shape = tuple(int(d) for d in mask_shape)
+    targets = (num_seqs if num_seqs is not None else 1, num_q_blocks, num_kv_blocks)
+    if len(shape) > 3:
+        raise RuntimeError(f"mask rank {len(shape)} > 3, cannot broadcast to [S, QB, KB]")
+    padded = (1, 1, shape[0]) if len(shape) == 1 else (1,) * (3 - len(shape)) + shape
+    for got, want in zip(padded, targets):
+        if got != 1 and got != want:
+            raise RuntimeError(
+                f"mask dim {got} incompatible with expected {want} "
+                f"(shape {shape} vs [S={targets[0]}, QB={num_q_blocks}, KB={num_kv_blocks}])")
+
+
+def _broadcast_strides(shape: Sequence[int], target: Sequence[int]) -> tuple[int, ...]:
+    """Element strides of a contiguous ``shape`` viewed under ``target``; broadcast axes get 0."""
+    shape = tuple(int(d) for d in shape)
+    if len(shape) > len(target):
+        raise RuntimeError(f"rank {len(shape)} exceeds target rank {len(target)}")
+    padded = (1,) * (len(target) - len(shape)) + shape
+    for got, want in zip(padded, target):
+        if got != 1 and got != want:
+            raise RuntimeError(f"dim {got} incompatible with {want}")
+    strides, running = [], 1
+    for ax in range(len(target) - 1, -1, -1):
+        strides.append(0 if padded[ax] == 1 else running)
+        running *= padded[ax]
+    return tuple(reversed(strides))
+
+
+# ---------------------------------------------------------------------------
+# Device plumbing
+# ---------------------------------------------------------------------------
+
+
+def _require_cuda() -> None:
+    if not HAS_TORCH:
+        raise RuntimeError("block attention requires torch (not installed on this host)")
+    if not torch.cuda.is_available():
+        raise RuntimeError("block_attention requires a CUDA device")
+    _native.lib()  # raises if the native library is not built
+
+
+def _dtype_code(dt) -> int:
+    if dt == torch.float32:
+        return _native.DTYPE_F32
+    if dt == torch.float16:
+        return _native.DTYPE_F16
+    if dt == torch.bfloat16:
+        return _native.DTYPE_BF16
+    raise RuntimeError(f"unsupported cache dtype {dt}; want float32, float16 or bfloat16")
+
+
+def _device_of(*tensors):
+    for t in tensors:
+        if t is not None and hasattr(t, "is_cuda") and t.is_cuda:
+            return t.device
+    return torch.device("cuda", torch.cuda.current_device())
+
+
+def _on(t, device, dtype=None):
+    """``t`` as a contiguous tensor on ``device`` (converted from lists/ints if needed)."""
+    if t is None:
+        return None
+    if not torch.is_tensor(t):
+        t = torch.as_tensor(t)
+    t = t.to(device=device, dtype=dtype if dtype is not None else t.dtype, non_blocking=True)
+    return t.contiguous()
+
+
+def _ptr(t) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def _stream_handle(device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def validate_page_table(page_table, seq_lens, num_phys_blocks: int) -> None:
+    """Raises RuntimeError on the first bad page-table entry.
+
+    The reference checks every entry on the host after ``.tolist()``
+    (block_attention.py:445-466); here one device pass finds the lowest bad
+    entry and 8 bytes come back. Same message texts.
+    """
+    _require_cuda()
+    S, max_b = page_table.shape
+    device = page_table.device
+    report = torch.empty(1, dtype=torch.int64, device=device)
+    _native.check(_native.lib().ouro_validate_page_table(
+        _ptr(page_table), _ptr(seq_lens), S, max_b, int(num_phys_blocks), _ptr(report),
+        _stream_handle(device)), "validate_page_table")
+    key = int(report.item()) & 0xFFFFFFFFFFFFFFFF
+    if key == 0xFFFFFFFFFFFFFFFF:
+        return
+    idx, code = key >> 2, key & 3
+    s, n = divmod(idx, max_b) if max_b else (idx, 0)
+    if code == 3:
+        ln = int(seq_lens[s].item())
+        need = -(-ln // BLOCK_SIZE)
+        if ln < 0:
+            raise RuntimeError(f"sequence {s} has negative length {ln}")
+        raise RuntimeError(f"sequence {s} needs {need} blocks > table width {max_b}")
+    phys = int(page_table[s, n].item())
+    if code == 2:
+        ln = int(seq_lens[s].item())
+        raise RuntimeError(
+            f"page_table[{s}][{n}] must be PAD_ID({PAD_ID}) beyond seq_len {ln}, got {phys}")
+    raise RuntimeError(
+        f"page_table[{s}][{n}]={phys} out of range for {num_phys_blocks} physical blocks")
+
+
+_SM_SCOPE_ALIGN = 16
+
+
+def _scope_tensors(scope, S: int, device):
+    """(tags [S, W] uint8 with W % 16 == 0, span [S, 2] int32) from ``scope``.
+
+    ``scope`` is ``(tags, span)``: tags [S, L] (bool / uint8, 1 = GLOBAL token)
+    and span [S, 2] (the query's LOCAL span, (0, 0) for a GLOBAL query).
+    """
+    tags, span = scope
+    tags = torch.as_tensor(tags)
+    if tags.dim() != 2 or tags.shape[0] != S:
+        raise RuntimeError(f"scope tags must be [S={S}, L], got {tuple(tags.shape)}")
+    L = tags.shape[1]
+    W = max(_SM_SCOPE_ALIGN, -(-L // _SM_SCOPE_ALIGN) * _SM_SCOPE_ALIGN)
+    padded = torch.zeros((S, W), dtype=torch.uint8, device=device)
+    padded[:, :L] = tags.to(device=device, dtype=torch.uint8)
+    span = _on(span, device, torch.int32)
+    if span is None or tuple(span.shape) != (S, 2):
+        raise RuntimeError(f"scope span must be [S={S}, 2]")
+    return padded, span
+
+
+def _decode_args(page_table, q, k_cache, v_cache, seq_lens, cos, sin, positions, mask, scope,
+                 causal, softmax_scale, split_blocks, kernel, out, workspace, status):
+    S, Hq, D = q.shape
+    n_phys, Hkv, blk, Dk = k_cache.shape
+    a = _capi.DecodeArgs()
+    a.q, a.k_cache, a.v_cache = _ptr(q), _ptr(k_cache), _ptr(v_cache)
+    a.page_table, a.seq_lens = _ptr(page_table), _ptr(seq_lens)
+    a.positions = _ptr(positions)
+    a.cos, a.sin = _ptr(cos), _ptr(sin)
+    if mask is not None:
+        a.block_mask = _ptr(mask[0])
+        a.mask_stride_s, a.mask_stride_q, a.mask_stride_k = mask[1]
+    if scope is not None:
+        a.scope_tags = _ptr(scope[0])
+        a.scope_stride = scope[0].shape[1]
+        a.scope_span = _ptr(scope[1])
+    a.out = _ptr(out)
+    if workspace is not None:
+        a.workspace = _ptr(workspace)
+        a.workspace_bytes = workspace.numel() * workspace.element_size()
+    a.status = _ptr(status)
+    a.num_seqs, a.num_q_heads, a.num_kv_heads, a.head_dim = S, Hq, Hkv, D
+    a.max_blocks = page_table.shape[1]
+    a.num_phys_blocks = n_phys
+    a.max_positions = cos.shape[0]
+    a.dtype = _dtype_code(k_cache.dtype)
+    a.split_blocks = int(split_blocks)
+    a.causal = 1 if causal else 0
+    a.kernel = _KERNELS[kernel]
+    a.softmax_scale = float(softmax_scale) if softmax_scale is not None else 0.0
+    return a
+
+
+def decode_plan(args: "_capi.DecodeArgs") -> dict:
+    """Split-K plan the library picks for these arguments."""
+    split, nsplit, tc = ctypes.c_int32(), ctypes.c_int32(), ctypes.c_int32()
+    ws = ctypes.c_size_t()
+    _native.check(_native.lib().ouro_decode_plan(ctypes.byref(args), ctypes.byref(split),
+                                                 ctypes.byref(nsplit), ctypes.byref(ws),
+                                                 ctypes.byref(tc)), "decode plan")
+    return {"split_blocks": split.value, "max_splits": nsplit.value,
+            "workspace_bytes": ws.value, "tensor_cores": bool(tc.value)}
+
+
+class DecodeCall:
+    """A prepared decode launch: validated, device-resident arguments.
+
+    Building one does the checks and conversions once; :meth:`launch` then
+    only enqueues the kernels on the current stream (no host work besides the
+    C call), so a serving loop or a CUDA graph can replay it.
+    """
+
+    def __init__(self, page_table, q, k_cache, v_cache, seq_lens, cos, sin, *, positions=None,
+                 mask=None, scope=None, causal=False, softmax_scale=None, out=None,
+                 validate=True, split_blocks=0, kernel="auto", workspace=None, status=None):
+        _require_cuda()
+        if kernel not in _KERNELS:
+            raise RuntimeError(f"kernel must be one of {sorted(_KERNELS)}, got {kernel!r}")
+        device = _device_of(k_cache, q, page_table, v_cache)
+        k_cache = _on(k_cache, device)
+        v_cache = _on(v_cache, device)
+        if k_cache.dim() != 4:
+            raise RuntimeError("k_cache must be [n_phys, Hkv, 64, D]")
+        n_phys, Hkv, blk, D = k_cache.shape
+        if blk != BLOCK_SIZE:
+            raise RuntimeError(f"k_cache block dim must be {BLOCK_SIZE}, got {blk}")
+        if v_cache.shape != k_cache.shape or v_cache.dtype != k_cache.dtype:
+            raise RuntimeError("k/v caches must share the [n_phys, Hkv, 64, D] layout and dtype")
+        if D < 2 or D % 2 != 0:
+            raise RuntimeError(f"head dim must be even for half-split RoPE, got {D}")
+        q = _on(q, device, k_cache.dtype)
+        if q.dim() != 3 or q.shape[2] != D:
+            raise RuntimeError(f"q must be [S, Hq, {D}], got {tuple(q.shape)}")
+        S, Hq = q.shape[0], q.shape[1]
+        if Hq % Hkv != 0:
+            raise RuntimeError(f"query heads {Hq} must be a multiple of KV heads {Hkv}")
+        page_table = _on(page_table, device)
+        if page_table.dtype not in (torch.int32, torch.int64):
+            raise RuntimeError(f"page_table must be int32/int64, got {page_table.dtype}")
+        page_table = page_table.to(torch.int32)
+        if page_table.dim() != 2 or page_table.shape[0] != S:
+            raise RuntimeError(f"page_table must be [S={S}, max_blocks]")
+        seq_lens = _on(seq_lens, device)
+        if seq_lens.dtype not in (torch.int32, torch.int64):
+            raise RuntimeError(f"seq_lens must be int32/int64, got {seq_lens.dtype}")
+        seq_lens = seq_lens.to(torch.int32)
+        if tuple(seq_lens.shape) != (S,):
+            raise RuntimeError(f"seq_lens must have shape [{S}], got {tuple(seq_lens.shape)}")
+        cos = _on(cos, device, torch.float32)
+        sin = _on(sin, device, torch.float32)
+        max_b = page_table.shape[1]
+        if cos.dim() != 2 or cos.shape != sin.shape or cos.shape[1] != D // 2:
+            raise RuntimeError(f"rope tables must be [max_positions, {D // 2}]")
+        if cos.shape[0] < max_b * BLOCK_SIZE:
+            raise RuntimeError(
+                f"rope tables must cover {max_b * BLOCK_SIZE} positions, got {cos.shape[0]}")
+        positions = _on(positions, device, torch.int32)
+        if positions is not None and tuple(positions.shape) != (S,):
+            raise RuntimeError(f"positions must have shape [{S}]")
+        mask_arg = None
+        if mask is not None:
+            mask = _on(mask, device)
+            validate_mask_shape(tuple(mask.shape), num_seqs=S, num_q_blocks=max_b,
+                                num_kv_blocks=max_b)
+            mask = mask.to(torch.int8).contiguous()
+            mask_arg = (mask, _broadcast_strides(tuple(mask.shape), (S, max_b, max_b)))
+        scope_arg = _scope_tensors(scope, S, device) if scope is not None else None
+        if validate:
+            validate_page_table(page_table, seq_lens, n_phys)
+        if out is None:
+            out = torch.empty((S, Hq, D), dtype=k_cache.dtype, device=device)
+        elif out.shape != (S, Hq, D) or out.dtype != k_cache.dtype or not out.is_contiguous():
+            raise RuntimeError(f"out must be a contiguous [S, Hq, D] {k_cache.dtype} tensor")
+        self._keep = (page_table, q, k_cache, v_cache, seq_lens, cos, sin, positions, mask_arg,
+                      scope_arg)
+        self.out = out
+        self.device = device
+        self.status = status
+        args = _decode_args(page_table, q, k_cache, v_cache, seq_lens, cos, sin, positions,
+                            mask_arg, scope_arg, causal, softmax_scale, split_blocks, kernel, out,
+                            None, status)
+        self.plan = decode_plan(args)
+        if self.plan["workspace_bytes"]:
+            need = self.plan["workspace_bytes"]
+            if workspace is None:
+                workspace = torch.empty(-(-need // 16) * 4, dtype=torch.float32, device=device)
+            elif workspace.numel() * workspace.element_size() < need:
+                raise RuntimeError(f"workspace too small: need {need} bytes")
+            args.workspace = _ptr(workspace)
+            args.workspace_bytes = workspace.numel() * workspace.element_size()
+        self.workspace = workspace
+        self.args = args
+
+    def launch(self):
+        _native.check(_native.lib().ouro_paged_decode(ctypes.byref(self.args),
+                                                      _stream_handle(self.device)), "decode")
+        return self.out
+
+
+def block_attention_decode(page_table, q, k_cache, v_cache, seq_lens, cos, sin, *,
+                           positions=None, mask=None, scope=None, causal=False,
+                           softmax_scale=None, out=None, validate=True, split_blocks=0,
+                           kernel="auto", workspace=None, status=None):
+    """Paged decode attention: one query token per sequence.
+
+    Args:
+        page_table: [S, max_blocks] int32/int64; row s lists the physical
+            blocks of sequence s, PAD_ID (-1) past its chain
+            (:func:`src.block_table.build_page_table` / ``export_page_table``).
+        q: [S, Hq, D] query of the token being decoded (un-rotated).
+        k_cache, v_cache: [n_phys, Hkv, 64, D] paged caches (fp32/fp16/bf16);
+            query head h reads KV head h // (Hq / Hkv).
+        seq_lens: [S] keys per sequence (the decoded token's K/V included).
+        cos, sin: [max_positions, D/2] fp32 RoPE tables (half-split pairs).
+        positions: optional [S] query positions (default seq_len - 1).
+        mask: optional block mask broadcastable to [S, max_blocks, max_blocks];
+            the query's row is positions // 64, zero entries drop whole blocks.
+        scope: optional ``(tags [S, L], span [S, 2])`` token scope
+            (:func:`src.scoping_mask.decode_scope`): key j is kept when
+            tags[s, j] or span[s,0] <= j < span[s,1].
+        causal: keep only keys j <= positions[s].
+        softmax_scale: default 1/sqrt(D).
+        validate: check the page table on the device first (one 8-byte read
+            back; raises RuntimeError with the reference's messages).
+        split_blocks / kernel / workspace / status: launch controls; see
+            :class:`DecodeCall`.
+
+    Returns:
+        [S, Hq, D] tensor in the cache dtype.
+    """
+    call = DecodeCall(page_table, q, k_cache, v_cache, seq_lens, cos, sin, positions=positions,
+                      mask=mask, scope=scope, causal=causal, softmax_scale=softmax_scale,
+                      out=out, validate=validate, split_blocks=split_blocks, kernel=kernel,
+                      workspace=workspace, status=status)
+    return call.launch()
