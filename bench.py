@@ -1,0 +1,424 @@
+"""Paged-decode benchmark: tokens/s and achieved HBM GB/s on B200.
+
+Workload (one GPU): GQA paged decode, Llama-3-70B attention shape — 256
+sequences, 64 query heads, 8 KV heads, head_dim 128, bf16, context lengths
+uniform in [8192, 32768], 64-token blocks scattered over a per-GPU pool sized
+to the shard + 5 %, Q/K/V ~ 0.5 N(0, 1), RoPE base 500000. A step decodes
+one token for every sequence (split-K decode + combine).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Under torchrun (N > 1) every rank holds its own 256-sequence shard (weak
+scaling); `value` is the sum over ranks, timed as the max over ranks.
+`--impl reference` times the CPU path (the numpy restatement of the
+reference's dense_reference, one query row per sequence) on this host's
+cores, rank 0 only.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import random
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "ouroboros-triton_b200"))
+sys.path.insert(0, str(ROOT))
+
+WORKLOAD = dict(workload="gqa_paged_decode_llama3_70b", seqs_per_gpu=256, q_heads=64,
+                kv_heads=8, head_dim=128, dtype="bf16", ctx_min=8192, ctx_max=32768,
+                block_tokens=64, rope_base=500000.0, pool_headroom=0.05)
+METRIC = "paged-decode attn tokens/s + achieved HBM GB/s vs peak at 1/2/4/8 B200"
+FALLBACK_HBM_GBS = 6650.0
+
+
+def _peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return FALLBACK_HBM_GBS, "fallback"
+
+
+def _lens(seed: int, n: int):
+    rng = random.Random(seed)
+    return [rng.randint(WORKLOAD["ctx_min"], WORKLOAD["ctx_max"]) for _ in range(n)]
+
+
+def _dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+class ClockSampler:
+    """SM clocks and throttle reasons sampled every 10 ms during the timed region.
+
+    Reads NVML (the library behind nvidia-smi) from a background thread;
+    falls back to an `nvidia-smi -lms` subprocess when NVML is unavailable.
+    """
+
+    REASONS = {"hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40,
+               "sw_power_cap": 0x4}
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.samples, self.reasons, self.max_mhz = [], set(), None
+        self._stop = None
+        self._thread = None
+        self._smi = None
+
+    def __enter__(self):
+        import threading
+        try:
+            import pynvml as nv
+            nv.nvmlInit()
+            h = nv.nvmlDeviceGetHandleByIndex(self.gpu)
+            self.max_mhz = float(nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM))
+            self._stop = threading.Event()
+
+            def loop():
+                while not self._stop.is_set():
+                    try:
+                        self.samples.append(float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)))
+                        bits = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+                        for name, bit in self.REASONS.items():
+                            if bits & bit:
+                                self.reasons.add(name)
+                    except Exception:  # noqa: BLE001 - sampling must never break the bench
+                        pass
+                    self._stop.wait(0.01)
+
+            self._thread = threading.Thread(target=loop, daemon=True)
+            self._thread.start()
+        except Exception:  # noqa: BLE001
+            self._thread = None
+        return self
+
+    def __exit__(self, *exc):
+        if self._thread is not None:
+            self._stop.set()
+            self._thread.join(timeout=2)
+
+    def summary(self):
+        if self._thread is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "samples": 0,
+                    "reasons": ["NVML unavailable"]}
+        return {"sm_mhz": statistics.median(self.samples) if self.samples else None,
+                "sm_max_mhz": self.max_mhz, "samples": len(self.samples),
+                "reasons": sorted(self.reasons)}
+
+
+# ---------------------------------------------------------------------------
+# CPU path (reference arm and cpu_baseline): the oracle's decode restatement
+# ---------------------------------------------------------------------------
+
+def _cpu_decode_sample(n_seqs: int, threads: int, seed: int):
+    """Times the numpy decode restatement on n_seqs sequences of the workload shape.
+
+    Returns (seconds, tokens decoded). Each sequence gets its own scattered
+    paged caches (same shapes and value distribution as the GPU workload).
+    """
+    import numpy as np
+    from concurrent.futures import ThreadPoolExecutor
+
+    from oracle import attention_oracle as ao
+
+    W = WORKLOAD
+    lens = _lens(seed, n_seqs)
+    hkv, hq, d = W["kv_heads"], W["q_heads"], W["head_dim"]
+    max_b = -(-W["ctx_max"] // 64)
+    cos, sin = ao.rope_tables(max_b * 64, d, W["rope_base"])
+    rng = np.random.default_rng(seed)
+    jobs = []
+    for n in lens:
+        nb = -(-n // 64)
+        perm = rng.permutation(nb + 8)[:nb]
+        k = (rng.standard_normal((nb + 8, hkv, 64, d), dtype=np.float32) * 0.5).astype(np.float16)
+        v = (rng.standard_normal((nb + 8, hkv, 64, d), dtype=np.float32) * 0.5).astype(np.float16)
+        pt = np.full((1, max_b), -1, np.int32)
+        pt[0, :nb] = perm
+        q = (rng.standard_normal((1, hq, d), dtype=np.float32) * 0.5).astype(np.float16)
+        jobs.append((pt, q, k, v, [n]))
+
+    def one(job):
+        pt, q, k, v, ln = job
+        return ao.decode_attention(pt, q, k, v, ln, cos, sin)
+
+    t0 = time.perf_counter()
+    with ThreadPoolExecutor(max_workers=threads) as ex:
+        list(ex.map(one, jobs))
+    return time.perf_counter() - t0, n_seqs
+
+
+def run_reference(args):
+    world, rank, _ = _dist_env()
+    if rank != 0:
+        return 0
+    threads = os.cpu_count() or 1
+    per_step = max(1, min(threads, 16))
+    for i in range(args.warmup):
+        _cpu_decode_sample(per_step, threads, 1000 + i)
+    secs, toks = 0.0, 0
+    for i in range(args.steps):
+        s, t = _cpu_decode_sample(per_step, threads, 2000 + i)
+        secs += s
+        toks += t
+    value = toks / secs
+    sample = (f"{per_step} sequences per step of the {WORKLOAD['workload']} shape "
+              f"(lens U[{WORKLOAD['ctx_min']},{WORKLOAD['ctx_max']}]), numpy fp32 row-restricted "
+              "restatement of the reference's dense_reference (its full TxT form is infeasible "
+              "at these lengths)")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1000.0 * secs / max(args.steps, 1), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": dict(WORKLOAD, parallelism=f"replicas{world}", l2_flush="inputs>L2"),
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ---------------------------------------------------------------------------
+# GPU path
+# ---------------------------------------------------------------------------
+
+def _build_shard(torch, device, seed: int, n_seqs: int):
+    import numpy as np
+
+    from oracle import attention_oracle as ao  # RoPE table construction only
+    from src.block_table import BlockTable
+
+    W = WORKLOAD
+    S, hq, hkv, d = n_seqs, W["q_heads"], W["kv_heads"], W["head_dim"]
+    lens = _lens(seed, S)
+    need = sum(-(-n // 64) for n in lens)
+    pool = int(math.ceil(need * (1 + W["pool_headroom"])))
+    bt = BlockTable(pool)
+    ids = [bt.allocate_block() for _ in range(pool)]
+    random.Random(seed).shuffle(ids)
+    for i in ids:
+        bt.free_block(i)
+    heads = [bt.allocate_chain(-(-n // 64)) for n in lens]
+    max_b = -(-W["ctx_max"] // 64)
+    pt_host = bt.export_page_table(heads, max_b)
+    g = torch.Generator(device=device).manual_seed(seed)
+    k = torch.empty((pool, hkv, 64, d), dtype=torch.bfloat16, device=device)
+    v = torch.empty_like(k)
+    chunk = 4096
+    for lo in range(0, pool, chunk):
+        hi = min(pool, lo + chunk)
+        k[lo:hi] = (torch.randn((hi - lo, hkv, 64, d), generator=g, device=device) * 0.5)
+        v[lo:hi] = (torch.randn((hi - lo, hkv, 64, d), generator=g, device=device) * 0.5)
+    q = (torch.randn((S, hq, d), generator=g, device=device) * 0.5).to(torch.bfloat16)
+    cos, sin = ao.rope_tables(max_b * 64, d, W["rope_base"])
+    return dict(lens=lens, pool=pool, table=bt, heads=heads, pt_host=pt_host,
+                pt=torch.from_numpy(pt_host).to(device),
+                seq_lens=torch.tensor(lens, dtype=torch.int32, device=device),
+                k=k, v=v, q=q, cos=torch.from_numpy(cos).to(device),
+                sin=torch.from_numpy(sin).to(device))
+
+
+def _cpu_baseline_leg():
+    threads = os.cpu_count() or 1
+    n = max(1, min(threads, 16))
+    secs, toks = _cpu_decode_sample(n, threads, 77)
+    return {"value": toks / secs, "unit": "tokens/s", "cores": threads, "kind": "port",
+            "sample": f"{n} sequences of the workload shape, numpy fp32 row-restricted "
+                      "restatement of dense_reference, one thread per sequence"}
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    from src.kernels.block_attention import DecodeCall, block_attention_decode
+
+    world, rank, local = _dist_env()
+    if world > 1:
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=120))
+    device = torch.device("cuda", local if world > 1 else 0)
+    torch.cuda.set_device(device)
+
+    W = WORKLOAD
+    S = args.seqs if args.seqs > 0 else W["seqs_per_gpu"]
+    sh = _build_shard(torch, device, seed=1234 + rank, n_seqs=S)
+    call = DecodeCall(sh["pt"], sh["q"], sh["k"], sh["v"], sh["seq_lens"], sh["cos"], sh["sin"],
+                      validate=True, split_blocks=args.split_blocks, kernel=args.kernel)
+    plan = call.plan
+    kv_bytes = sum(sh["lens"]) * W["kv_heads"] * W["head_dim"] * 2 * 2
+    stream = torch.cuda.current_stream(device)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(device)
+
+    for _ in range(max(args.warmup, 3)):
+        call.launch()
+    barrier()
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(device.index if world == 1 else local) as clk:
+        barrier()
+        start.record(stream)
+        for _ in range(args.steps):
+            call.launch()
+        stop.record(stream)
+        barrier()
+    ms = start.elapsed_time(stop)
+    t = torch.tensor([ms], dtype=torch.float64, device=device)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_max = float(t.item())
+    step_ms = ms_max / args.steps
+    value = world * S * args.steps / (ms_max / 1000.0)
+    achieved = kv_bytes / (ms / args.steps / 1000.0) / 1e9  # this rank's kernel, GB/s
+
+    # correctness guard on the measured configuration: a few rows vs the oracle
+    check = _spot_check(torch, sh, call.out) if rank == 0 else None
+
+    # e2e through the public API with host buffers: q, page table and lengths
+    # copied in from pinned memory, the output read back, every step.
+    q_host = sh["q"].cpu().pin_memory()
+    pt_host = torch.from_numpy(sh["pt_host"]).pin_memory()
+    lens_host = torch.tensor(sh["lens"], dtype=torch.int32).pin_memory()
+    out_host = torch.empty((S, W["q_heads"], W["head_dim"]), dtype=torch.bfloat16).pin_memory()
+    q_dev, pt_dev, lens_dev = (torch.empty_like(x, device=device)
+                               for x in (q_host, pt_host, lens_host))
+    out_dev = torch.empty_like(out_host, device=device)
+    gathered = ([torch.empty_like(out_dev) for _ in range(world)]
+                if world > 1 and rank == 0 else None)
+    h2d = sum(x.numel() * x.element_size() for x in (q_host, pt_host, lens_host))
+    d2h = out_host.numel() * out_host.element_size() * (world if rank == 0 else 1)
+
+    def e2e_step():
+        q_dev.copy_(q_host, non_blocking=True)
+        pt_dev.copy_(pt_host, non_blocking=True)
+        lens_dev.copy_(lens_host, non_blocking=True)
+        block_attention_decode(pt_dev, q_dev, sh["k"], sh["v"], lens_dev, sh["cos"], sh["sin"],
+                               out=out_dev, workspace=call.workspace, validate=False,
+                               split_blocks=plan["split_blocks"], kernel=args.kernel)
+        if world > 1:  # the Supervisor (rank 0) gathers every shard's rows over NCCL
+            dist.gather(out_dev, gathered, dst=0)
+            if rank == 0:
+                for gbuf in gathered:
+                    out_host.copy_(gbuf, non_blocking=True)
+        else:
+            out_host.copy_(out_dev, non_blocking=True)
+
+    for _ in range(3):
+        e2e_step()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e2e_steps = max(5, min(args.steps, 20))
+    e0.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    e1.record(stream)
+    barrier()
+    te = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=device)
+    if world > 1:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    e2e_value = world * S * e2e_steps / (float(te.item()) / 1000.0)
+
+    cpu = _cpu_baseline_leg() if (rank == 0 and world == 1 and not args.no_cpu) else None
+    peak, peak_kind = _peaks()
+    launches = args.steps * (1 + (1 if plan["max_splits"] > 1 else 0))
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_ms,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded; random-init K/V/Q, no dataset)",
+            "config": dict(WORKLOAD, seqs_per_gpu=S,
+                           parallelism=f"dp{world} (whole-sequence shards)",
+                           l2_flush="inputs>L2 (K+V %.1f GB per GPU)" % (kv_bytes / 1e9),
+                           split_blocks=plan["split_blocks"], max_splits=plan["max_splits"],
+                           kernel="tensor_cores" if plan["tensor_cores"] else "cuda_cores"),
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "traffic": _traffic_from_profile(),
+                         "peak_source": peak_kind,
+                         "algorithmic_bytes_per_launch": kv_bytes,
+                         "note": "decode + combine per step, K+V bytes once per KV head"},
+            "cpu_baseline": cpu,
+            "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h, "steps": e2e_steps},
+            "gpu_launches": launches,
+            "clocks": clk.summary(),
+            "check": check,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def _spot_check(torch, sh, out):
+    """Max-abs error of 4 sequences' rows vs the fp32 oracle (kept cheap)."""
+    import numpy as np
+
+    from oracle import attention_oracle as ao
+
+    idx = [0, 1, 2, 3]
+    pt = sh["pt_host"][idx]
+    used = sorted({int(x) for x in pt.reshape(-1) if x >= 0})
+    remap = {p: i for i, p in enumerate(used)}
+    pt_small = np.vectorize(lambda x: remap.get(int(x), -1))(pt).astype(np.int32)
+    sel = torch.tensor(used, device=sh["k"].device)
+    k = sh["k"].index_select(0, sel).float().cpu().numpy()
+    v = sh["v"].index_select(0, sel).float().cpu().numpy()
+    q = sh["q"][idx].float().cpu().numpy()
+    want = ao.decode_attention(pt_small, q, k, v, [sh["lens"][i] for i in idx],
+                               sh["cos"].cpu().numpy(), sh["sin"].cpu().numpy())
+    got = out[idx].float().cpu().numpy()
+    err = np.abs(got - want)
+    return {"rows": len(idx), "max_abs": float(err.max()), "mean_abs": float(err.mean())}
+
+
+def _traffic_from_profile():
+    """DRAM bytes per launch recorded from the ncu capture of this workload, if any."""
+    p = ROOT / "profiles" / "decode_config3_traffic.json"
+    if p.exists():
+        try:
+            return json.loads(p.read_text()).get("dram_bytes_per_launch")
+        except (ValueError, OSError):
+            return None
+    return None
+
+
+def main() -> int:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--split-blocks", type=int, default=0)
+    ap.add_argument("--kernel", default="auto", choices=["auto", "tc", "simt"])
+    ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
+    ap.add_argument("--seqs", type=int, default=0,
+                    help="sequences per GPU (default: the workload's 256); smaller values "
+                         "make a profiling case of the same kernel")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -167,6 +167,58 @@ int ouro_validate_page_table(const int32_t* page_table, const int32_t* seq_lens,
                              int32_t num_seqs, int32_t max_blocks, int32_t num_phys_blocks,
                              void* report, void* stream);
 
+/* ------------------------------------------------------------------------
+ * Multi-row paged attention: the reference's block_attention (every query
+ * row of every sequence, src/kernels/block_attention.py:368-527) and
+ * chunked prefill (a dense chunk of query rows over all earlier keys).
+ *
+ * Row i of sequence s sits at absolute position P = q_start[s] + i (0 when
+ * q_start is NULL) and is computed when P < seq_lens[s]; it attends to keys
+ * j in [0, seq_lens[s]) (j <= P when causal), drops whole KV blocks whose
+ * block-mask element (s, i / 64, j / 64) is 0, adds bias(s, h, i, j) to the
+ * scaled score, and applies half-split RoPE at P to q and at j to k_j.
+ * Rows that are not computed are left untouched in `out`.
+ * ---------------------------------------------------------------------- */
+typedef struct ouro_attention_args {
+  const void* q;              /* q_paged: [n_phys, Hq, 64, D] read through the page
+                                 table at position P; else dense [S, Hq, q_len, D] */
+  int32_t q_paged;
+  const void* k_cache;        /* [n_phys, Hkv, 64, D] */
+  const void* v_cache;
+  const int32_t* page_table;  /* [S, max_blocks] */
+  const int32_t* seq_lens;    /* [S] */
+  const int32_t* q_start;     /* [S] or NULL */
+  const float* cos;           /* [max_positions, D/2] */
+  const float* sin;
+  const float* bias;          /* optional fp32, element (s, h, i, j) at the strides below */
+  int64_t bias_stride_s, bias_stride_h, bias_stride_q, bias_stride_k;
+  const int8_t* block_mask;   /* optional, element (s, qb, kb) at the strides below */
+  int64_t mask_stride_s, mask_stride_q, mask_stride_k;
+  void* out;                  /* [S, Hq, q_len, D], dtype */
+  int32_t* status;            /* optional device int32 (bit 1: bad page entry) */
+  int32_t num_seqs, num_q_heads, num_kv_heads, head_dim, q_len;
+  int32_t max_blocks, num_phys_blocks, max_positions;
+  int32_t dtype, causal, kernel; /* kernel: 0 auto, 1 CUDA cores, 2 tensor cores */
+  float softmax_scale;        /* <= 0: 1/sqrt(D) */
+} ouro_attention_args;
+
+int ouro_paged_attention(const ouro_attention_args* args, void* stream);
+
+/* ------------------------------------------------------------------------
+ * Paged K/V write ([EXPAND] data step, no reference counterpart: the
+ * reference grows chains, src/block_table.py:152-165, but stores no K/V).
+ * Token t < counts[s] of sequence s, from k_new/v_new [S, Hkv, new_len, D],
+ * lands at position start[s] + t of its chain: block
+ * page_table[s][(start[s]+t)/64], slot (start[s]+t) % 64. head_dim *
+ * elem_bytes must be a multiple of 16 and all buffers 16-byte aligned.
+ * Entries outside [0, n_phys) are skipped and set bit 1 of *status.
+ * ---------------------------------------------------------------------- */
+int ouro_kv_append(const void* k_new, const void* v_new, const int32_t* page_table,
+                   const int32_t* start, const int32_t* counts, void* k_cache, void* v_cache,
+                   int32_t num_seqs, int32_t num_kv_heads, int32_t new_len, int32_t head_dim,
+                   int32_t elem_bytes, int32_t max_blocks, int32_t num_phys_blocks,
+                   int32_t* status, void* stream);
+
 #ifdef __cplusplus
 }  /* extern "C" */
 #endif

@@ -9,6 +9,7 @@
 #include <string>
 
 #include "attention.hpp"
+#include "rows.hpp"
 #include "block_table.hpp"
 #include "capi_common.hpp"
 
@@ -128,7 +129,7 @@ void plan(ouro::DecodeParams& p, const ouro_decode_args* a, bool* use_tc, size_t
   }
   int split = a->split_blocks > 0 ? a->split_blocks : choose_split(p, tc, 16);
   split = std::min(split, std::max(p.max_blocks, 1));
-  if (tc) split = std::min(split, 1024);
+  if (tc) split = std::min(split, 512);  // block list lives in shared memory
   p.split_blocks = split;
   p.max_splits = std::max(1, (p.max_blocks + split - 1) / split);
   *use_tc = tc;
@@ -137,9 +138,71 @@ void plan(ouro::DecodeParams& p, const ouro_decode_args* a, bool* use_tc, size_t
                   : 0;
 }
 
+ouro::RowsParams to_rows(const ouro_attention_args* a) {
+  if (a == nullptr) fail(OURO_EINVAL, "null attention args");
+  ouro::RowsParams p{};
+  p.q = a->q;
+  p.q_paged = a->q_paged ? 1 : 0;
+  p.k = a->k_cache;
+  p.v = a->v_cache;
+  p.page_table = a->page_table;
+  p.seq_lens = a->seq_lens;
+  p.q_start = a->q_start;
+  p.cos = a->cos;
+  p.sin = a->sin;
+  p.bias = a->bias;
+  p.bias_s = a->bias_stride_s;
+  p.bias_h = a->bias_stride_h;
+  p.bias_q = a->bias_stride_q;
+  p.bias_k = a->bias_stride_k;
+  p.mask = a->block_mask;
+  p.mask_s = a->mask_stride_s;
+  p.mask_q = a->mask_stride_q;
+  p.mask_k = a->mask_stride_k;
+  p.out = a->out;
+  p.status = a->status;
+  p.S = a->num_seqs;
+  p.Hq = a->num_q_heads;
+  p.Hkv = a->num_kv_heads;
+  p.D = a->head_dim;
+  p.Lq = a->q_len;
+  p.max_blocks = a->max_blocks;
+  p.n_phys = a->num_phys_blocks;
+  p.max_pos = a->max_positions;
+  p.causal = a->causal ? 1 : 0;
+  const float scale = a->softmax_scale > 0.f ? a->softmax_scale
+                                             : 1.0f / std::sqrt(static_cast<float>(a->head_dim));
+  p.scale_log2 = scale * ouro::kLog2e;
+  if (dtype_bytes(a->dtype) == 0) fail(OURO_EUNSUPPORTED, "unsupported dtype code");
+  if (p.S < 0 || p.Lq < 0) fail(OURO_EINVAL, "num_seqs and q_len must be >= 0");
+  if (p.Hq <= 0 || p.Hkv <= 0 || p.Hq % p.Hkv != 0)
+    fail(OURO_EINVAL, "num_q_heads must be a positive multiple of num_kv_heads");
+  if (p.q_paged && p.Hq != p.Hkv)
+    fail(OURO_EINVAL, "paged queries need as many query heads as KV heads");
+  p.G = p.Hq / p.Hkv;
+  if (p.D < 2 || p.D % 2 != 0 || p.D > 256)
+    fail(OURO_EUNSUPPORTED, "head dim must be even and in [2, 256], got " + std::to_string(p.D));
+  if (p.max_blocks < 0 || p.n_phys <= 0 || p.max_pos <= 0)
+    fail(OURO_EINVAL, "max_blocks, num_phys_blocks and max_positions must be positive");
+  if (p.S > 0 && p.Lq > 0 &&
+      (!p.q || !p.k || !p.v || !p.page_table || !p.seq_lens || !p.cos || !p.sin || !p.out))
+    fail(OURO_EINVAL, "null tensor pointer in attention args");
+  return p;
+}
+
 }  // namespace
 
 extern "C" {
+
+int ouro_paged_attention(const ouro_attention_args* args, void* stream) {
+  OURO_CAPI_GUARD({
+    ouro::RowsParams p = to_rows(args);
+    if (args->kernel != 0 && args->kernel != 1)
+      fail(OURO_EUNSUPPORTED, "only the CUDA-core multi-row kernel is built for these arguments");
+    auto st = static_cast<cudaStream_t>(stream);
+    check_cuda(ouro::launch_attend_rows_simt(p, args->dtype, st), "paged attention (cuda cores)");
+  })
+}
 
 int ouro_decode_plan(const ouro_decode_args* args, int32_t* split_blocks, int32_t* max_splits,
                      size_t* workspace_bytes, int32_t* uses_tensor_cores) {

@@ -29,10 +29,10 @@ class CapiError : public std::exception {
 }  // namespace ouro
 
 // Runs `body` (a statement block) and maps exceptions to OURO_E* codes.
-#define OURO_CAPI_GUARD(body)                                  \
+#define OURO_CAPI_GUARD(...)                                   \
   try {                                                        \
     ::ouro::clear_error();                                     \
-    body;                                                      \
+    __VA_ARGS__;                                               \
     return OURO_OK;                                            \
   } catch (const ::ouro::CapiError& e) {                       \
     ::ouro::set_error(e.what());                               \

@@ -1,0 +1,35 @@
+// Parameters of the multi-row attention kernels: the reference's full
+// self-attention (every row, paged queries) and chunked prefill (a dense
+// chunk of query rows, causal).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cstdint>
+
+namespace ouro {
+
+struct RowsParams {
+  const void* q;              // q_paged: [n_phys, Hq, 64, D]; else [S, Hq, Lq, D]
+  int32_t q_paged;
+  const void* k;              // [n_phys, Hkv, 64, D]
+  const void* v;
+  const int32_t* page_table;  // [S, max_blocks]
+  const int32_t* seq_lens;    // [S] keys per sequence
+  const int32_t* q_start;     // [S] absolute position of query row 0, or null (0)
+  const float* cos;           // [max_pos, D/2]
+  const float* sin;
+  const float* bias;          // optional fp32, element (s,h,i,j) at the four strides
+  int64_t bias_s, bias_h, bias_q, bias_k;
+  const int8_t* mask;         // optional block mask, element (s, qb, kb)
+  int64_t mask_s, mask_q, mask_k;
+  void* out;                  // [S, Hq, Lq, D]; rows past the sequence are not written
+  int32_t* status;
+  int32_t S, Hq, Hkv, G, D, Lq;
+  int32_t max_blocks, n_phys, max_pos;
+  int32_t causal;
+  float scale_log2;
+};
+
+cudaError_t launch_attend_rows_simt(const RowsParams& p, int dtype, cudaStream_t stream);
+
+}  // namespace ouro

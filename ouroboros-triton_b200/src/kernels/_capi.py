@@ -35,3 +35,28 @@ _native.register("ouro_decode_plan", ctypes.c_int,
 _native.register("ouro_paged_decode", ctypes.c_int, [ctypes.POINTER(DecodeArgs), _vp])
 _native.register("ouro_validate_page_table", ctypes.c_int,
                  [_vp, _vp, _i32, _i32, _i32, _vp, _vp])
+
+
+class AttentionArgs(ctypes.Structure):
+    """``ouro_attention_args`` (field order and types must match the header)."""
+
+    _fields_ = [
+        ("q", _vp), ("q_paged", _i32), ("k_cache", _vp), ("v_cache", _vp),
+        ("page_table", _vp), ("seq_lens", _vp), ("q_start", _vp),
+        ("cos", _vp), ("sin", _vp),
+        ("bias", _vp), ("bias_stride_s", _i64), ("bias_stride_h", _i64),
+        ("bias_stride_q", _i64), ("bias_stride_k", _i64),
+        ("block_mask", _vp), ("mask_stride_s", _i64), ("mask_stride_q", _i64),
+        ("mask_stride_k", _i64),
+        ("out", _vp), ("status", _vp),
+        ("num_seqs", _i32), ("num_q_heads", _i32), ("num_kv_heads", _i32), ("head_dim", _i32),
+        ("q_len", _i32), ("max_blocks", _i32), ("num_phys_blocks", _i32),
+        ("max_positions", _i32), ("dtype", _i32), ("causal", _i32), ("kernel", _i32),
+        ("softmax_scale", ctypes.c_float),
+    ]
+
+
+_native.register("ouro_paged_attention", ctypes.c_int, [ctypes.POINTER(AttentionArgs), _vp])
+_native.register("ouro_kv_append", ctypes.c_int,
+                 [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _i32, _i32,
+                  _vp, _vp])

@@ -2,6 +2,11 @@
 ``src/kernels/block_attention.py``.
 
 Entry points
+  * :func:`block_attention` — the reference's entry point, same signature and
+    result: full self-attention over every row of every sequence, paged
+    q/k/v, RoPE, additive bias, block mask (block_attention.py:368-527).
+  * :func:`chunked_prefill_attention` — a dense chunk of query rows per
+    sequence over all its earlier keys, causal, GQA.
   * :func:`block_attention_decode` — one query token per sequence (the decode
     step) over its paged K/V: GQA, explicit positions, split-K, fused RoPE,
     block mask and token-granular Table-1 scope. sm_100a kernels in
@@ -39,7 +44,10 @@ HAS_TRITON = False
 __all__ = [
     "HAS_TRITON",
     "HAS_TORCH",
+    "block_attention",
     "block_attention_decode",
+    "chunked_prefill_attention",
+    "paged_kv_append",
     "decode_plan",
     "validate_bias_shape",
     "validate_mask_shape",
@@ -380,3 +388,186 @@ def block_attention_decode(page_table, q, k_cache, v_cache, seq_lens, cos, sin, 
                       out=out, validate=validate, split_blocks=split_blocks, kernel=kernel,
                       workspace=workspace, status=status)
     return call.launch()
+
+
+# ---------------------------------------------------------------------------
+# Multi-row attention: the reference's block_attention and chunked prefill
+# ---------------------------------------------------------------------------
+
+
+def _rows_args(q, q_paged, k_cache, v_cache, page_table, seq_lens, q_start, cos, sin, bias,
+               mask, out, status, Hq, Lq, causal, softmax_scale, kernel):
+    n_phys, Hkv, _, D = k_cache.shape
+    a = _capi.AttentionArgs()
+    a.q, a.q_paged = _ptr(q), 1 if q_paged else 0
+    a.k_cache, a.v_cache = _ptr(k_cache), _ptr(v_cache)
+    a.page_table, a.seq_lens, a.q_start = _ptr(page_table), _ptr(seq_lens), _ptr(q_start)
+    a.cos, a.sin = _ptr(cos), _ptr(sin)
+    if bias is not None:
+        a.bias = _ptr(bias[0])
+        a.bias_stride_s, a.bias_stride_h, a.bias_stride_q, a.bias_stride_k = bias[1]
+    if mask is not None:
+        a.block_mask = _ptr(mask[0])
+        a.mask_stride_s, a.mask_stride_q, a.mask_stride_k = mask[1]
+    a.out, a.status = _ptr(out), _ptr(status)
+    a.num_seqs, a.num_q_heads, a.num_kv_heads, a.head_dim = page_table.shape[0], Hq, Hkv, D
+    a.q_len = Lq
+    a.max_blocks, a.num_phys_blocks, a.max_positions = page_table.shape[1], n_phys, cos.shape[0]
+    a.dtype = _dtype_code(k_cache.dtype)
+    a.causal = 1 if causal else 0
+    a.kernel = _KERNELS[kernel]
+    a.softmax_scale = float(softmax_scale) if softmax_scale is not None else 0.0
+    return a
+
+
+def _launch_rows(args, device):
+    _native.check(_native.lib().ouro_paged_attention(ctypes.byref(args), _stream_handle(device)),
+                  "paged attention")
+
+
+def _as_int32(t, name: str):
+    if t.dtype not in (torch.int32, torch.int64):
+        raise RuntimeError(f"{name} must be int32/int64, got {t.dtype}")
+    return t.to(torch.int32).contiguous()
+
+
+def block_attention(page_table, q_cache, k_cache, v_cache, seq_lens, cos, sin, bias=None,
+                    mask=None, softmax_scale: float | None = None):
+    """Full paged self-attention: the reference's ``block_attention``, on B200.
+
+    Same arguments, checks, error texts and result as the reference
+    (src/kernels/block_attention.py:368-527):
+
+    * ``page_table`` [S, max_blocks]: physical block of logical block n of
+      sequence s, PAD_ID past the chain;
+    * ``q_cache, k_cache, v_cache`` [n_phys, H, 64, D] (fp32/fp16/bf16);
+    * ``seq_lens`` [S]: self-attention, query extent = key extent;
+    * ``cos, sin`` [max_positions, D/2] fp32, half-split RoPE at absolute
+      positions;
+    * ``bias`` broadcastable to [S, H, Q, K], added to the scaled scores;
+    * ``mask`` block mask broadcastable to [S, QB, KB], zero = KV block dropped;
+    * ``softmax_scale`` defaults to 1/sqrt(D).
+
+    Returns [S, H, max_len, D] in the cache dtype; rows past seq_lens[s] are 0.
+    """
+    _require_cuda()
+    named = (page_table, q_cache, k_cache, v_cache, seq_lens, cos, sin)
+    device = _device_of(*named, bias, mask)
+    page_table, q_cache, k_cache, v_cache, seq_lens = (
+        _on(t, device) for t in (page_table, q_cache, k_cache, v_cache, seq_lens))
+    cos, sin = _on(cos, device, torch.float32), _on(sin, device, torch.float32)
+    S, max_b = page_table.shape
+    n_phys, H, blk, D = q_cache.shape
+    if blk != BLOCK_SIZE:
+        raise RuntimeError(f"q_cache block dim must be {BLOCK_SIZE}, got {blk}")
+    if k_cache.shape != q_cache.shape or v_cache.shape != q_cache.shape:
+        raise RuntimeError("q/k/v caches must share the [n_phys, H, 64, D] layout")
+    if D < 32 or D % 2 != 0:
+        raise RuntimeError(f"head dim must be even and >= 32 for half-dot RoPE, got {D}")
+    if tuple(seq_lens.shape) != (S,):
+        raise RuntimeError(f"seq_lens must have shape [{S}], got {tuple(seq_lens.shape)}")
+    pt = _as_int32(page_table, "page_table")
+    lens = _as_int32(seq_lens, "seq_lens")
+    validate_page_table(pt, lens, n_phys)
+    max_len = int(lens.max().item()) if S else 0
+    if max_len == 0:
+        raise RuntimeError("all sequences are empty")
+    if cos.shape[0] < max_b * BLOCK_SIZE or sin.shape[0] < max_b * BLOCK_SIZE:
+        raise RuntimeError(
+            f"rope tables must cover {max_b * BLOCK_SIZE} positions, got {cos.shape[0]}")
+    qb_max = -(-max_len // BLOCK_SIZE)
+    bias_arg = mask_arg = None
+    if bias is not None:
+        bias = _on(bias, device)
+        validate_bias_shape(tuple(bias.shape), num_seqs=S, num_heads=H, q_len=max_len,
+                            kv_len=max_len)
+        bias = bias.to(torch.float32).contiguous()
+        bias_arg = (bias, _broadcast_strides(tuple(bias.shape), (S, H, max_len, max_len)))
+    if mask is not None:
+        mask = _on(mask, device)
+        validate_mask_shape(tuple(mask.shape), num_seqs=S, num_q_blocks=qb_max,
+                            num_kv_blocks=qb_max)
+        mask = mask.to(torch.int8).contiguous()
+        mask_arg = (mask, _broadcast_strides(tuple(mask.shape), (S, qb_max, qb_max)))
+    q_c = q_cache.to(k_cache.dtype).contiguous()
+    out = torch.zeros((S, H, max_len, D), dtype=k_cache.dtype, device=device)
+    args = _rows_args(q_c, True, k_cache, v_cache, pt, lens, None, cos, sin, bias_arg, mask_arg,
+                      out, None, H, max_len, False, softmax_scale, "auto")
+    _launch_rows(args, device)
+    return out
+
+
+def chunked_prefill_attention(page_table, q, k_cache, v_cache, q_start, seq_lens, cos, sin, *,
+                              causal: bool = True, softmax_scale=None, out=None,
+                              validate: bool = True, kernel: str = "auto", status=None):
+    """Chunked prefill: q [S, Hq, L, D] rows at positions q_start[s] + i.
+
+    Keys are every paged token j < seq_lens[s] (the chunk's own K/V already
+    written into the cache), j <= q_start[s] + i when ``causal``. Query head h
+    reads KV head h // (Hq / Hkv). Rows whose position is >= seq_lens[s] stay
+    zero. Returns [S, Hq, L, D] in the cache dtype.
+    """
+    _require_cuda()
+    if kernel not in _KERNELS:
+        raise RuntimeError(f"kernel must be one of {sorted(_KERNELS)}, got {kernel!r}")
+    device = _device_of(k_cache, q, page_table)
+    k_cache, v_cache = _on(k_cache, device), _on(v_cache, device)
+    n_phys, Hkv, blk, D = k_cache.shape
+    if blk != BLOCK_SIZE:
+        raise RuntimeError(f"k_cache block dim must be {BLOCK_SIZE}, got {blk}")
+    if v_cache.shape != k_cache.shape or v_cache.dtype != k_cache.dtype:
+        raise RuntimeError("k/v caches must share the [n_phys, Hkv, 64, D] layout and dtype")
+    q = _on(q, device, k_cache.dtype)
+    if q.dim() != 4 or q.shape[3] != D:
+        raise RuntimeError(f"q must be [S, Hq, L, {D}], got {tuple(q.shape)}")
+    S, Hq, L = q.shape[0], q.shape[1], q.shape[2]
+    if Hq % Hkv != 0:
+        raise RuntimeError(f"query heads {Hq} must be a multiple of KV heads {Hkv}")
+    pt = _as_int32(_on(page_table, device), "page_table")
+    if pt.dim() != 2 or pt.shape[0] != S:
+        raise RuntimeError(f"page_table must be [S={S}, max_blocks]")
+    lens = _as_int32(_on(seq_lens, device), "seq_lens")
+    starts = _as_int32(_on(q_start, device), "q_start")
+    if tuple(lens.shape) != (S,) or tuple(starts.shape) != (S,):
+        raise RuntimeError(f"seq_lens and q_start must have shape [{S}]")
+    cos, sin = _on(cos, device, torch.float32), _on(sin, device, torch.float32)
+    if cos.dim() != 2 or cos.shape != sin.shape or cos.shape[1] != D // 2:
+        raise RuntimeError(f"rope tables must be [max_positions, {D // 2}]")
+    if cos.shape[0] < pt.shape[1] * BLOCK_SIZE:
+        raise RuntimeError(
+            f"rope tables must cover {pt.shape[1] * BLOCK_SIZE} positions, got {cos.shape[0]}")
+    if validate:
+        validate_page_table(pt, lens, n_phys)
+    if out is None:
+        out = torch.zeros((S, Hq, L, D), dtype=k_cache.dtype, device=device)
+    elif out.shape != (S, Hq, L, D) or out.dtype != k_cache.dtype or not out.is_contiguous():
+        raise RuntimeError(f"out must be a contiguous [S, Hq, L, D] {k_cache.dtype} tensor")
+    args = _rows_args(q, False, k_cache, v_cache, pt, lens, starts, cos, sin, None, None, out,
+                      status, Hq, L, causal, softmax_scale, kernel)
+    _launch_rows(args, device)
+    return out
+
+
+def paged_kv_append(k_new, v_new, page_table, start, counts, k_cache, v_cache, *, status=None):
+    """Writes new tokens into the paged caches (the [EXPAND] data step).
+
+    ``k_new``/``v_new`` [S, Hkv, L, D]; token t < counts[s] of sequence s goes to
+    position start[s] + t of its chain (block page_table[s][pos // 64], slot
+    pos % 64). The chains must already cover those positions.
+    """
+    _require_cuda()
+    device = _device_of(k_cache)
+    if k_new.shape != v_new.shape or k_new.dim() != 4:
+        raise RuntimeError("k_new / v_new must both be [S, Hkv, L, D]")
+    S, Hkv, L, D = k_new.shape
+    if k_cache.shape[1] != Hkv or k_cache.shape[3] != D or k_cache.shape[2] != BLOCK_SIZE:
+        raise RuntimeError("new K/V heads and head_dim must match the cache")
+    k_new = _on(k_new, device, k_cache.dtype)
+    v_new = _on(v_new, device, k_cache.dtype)
+    pt = _as_int32(_on(page_table, device), "page_table")
+    st = _as_int32(_on(start, device), "start")
+    ct = _as_int32(_on(counts, device), "counts")
+    _native.check(_native.lib().ouro_kv_append(
+        _ptr(k_new), _ptr(v_new), _ptr(pt), _ptr(st), _ptr(ct), _ptr(k_cache), _ptr(v_cache),
+        S, Hkv, L, D, k_cache.element_size(), pt.shape[1], k_cache.shape[0], _ptr(status),
+        _stream_handle(device)), "kv append")
