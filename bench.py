@@ -258,8 +258,10 @@ def run_ours(args):
     W = WORKLOAD
     S = args.seqs if args.seqs > 0 else W["seqs_per_gpu"]
     sh = _build_shard(torch, device, seed=1234 + rank, n_seqs=S)
+    status = torch.zeros(1, dtype=torch.int32, device=device)
     call = DecodeCall(sh["pt"], sh["q"], sh["k"], sh["v"], sh["seq_lens"], sh["cos"], sh["sin"],
-                      validate=True, split_blocks=args.split_blocks, kernel=args.kernel)
+                      validate=True, split_blocks=args.split_blocks, kernel=args.kernel,
+                      status=status)
     plan = call.plan
     kv_bytes = sum(sh["lens"]) * W["kv_heads"] * W["head_dim"] * 2 * 2
     stream = torch.cuda.current_stream(device)
@@ -291,6 +293,11 @@ def run_ours(args):
 
     # correctness guard on the measured configuration: a few rows vs the oracle
     check = _spot_check(torch, sh, call.out) if rank == 0 else None
+    kernel_status = int(status.item())  # nonzero: a bounded wait gave up or a bad entry
+    if check is not None:
+        check["kernel_status"] = kernel_status
+    if kernel_status != 0:
+        print(f"rank {rank}: decode kernels reported status {kernel_status}", file=sys.stderr)
 
     # e2e through the public API with host buffers: q, page table and lengths
     # copied in from pinned memory, the output read back, every step.

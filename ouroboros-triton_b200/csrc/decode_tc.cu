@@ -1,24 +1,30 @@
 // Paged GQA decode on tensor cores for fp16 / bf16 caches, head_dim 64 or 128,
 // query-group size <= 8.
 //
-// Work: one CTA per (split-K chunk, group of HPC KV heads, sequence).
-//   * Warp HPC (producer) builds the chunk's block list from the page table
-//     and the block mask (masked blocks are skipped, never loaded), then
-//     streams 16-token stages through a STAGES-deep ring: for every KV head
-//     the K and V rows of the 16 tokens (each a contiguous 4 KB run of the
-//     [n_phys, Hkv, 64, D] cache) plus the cos/sin rows of their positions,
-//     all as TMA tiles with 128-byte swizzle, completion on an mbarrier.
-//     K/V use an evict-first L2 policy (streamed once); the RoPE tables use
-//     evict-last (shared by every sequence and KV head).
-//   * Warp w < HPC (consumer) owns KV head kvh0 + w and its G query heads:
+// Work: one CTA per (split-K chunk, group of HPC KV heads, sequence), 2 warps
+// per KV head.
+//   * Warp 0 builds the chunk's block list from the page table and the block
+//     mask (masked blocks are skipped, never loaded) and primes a STAGES-deep
+//     ring of 16-token stages: for every KV head the K and V rows of the 16
+//     tokens (each a contiguous 4 KB run of the [n_phys, Hkv, 64, D] cache)
+//     plus the cos/sin rows of their positions, all TMA tiles with 128-byte
+//     swizzle, completion on an mbarrier. K/V use an evict-first L2 policy
+//     (streamed once); the RoPE tables evict-last (shared by every sequence).
+//   * Stage i is consumed by the warps (head, i % 2): each owns KV head
+//     kvh0 + head and its G query heads, and keeps its own online-softmax
+//     state; the last of the HPC warps releasing a stage issues the TMA
+//     refill for stage i + STAGES (no dedicated producer warp, so all 16
+//     warps compute and each gets 128 registers).
+//   * Per stage and warp:
 //       S^T[16 tok x 8 heads] = K[16 x D] . Q^T          (mma m16n8k16)
 //     with RoPE applied to the K fragments in registers (the half-split
 //     partner of column d, d + D/2, sits in the same lane's fragment of the
-//     chunk D/32 further on), masking (ragged tail, token scope), online
-//     softmax in base 2 with quad-shuffle max, P^T moved into the B-operand
-//     layout by movmatrix, and
+//     chunk D/32 further on; the rotation runs on the packed f32x2 pipe),
+//     masking (ragged tail, token scope), online softmax in base 2 with
+//     quad-shuffle max, P^T moved into the B-operand layout by movmatrix, and
 //       O^T[D x 8 heads] += V^T[D x 16 tok] . P^T        (mma m16n8k16)
 //     with V^T fragments from ldmatrix.trans.
+//   * The two warps of a head merge their states through shared memory.
 // The GQA group is the MMA's N dimension, so no query rows are padded.
 // Output: the final row when the sequence has one chunk, else an unnormalised
 // partial plus (max, sum) for the combine kernel.
@@ -38,6 +44,7 @@ namespace ouro {
 namespace {
 
 constexpr int kTok = 16;  // tokens per stage
+constexpr int kWph = 2;   // consumer warps per KV head; they take alternate stages
 
 template <int D, int HPC>
 struct TcLayout {
@@ -59,8 +66,54 @@ __device__ __forceinline__ bool scope_ok(const DecodeParams& p, const uint8_t* t
   return tags_stage[row] != 0 || (j >= lo && j < hi);
 }
 
+// Waits (bounded, like mbar_wait) until use `use` of a stage has been issued.
+__device__ __forceinline__ bool wait_use(volatile int32_t* slot, int use,
+                                         uint64_t limit_ns = 2000000000ull) {
+  if (*slot == use) return true;
+  const uint64_t t0 = global_timer_ns();
+  for (uint32_t i = 1;; ++i) {
+    if (*slot == use) return true;
+    if ((i & 63u) == 0 && global_timer_ns() - t0 > limit_ns) return false;
+  }
+}
+
+// Issues the TMA copies of iteration `it` (block list entry it / 4, 16-token
+// sub-tile it % 4) into stage `st`; called by one thread. The stage's use
+// number (it / STAGES) is published first: two warp groups take alternate
+// iterations, so a warp can ask for use n of a stage whose use n - 1 has not
+// landed yet, when the mbarrier's parity alone cannot tell use n from n - 2.
+template <int D, int HPC>
+__device__ __forceinline__ void issue_stage(const CUtensorMap* tm_k, const CUtensorMap* tm_v,
+                                            const CUtensorMap* tm_cos, const CUtensorMap* tm_sin,
+                                            const DecodeParams& p, uint8_t* stg, uint64_t* full,
+                                            uint8_t* tag_dst, volatile int32_t* use_slot,
+                                            int use, int s, int kvh0, int b, int phys, int u,
+                                            uint64_t pol_stream, uint64_t pol_keep) {
+  using L = TcLayout<D, HPC>;
+  *use_slot = use;  // consumers of this use wait for this word before the parity wait
+  mbar_arrive_expect_tx(full, L::kStage + (p.scope_tags ? 16u : 0u));
+  const int pos_row = b * kBlock + u * kTok;
+#pragma unroll
+  for (int h = 0; h < HPC; ++h) {
+    const int y = (phys * p.Hkv + kvh0 + h) * kBlock + u * kTok;
+#pragma unroll
+    for (int bx = 0; bx < L::kKBoxes; ++bx) {
+      tma_load_2d(stg + L::kK + h * L::kHeadTile + bx * (kTok * 128), tm_k, bx * 64, y, full,
+                  pol_stream);
+      tma_load_2d(stg + L::kV + h * L::kHeadTile + bx * (kTok * 128), tm_v, bx * 64, y, full,
+                  pol_stream);
+    }
+  }
+#pragma unroll
+  for (int bx = 0; bx < L::kTBoxes; ++bx) {
+    tma_load_2d(stg + L::kCos + bx * (kTok * 128), tm_cos, bx * 32, pos_row, full, pol_keep);
+    tma_load_2d(stg + L::kSin + bx * (kTok * 128), tm_sin, bx * 32, pos_row, full, pol_keep);
+  }
+  if (p.scope_tags) bulk_load(tag_dst, p.scope_tags + s * p.scope_stride + pos_row, 16, full);
+}
+
 template <typename T, int D, int HPC>
-__global__ void __launch_bounds__((HPC + 1) * 32, 1)
+__global__ void __launch_bounds__(HPC * kWph * 32, 1)
     decode_tc_kernel(const __grid_constant__ CUtensorMap tm_k,
                      const __grid_constant__ CUtensorMap tm_v,
                      const __grid_constant__ CUtensorMap tm_cos,
@@ -70,19 +123,24 @@ __global__ void __launch_bounds__((HPC + 1) * 32, 1)
   constexpr int S_ = L::kStages;
   constexpr int KC = D / 16;     // 16-column chunks of head_dim
   constexpr int HALF_KC = KC / 2;
+  constexpr int kConsumers = HPC * kWph;
 
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   uint8_t* stages = smem;
   uint64_t* full = reinterpret_cast<uint64_t*>(stages + S_ * L::kStage);
-  uint64_t* empty = full + S_;
-  uint8_t* tags = reinterpret_cast<uint8_t*>(empty + S_);      // [S_][16]
+  uint32_t* released = reinterpret_cast<uint32_t*>(full + S_);  // [S_] release counts
+  uint8_t* tags = reinterpret_cast<uint8_t*>(                        // [S_][16], 16-B aligned
+      (reinterpret_cast<uintptr_t>(released + S_) + 15) & ~static_cast<uintptr_t>(15));
   int32_t* list_b = reinterpret_cast<int32_t*>(tags + S_ * 16);
   int32_t* list_p = list_b + p.split_blocks;
   __shared__ int32_t s_nitems;
   __shared__ int32_t s_abort_flag;
+  __shared__ int32_t s_issued;
+  __shared__ int32_t s_use[8];  // use number of the copy last issued into each stage
   volatile int32_t* s_abort = &s_abort_flag;
+  static_assert(L::kStages <= 8, "s_use holds at most 8 stages");
 
   const int split = blockIdx.x;
   const int s = blockIdx.z;
@@ -101,8 +159,10 @@ __global__ void __launch_bounds__((HPC + 1) * 32, 1)
   const int b_begin = split * p.split_blocks;
   const int b_end = min(g.nb, b_begin + p.split_blocks);
   const int qb = g.pos >= 0 ? g.pos / kBlock : 0;
+  // Only the sequence's last block can be partial: it has ceil(rest / 16) sub-tiles.
+  const int last_sub = min(4, (g.kv_len - (g.nb - 1) * kBlock + kTok - 1) / kTok);
 
-  if (warp == HPC) {
+  if (warp == 0) {
     // Block list: allowed blocks of this chunk with their physical ids.
     int n = 0;
     for (int base = b_begin; base < b_end; base += 32) {
@@ -126,81 +186,36 @@ __global__ void __launch_bounds__((HPC + 1) * 32, 1)
       }
       n += __popc(bal);
     }
+    __syncwarp();
     if (lane == 0) {
       s_nitems = n;
       *s_abort = 0;
       for (int i = 0; i < S_; ++i) {
         mbar_init(&full[i], 1);
-        mbar_init(&empty[i], HPC);
+        released[i] = 0;
+        s_use[i] = -1;
       }
       fence_barrier_init();
+      // Prime the ring.
+      const int total = n == 0 ? 0 : (n - 1) * 4 + (list_b[n - 1] == g.nb - 1 ? last_sub : 4);
+      const uint64_t pol_stream = policy_evict_first(), pol_keep = policy_evict_last();
+      int it = 0;
+      for (; it < S_ && it < total; ++it)
+        issue_stage<D, HPC>(&tm_k, &tm_v, &tm_cos, &tm_sin, p, stages + it * L::kStage,
+                            &full[it], tags + it * 16, &s_use[it], 0, s, kvh0, list_b[it >> 2],
+                            list_p[it >> 2], it & 3, pol_stream, pol_keep);
+      s_issued = it;
     }
   }
   __syncthreads();
   const int nitems = s_nitems;
+  const int total_iters =
+      nitems == 0 ? 0 : (nitems - 1) * 4 + (list_b[nitems - 1] == g.nb - 1 ? last_sub : 4);
 
-  if (warp == HPC) {
-    // ---------------- producer ----------------
-    if (lane == 0) {
-      tma_prefetch_desc(&tm_k);
-      tma_prefetch_desc(&tm_v);
-      tma_prefetch_desc(&tm_cos);
-      tma_prefetch_desc(&tm_sin);
-      const uint64_t pol_stream = policy_evict_first();
-      const uint64_t pol_keep = policy_evict_last();
-      const uint32_t bytes = L::kStage + (p.scope_tags ? 16u : 0u);
-      int it = 0;
-      for (int k = 0; k < nitems && !*s_abort; ++k) {
-        const int b = list_b[k];
-        const int phys = list_p[k];
-        const int nsub = min(4, (g.kv_len - b * kBlock + kTok - 1) / kTok);
-        for (int u = 0; u < nsub; ++u, ++it) {
-          const int st = it % S_;
-          if (it >= S_ && !mbar_wait(&empty[st], ((it / S_) - 1) & 1)) {
-            if (p.status) atomicOr(p.status, kStatusWaitTimeout);
-            *s_abort = 1;
-            break;
-          }
-          uint8_t* stg = stages + st * L::kStage;
-          mbar_arrive_expect_tx(&full[st], bytes);
-          const int pos_row = b * kBlock + u * kTok;
-#pragma unroll
-          for (int h = 0; h < HPC; ++h) {
-            const int y = (phys * p.Hkv + kvh0 + h) * kBlock + u * kTok;
-#pragma unroll
-            for (int bx = 0; bx < L::kKBoxes; ++bx) {
-              tma_load_2d(stg + L::kK + h * L::kHeadTile + bx * (kTok * 128), &tm_k, bx * 64, y,
-                          &full[st], pol_stream);
-              tma_load_2d(stg + L::kV + h * L::kHeadTile + bx * (kTok * 128), &tm_v, bx * 64, y,
-                          &full[st], pol_stream);
-            }
-          }
-#pragma unroll
-          for (int bx = 0; bx < L::kTBoxes; ++bx) {
-            tma_load_2d(stg + L::kCos + bx * (kTok * 128), &tm_cos, bx * 32, pos_row, &full[st],
-                        pol_keep);
-            tma_load_2d(stg + L::kSin + bx * (kTok * 128), &tm_sin, bx * 32, pos_row, &full[st],
-                        pol_keep);
-          }
-          if (p.scope_tags)
-            bulk_load(tags + st * 16, p.scope_tags + s * p.scope_stride + pos_row, 16, &full[st]);
-        }
-        if (*s_abort) break;
-      }
-      // Do not leave while copies into this CTA's shared memory are in flight.
-      const int issued = it;
-      for (int i = max(0, issued - S_); i < issued; ++i) {
-        if (!mbar_wait(&full[i % S_], (i / S_) & 1)) {
-          if (p.status) atomicOr(p.status, kStatusWaitTimeout);
-          break;
-        }
-      }
-    }
-    return;
-  }
-
-  // ---------------- consumer: KV head kvh0 + warp ----------------
-  const int kvh = kvh0 + warp;
+  // ---------------- consumers: warp (head, sub) takes the stages with it % 2 == sub ----------
+  const int head = warp % HPC;
+  const int sub = warp / HPC;
+  const int kvh = kvh0 + head;
   const int r = lane >> 2;  // token row (and B-operand column: query head)
   const int q4 = lane & 3;  // column pair
   const int G = p.G;
@@ -249,52 +264,54 @@ __global__ void __launch_bounds__((HPC + 1) * 32, 1)
   const int k_row = (lane & 7) + ((lane >> 3) & 1) * 8, k_chunk = lane >> 4;
   const int v_row = (lane & 7) + (lane >> 4) * 8, v_chunk = (lane >> 3) & 1;
 
-  int it = 0;
   bool ok = true;
-  for (int k = 0; k < nitems && ok; ++k) {
-    const int b = list_b[k];
-    const int nsub = min(4, (g.kv_len - b * kBlock + kTok - 1) / kTok);
-    for (int u = 0; u < nsub; ++u, ++it) {
+  const uint64_t pol_stream = policy_evict_first(), pol_keep = policy_evict_last();
+  for (int it = sub; it < total_iters && ok; it += kWph) {
+    const int b = list_b[it >> 2];
+    const int u = it & 3;
+    {
       const int st = it % S_;
-      if (!mbar_wait(&full[st], (it / S_) & 1)) {
+      if (!wait_use(&s_use[st], it / S_) || !mbar_wait(&full[st], (it / S_) & 1)) {
         if (lane == 0 && p.status) atomicOr(p.status, kStatusWaitTimeout);
         ok = false;
         break;
       }
       const uint8_t* stg = stages + st * L::kStage;
-      const uint32_t kbase = smem_u32(stg + L::kK + warp * L::kHeadTile);
-      const uint32_t vbase = smem_u32(stg + L::kV + warp * L::kHeadTile);
+      const uint32_t kbase = smem_u32(stg + L::kK + head * L::kHeadTile);
+      const uint32_t vbase = smem_u32(stg + L::kV + head * L::kHeadTile);
       const uint8_t* cosb = stg + L::kCos;
       const uint8_t* sinb = stg + L::kSin;
 
-      // K fragments (A operand, tokens x head_dim), then RoPE in registers.
-      uint32_t kf[KC][4];
-#pragma unroll
-      for (int kc = 0; kc < KC; ++kc) {
-        const int box = kc >> 2, chunk = (kc & 3) * 2 + k_chunk;
-        ldmatrix_x4(kbase + box * (kTok * 128) + swz128(k_row, chunk), kf[kc][0], kf[kc][1],
-                    kf[kc][2], kf[kc][3]);
-      }
+      // S^T = K . Q^T over chunk pairs (kc, kc + D/32): the pair holds the
+      // half-split RoPE partners, rotated in registers right after ldmatrix.
+      float sa[4] = {0.f, 0.f, 0.f, 0.f}, sb[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int kc = 0; kc < HALF_KC; ++kc) {
+        uint32_t ka[4], kb[4];
+        {
+          const int kc2 = kc + HALF_KC;
+          ldmatrix_x4(kbase + (kc >> 2) * (kTok * 128) + swz128(k_row, (kc & 3) * 2 + k_chunk),
+                      ka[0], ka[1], ka[2], ka[3]);
+          ldmatrix_x4(kbase + (kc2 >> 2) * (kTok * 128) + swz128(k_row, (kc2 & 3) * 2 + k_chunk),
+                      kb[0], kb[1], kb[2], kb[3]);
+        }
 #pragma unroll
         for (int reg = 0; reg < 4; ++reg) {
           const int row = r + (reg & 1) * 8;
           const int t = kc * 16 + 2 * q4 + (reg & 2) * 4;
           const uint32_t off = (t >> 5) * (kTok * 128) + swz128(row, (t & 31) >> 2) + (t & 3) * 4;
-          const float2 c = *reinterpret_cast<const float2*>(cosb + off);
-          const float2 sn = *reinterpret_cast<const float2*>(sinb + off);
-          const float2 lo2 = MK::unpack(kf[kc][reg]);
-          const float2 hi2 = MK::unpack(kf[kc + HALF_KC][reg]);
-          kf[kc][reg] = MK::pack(lo2.x * c.x - hi2.x * sn.x, lo2.y * c.y - hi2.y * sn.y);
-          kf[kc + HALF_KC][reg] = MK::pack(lo2.x * sn.x + hi2.x * c.x, lo2.y * sn.y + hi2.y * c.y);
+          const uint64_t c2 = *reinterpret_cast<const uint64_t*>(cosb + off);
+          const uint64_t s2 = *reinterpret_cast<const uint64_t*>(sinb + off);
+          const uint64_t lo2 = MK::unpack2(ka[reg]);
+          const uint64_t hi2 = MK::unpack2(kb[reg]);
+          // (lo, hi) -> (lo c - hi s, lo s + hi c), two lanes of fp32 per instruction
+          ka[reg] = MK::pack2(f2sub(f2mul(lo2, c2), f2mul(hi2, s2)));
+          kb[reg] = MK::pack2(f2fma(lo2, s2, f2mul(hi2, c2)));
         }
+        MK::mma(sa, ka, qf[kc][0], qf[kc][1]);
+        MK::mma(sb, kb, qf[kc + HALF_KC][0], qf[kc + HALF_KC][1]);
       }
-
-      // S^T = K . Q^T  -> sacc[0,1] = (token r, heads 2q4, 2q4+1), sacc[2,3] = token r + 8
-      float sacc[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-      for (int kc = 0; kc < KC; ++kc) MK::mma(sacc, kf[kc], qf[kc][0], qf[kc][1]);
+      float sacc[4] = {sa[0] + sb[0], sa[1] + sb[1], sa[2] + sb[2], sa[3] + sb[3]};
 
       const int j0 = b * kBlock + u * kTok + r;
       const int j1 = j0 + 8;
@@ -312,20 +329,25 @@ __global__ void __launch_bounds__((HPC + 1) * 32, 1)
       const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
       const float base0 = mn0 == -INFINITY ? 0.f : mn0;
       const float base1 = mn1 == -INFINITY ? 0.f : mn1;
-      const float a0 = exp2f(m0 - base0), a1 = exp2f(m1 - base1);
       const float p00 = exp2f(sacc[0] - base0), p01 = exp2f(sacc[1] - base1);
       const float p10 = exp2f(sacc[2] - base0), p11 = exp2f(sacc[3] - base1);
-      l0 = l0 * a0 + p00 + p10;
-      l1 = l1 * a1 + p01 + p11;
-      m0 = mn0;
-      m1 = mn1;
+      // Rescale the running sums only when some head's max moved (rare after a few stages).
+      if (__any_sync(0xffffffffu, mn0 != m0 || mn1 != m1)) {
+        const float a0 = exp2f(m0 - base0), a1 = exp2f(m1 - base1);
+        l0 *= a0;
+        l1 *= a1;
 #pragma unroll
-      for (int mt = 0; mt < KC; ++mt) {
-        o[mt][0] *= a0;
-        o[mt][1] *= a1;
-        o[mt][2] *= a0;
-        o[mt][3] *= a1;
+        for (int mt = 0; mt < KC; ++mt) {
+          o[mt][0] *= a0;
+          o[mt][1] *= a1;
+          o[mt][2] *= a0;
+          o[mt][3] *= a1;
+        }
+        m0 = mn0;
+        m1 = mn1;
       }
+      l0 += p00 + p10;
+      l1 += p01 + p11;
       const uint32_t pb0 = movmatrix_trans(MK::pack(p00, p01));
       const uint32_t pb1 = movmatrix_trans(MK::pack(p10, p11));
 
@@ -338,8 +360,23 @@ __global__ void __launch_bounds__((HPC + 1) * 32, 1)
                           vf[3]);
         MK::mma(o[mt], vf, pb0, pb1);
       }
+      // Release the stage; the last of the HPC warps reading it refills it.
       __syncwarp();
-      if (lane == 0) mbar_arrive(&empty[st]);
+      if (lane == 0) {
+        __threadfence_block();
+        const uint32_t done = atomicAdd(&released[st], 1u) + 1u;
+        const int next = it + S_;
+        if (done == static_cast<uint32_t>(HPC) * (it / S_ + 1) && next < total_iters &&
+            !*s_abort) {
+          __threadfence_block();
+          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+          issue_stage<D, HPC>(&tm_k, &tm_v, &tm_cos, &tm_sin, p, stages + st * L::kStage,
+                              &full[st], tags + st * 16, &s_use[st], next / S_, s, kvh0,
+                              list_b[next >> 2], list_p[next >> 2], next & 3, pol_stream,
+                              pol_keep);
+          atomicMax(&s_issued, next + 1);
+        }
+      }
     }
   }
   if (!ok) *s_abort = 1;
@@ -350,6 +387,50 @@ __global__ void __launch_bounds__((HPC + 1) * 32, 1)
     l0 += __shfl_xor_sync(0xffffffffu, l0, sh);
     l1 += __shfl_xor_sync(0xffffffffu, l1, sh);
   }
+
+  // Merge the two warps of each KV head through the (now idle) stage buffers:
+  // layout [head][36 values][32 lanes] fp32. Every issued stage has been
+  // consumed unless a wait timed out; then wait (bounded) for the copies
+  // still in flight before reusing the buffers.
+  named_barrier(1, kConsumers * 32);
+  if (*s_abort && threadIdx.x == 0) {
+    const int issued = s_issued;
+    for (int i = max(0, issued - S_); i < issued; ++i)
+      if (!mbar_wait(&full[i % S_], (i / S_) & 1)) break;
+  }
+  named_barrier(1, kConsumers * 32);
+  float* mrg = reinterpret_cast<float*>(stages) + head * (36 * 32);
+  if (sub == 1) {
+#pragma unroll
+    for (int mt = 0; mt < KC; ++mt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) mrg[(mt * 4 + e) * 32 + lane] = o[mt][e];
+    mrg[32 * 32 + lane] = m0;
+    mrg[33 * 32 + lane] = m1;
+    mrg[34 * 32 + lane] = l0;
+    mrg[35 * 32 + lane] = l1;
+  }
+  named_barrier(1, kConsumers * 32);
+  if (sub == 1) return;
+  {
+    const float pm0 = mrg[32 * 32 + lane], pm1 = mrg[33 * 32 + lane];
+    const float M0 = fmaxf(m0, pm0), M1 = fmaxf(m1, pm1);
+    const float b0 = M0 == -INFINITY ? 0.f : M0, b1 = M1 == -INFINITY ? 0.f : M1;
+    const float sa0 = exp2f(m0 - b0), sp0 = exp2f(pm0 - b0);
+    const float sa1 = exp2f(m1 - b1), sp1 = exp2f(pm1 - b1);
+    l0 = l0 * sa0 + mrg[34 * 32 + lane] * sp0;
+    l1 = l1 * sa1 + mrg[35 * 32 + lane] * sp1;
+#pragma unroll
+    for (int mt = 0; mt < KC; ++mt) {
+      o[mt][0] = o[mt][0] * sa0 + mrg[(mt * 4 + 0) * 32 + lane] * sp0;
+      o[mt][1] = o[mt][1] * sa1 + mrg[(mt * 4 + 1) * 32 + lane] * sp1;
+      o[mt][2] = o[mt][2] * sa0 + mrg[(mt * 4 + 2) * 32 + lane] * sp0;
+      o[mt][3] = o[mt][3] * sa1 + mrg[(mt * 4 + 3) * 32 + lane] * sp1;
+    }
+    m0 = M0;
+    m1 = M1;
+  }
+
   const int ha = 2 * q4, hb = 2 * q4 + 1;
   const int64_t row_a = static_cast<int64_t>(s) * p.Hq + kvh * G + ha;
   const int64_t row_b = row_a + 1;
@@ -455,7 +536,7 @@ cudaError_t launch_tc_typed(const DecodeParams& p, CUtensorMapDataType dt, cudaS
                                        static_cast<int>(smem));
   if (e != cudaSuccess) return e;
   dim3 grid(p.max_splits, p.Hkv / HPC, p.S);
-  kernel<<<grid, (HPC + 1) * 32, smem, stream>>>(mk, mv, mc, ms, p);
+  kernel<<<grid, HPC * kWph * 32, smem, stream>>>(mk, mv, mc, ms, p);
   return cudaGetLastError();
 }
 

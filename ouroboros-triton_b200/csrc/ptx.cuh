@@ -148,6 +148,38 @@ __device__ __forceinline__ uint32_t movmatrix_trans(uint32_t a) {
   return d;
 }
 
+// Packed fp32 pairs (sm_100 f32x2 pipe): two IEEE fp32 operations per instruction.
+__device__ __forceinline__ uint64_t f2pack(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ float2 f2unpack(uint64_t v) {
+  float2 r;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(r.x), "=f"(r.y) : "l"(v));
+  return r;
+}
+__device__ __forceinline__ uint64_t f2mul(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2sub(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
+// Named barrier over `nthreads` threads (id 0 is __syncthreads).
+__device__ __forceinline__ void named_barrier(uint32_t id, uint32_t nthreads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
 template <typename T>
 struct MmaKind;
 template <>
@@ -163,6 +195,13 @@ struct MmaKind<__nv_bfloat16> {
   static __device__ __forceinline__ float2 unpack(uint32_t v) {
     // bf16 -> fp32 is a 16-bit shift of the bit pattern
     return make_float2(__uint_as_float(v << 16), __uint_as_float(v & 0xffff0000u));
+  }
+  static __device__ __forceinline__ uint64_t unpack2(uint32_t v) {
+    return f2pack(__uint_as_float(v << 16), __uint_as_float(v & 0xffff0000u));
+  }
+  static __device__ __forceinline__ uint32_t pack2(uint64_t v) {
+    const float2 f = f2unpack(v);
+    return pack(f.x, f.y);
   }
   static __device__ __forceinline__ uint32_t pack(float lo, float hi) {
     __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
@@ -182,6 +221,14 @@ struct MmaKind<__half> {
   static __device__ __forceinline__ float2 unpack(uint32_t v) {
     __half2 h = *reinterpret_cast<__half2*>(&v);
     return __half22float2(h);
+  }
+  static __device__ __forceinline__ uint64_t unpack2(uint32_t v) {
+    const float2 f = unpack(v);
+    return f2pack(f.x, f.y);
+  }
+  static __device__ __forceinline__ uint32_t pack2(uint64_t v) {
+    const float2 f = f2unpack(v);
+    return pack(f.x, f.y);
   }
   static __device__ __forceinline__ uint32_t pack(float lo, float hi) {
     __half2 h = __floats2half2_rn(lo, hi);

@@ -220,3 +220,46 @@ def test_long_context_checksum_property(cuda):
                                     torch.from_numpy(cos).cuda(), torch.from_numpy(sin).cuda())
     want = consts.repeat_interleave(8).view(1, 64, 1).expand(3, 64, 128)
     assert (out.float() - want).abs().max().item() < 1e-2
+
+
+def test_tc_pipeline_under_load_reports_clean_status(cuda):
+    """Many CTAs streaming long chains at once: every bounded wait must succeed.
+
+    The status word collects the kernels' error bits (a wait that gave up sets
+    bit 2); a clean run leaves it 0, and the rows still match the oracle.
+    """
+    rng = random.Random(8)
+    lens = [rng.randint(4000, 9000) for _ in range(48)]
+    pool = sum(-(-n // 64) for n in lens) + 11
+    bt = BlockTable(pool)
+    ids = [bt.allocate_block() for _ in range(pool)]
+    rng.shuffle(ids)
+    for i in ids:
+        bt.free_block(i)
+    heads = [bt.allocate_chain(-(-n // 64)) for n in lens]
+    pt = build_page_table_array(bt, heads)
+    g = torch.Generator(device="cuda").manual_seed(8)
+    k = (torch.randn(pool, 8, 64, 128, generator=g, device="cuda") * 0.5).bfloat16()
+    v = (torch.randn(pool, 8, 64, 128, generator=g, device="cuda") * 0.5).bfloat16()
+    q = (torch.randn(len(lens), 64, 128, generator=g, device="cuda") * 0.5).bfloat16()
+    cos, sin = ao.rope_tables(pt.shape[1] * 64, 128, 500000.0)
+    for split in (0, 8, 24):
+        status = torch.zeros(1, dtype=torch.int32, device="cuda")
+        out = ba.block_attention_decode(torch.from_numpy(pt).cuda(), q, k, v,
+                                        torch.tensor(lens).cuda(), torch.from_numpy(cos).cuda(),
+                                        torch.from_numpy(sin).cuda(), kernel="tc",
+                                        split_blocks=split, status=status)
+        torch.cuda.synchronize()
+        assert int(status.item()) == 0, split
+        for s in (0, 17, 47):
+            row = pt[s:s + 1]
+            used = sorted({int(x) for x in row.reshape(-1) if x >= 0})
+            remap = np.full(pool, -1, np.int32)
+            remap[used] = np.arange(len(used))
+            small = np.where(row >= 0, remap[np.maximum(row, 0)], -1).astype(np.int32)
+            sel = torch.tensor(used, device="cuda")
+            want = ao.decode_attention(small, q[s:s + 1].float().cpu().numpy(),
+                                       k.index_select(0, sel).float().cpu().numpy(),
+                                       v.index_select(0, sel).float().cpu().numpy(), [lens[s]],
+                                       cos, sin)
+            _close_half(out[s:s + 1], want, f"stress seq {s} split {split}")
