@@ -219,6 +219,24 @@ int ouro_kv_append(const void* k_new, const void* v_new, const int32_t* page_tab
                    int32_t elem_bytes, int32_t max_blocks, int32_t num_phys_blocks,
                    int32_t* status, void* stream);
 
+/* ------------------------------------------------------------------------
+ * Allocation-free paged decode. No counterpart in the reference.
+ *
+ * Same arguments and result as ouro_paged_decode, but `workspace` and
+ * `workspace_bytes` are ignored: the split-K partials go to a 32 MiB array
+ * compiled into this library, so the call allocates no device memory. For
+ * callers that cannot allocate while they run (a loop being captured into a
+ * CUDA graph by its host framework, a fixed memory budget, an allocator this
+ * library cannot reach). Each GPU on which the library's device code is
+ * loaded holds the 32 MiB until the process exits. If the partials would not
+ * fit, the call fails with OURO_EINVAL when split_blocks was given, and picks
+ * fewer, larger chunks when split_blocks is 0. All calls share the array:
+ * calls that overlap on the GPU race, so keep them on one stream. The first
+ * call on each device looks up the array's device address (with that device
+ * current); make it before any stream capture begins.
+ * ---------------------------------------------------------------------- */
+int ouro_paged_decode_noalloc(const ouro_decode_args* args, void* stream);
+
 #ifdef __cplusplus
 }  /* extern "C" */
 #endif

@@ -259,3 +259,17 @@ int ouro_validate_page_table(const int32_t* page_table, const int32_t* seq_lens,
 }
 
 }  // extern "C"
+
+// Named entry points into the decode argument checks and split-K planner for
+// other launchers in this library (declared in decode_capi.hpp).
+namespace ouro::capi {
+
+DecodeParams decode_params(const ouro_decode_args* a) { return to_params(a); }
+
+void decode_plan(DecodeParams& p, const ouro_decode_args* a, bool* use_tc, size_t* ws_bytes) {
+  plan(p, a, use_tc, ws_bytes);
+}
+
+void cuda_check(cudaError_t e, const char* what) { check_cuda(e, what); }
+
+}  // namespace ouro::capi

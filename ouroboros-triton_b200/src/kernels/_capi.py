@@ -60,3 +60,4 @@ _native.register("ouro_paged_attention", ctypes.c_int, [ctypes.POINTER(Attention
 _native.register("ouro_kv_append", ctypes.c_int,
                  [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _i32, _i32,
                   _vp, _vp])
+_native.register("ouro_paged_decode_noalloc", ctypes.c_int, [ctypes.POINTER(DecodeArgs), _vp])
