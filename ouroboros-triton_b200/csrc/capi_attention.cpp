@@ -197,10 +197,18 @@ extern "C" {
 int ouro_paged_attention(const ouro_attention_args* args, void* stream) {
   OURO_CAPI_GUARD({
     ouro::RowsParams p = to_rows(args);
-    if (args->kernel != 0 && args->kernel != 1)
-      fail(OURO_EUNSUPPORTED, "only the CUDA-core multi-row kernel is built for these arguments");
+    if (args->kernel < 0 || args->kernel > 2)
+      fail(OURO_EINVAL, "kernel selector must be 0 (auto), 1 (cuda cores) or 2 (tensor cores)");
+    const bool tc_ok = ouro::prefill_tc_supported(p, args->dtype);
+    if (args->kernel == 2 && !tc_ok)
+      fail(OURO_EUNSUPPORTED,
+           "tensor-core attention needs dense fp16/bf16 queries, head_dim 128, no bias or block "
+           "mask, and a GQA group dividing 128");
     auto st = static_cast<cudaStream_t>(stream);
-    check_cuda(ouro::launch_attend_rows_simt(p, args->dtype, st), "paged attention (cuda cores)");
+    if (args->kernel == 2 || (args->kernel == 0 && tc_ok))
+      check_cuda(ouro::launch_prefill_tc(p, args->dtype, st), "paged attention (tensor cores)");
+    else
+      check_cuda(ouro::launch_attend_rows_simt(p, args->dtype, st), "paged attention (cuda cores)");
   })
 }
 

@@ -31,5 +31,8 @@ struct RowsParams {
 };
 
 cudaError_t launch_attend_rows_simt(const RowsParams& p, int dtype, cudaStream_t stream);
+// tcgen05 chunked prefill: dense fp16/bf16 queries, head_dim 128, no bias / block mask.
+bool prefill_tc_supported(const RowsParams& p, int dtype);
+cudaError_t launch_prefill_tc(const RowsParams& p, int dtype, cudaStream_t stream);
 
 }  // namespace ouro

@@ -1,0 +1,120 @@
+"""Chunked prefill on the tcgen05 tensor-core kernel vs the oracle.
+
+Tolerance: max-abs 2e-2 and mean-abs 2e-3 (fp16/bf16) against the fp32
+oracle's prefill rows (the row form of dense_reference with a causal bias).
+Every launch also passes a status word that must stay 0 (no bounded wait
+gave up, no bad page entry).
+"""
+
+import random
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import attention_oracle as ao
+from src.block_table import BlockTable, build_page_table_array
+from src.kernels import block_attention as ba
+
+pytestmark = pytest.mark.gpu
+
+
+def _case(seed, totals, hq, hkv, L, dtype, d=128, base=500000.0):
+    rng = random.Random(seed)
+    pool = sum(-(-n // 64) for n in totals) + 9
+    bt = BlockTable(pool)
+    ids = [bt.allocate_block() for _ in range(pool)]
+    rng.shuffle(ids)
+    for i in ids:
+        bt.free_block(i)
+    heads = [bt.allocate_chain(-(-n // 64)) for n in totals]
+    pt = build_page_table_array(bt, heads)
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    k = (torch.randn(pool, hkv, 64, d, generator=g, device="cuda") * 0.5).to(dtype)
+    v = (torch.randn(pool, hkv, 64, d, generator=g, device="cuda") * 0.5).to(dtype)
+    q = (torch.randn(len(totals), hq, L, d, generator=g, device="cuda") * 0.5).to(dtype)
+    cos, sin = ao.rope_tables(pt.shape[1] * 64, d, base)
+    return pt, q, k, v, cos, sin
+
+
+def _run(pt, q, k, v, starts, totals, cos, sin, **kw):
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    out = ba.chunked_prefill_attention(torch.from_numpy(pt).cuda(), q, k, v,
+                                       torch.tensor(starts).cuda(), torch.tensor(totals).cuda(),
+                                       torch.from_numpy(cos).cuda(), torch.from_numpy(sin).cuda(),
+                                       status=status, **kw)
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    return out
+
+
+def _check(out, want, label):
+    err = np.abs(out.float().cpu().numpy() - want)
+    assert err.max() <= 2e-2 and err.mean() <= 2e-3, (label, err.max(), err.mean())
+
+
+@pytest.mark.parametrize("hq,hkv,dtype,causal", [
+    (32, 8, torch.bfloat16, True),     # Llama-3-8B attention shape (group 4)
+    (4, 4, torch.bfloat16, False),     # MHA, non-causal
+    (16, 2, torch.float16, True),      # group 8
+    (8, 4, torch.bfloat16, True),      # group 2
+])
+def test_tensor_core_prefill_vs_oracle(cuda, hq, hkv, dtype, causal):
+    L = 512
+    starts = [512, 0, 1024]
+    totals = [1024, 300, 1100]          # second and third sequences end inside the chunk
+    pt, q, k, v, cos, sin = _case(hq + hkv, totals, hq, hkv, L, dtype)
+    out = _run(pt, q, k, v, starts, totals, cos, sin, causal=causal, kernel="tc")
+    want = ao.prefill_attention(pt, q.float().cpu().numpy(), k.float().cpu().numpy(),
+                                v.float().cpu().numpy(), starts, totals, cos, sin, causal=causal)
+    _check(out, want, f"{hq}/{hkv} causal={causal}")
+    # rows past the sequence end are left untouched (zero-initialised output)
+    assert (out[1, :, 300:].float() == 0).all()
+
+
+def test_tensor_cores_agree_with_cuda_cores(cuda):
+    L, starts, totals = 256, [64, 700], [320, 956]
+    pt, q, k, v, cos, sin = _case(7, totals, 32, 8, L, torch.bfloat16)
+    a = _run(pt, q, k, v, starts, totals, cos, sin, kernel="tc")
+    b = _run(pt, q, k, v, starts, totals, cos, sin, kernel="simt")
+    _check(a, b.float().cpu().numpy(), "tc vs simt")
+
+
+def test_two_chunk_prefill_through_kv_append(cuda):
+    """Config-4 flow at small scale: each 512-token chunk's K/V is appended into
+    newly allocated blocks, then the chunk attends to everything before it."""
+    hq, hkv, d, L, chunks, S = 32, 8, 128, 512, 2, 2
+    total = L * chunks
+    bt = BlockTable(64)
+    heads = [bt.allocate_chain(L // 64) for _ in range(S)]
+    g = torch.Generator(device="cuda").manual_seed(3)
+    kc = torch.zeros(64, hkv, 64, d, dtype=torch.bfloat16, device="cuda")
+    vc = torch.zeros_like(kc)
+    cos, sin = ao.rope_tables(total, d, 500000.0)
+    q_all = (torch.randn(S, hq, total, d, generator=g, device="cuda") * 0.5).bfloat16()
+    k_all = (torch.randn(S, hkv, total, d, generator=g, device="cuda") * 0.5).bfloat16()
+    v_all = (torch.randn(S, hkv, total, d, generator=g, device="cuda") * 0.5).bfloat16()
+    outs = []
+    for c in range(chunks):
+        if c > 0:                                   # [EXPAND]: grow each chain by one chunk
+            for h in heads:
+                tail = bt.chain_tail(h)
+                for _ in range(L // 64):
+                    tail = bt.expand_chain(tail)
+        pt = torch.from_numpy(build_page_table_array(bt, heads, pad_to=total // 64)).cuda()
+        start = torch.full((S,), c * L, dtype=torch.int32, device="cuda")
+        cnt = torch.full((S,), L, dtype=torch.int32, device="cuda")
+        ba.paged_kv_append(k_all[:, :, c * L:(c + 1) * L], v_all[:, :, c * L:(c + 1) * L], pt,
+                           start, cnt, kc, vc)
+        lens = torch.full((S,), (c + 1) * L, dtype=torch.int32, device="cuda")
+        outs.append(ba.chunked_prefill_attention(pt, q_all[:, :, c * L:(c + 1) * L], kc, vc,
+                                                 start, lens, torch.from_numpy(cos).cuda(),
+                                                 torch.from_numpy(sin).cuda(), kernel="tc"))
+    got = torch.cat(outs, dim=2).float().cpu().numpy()
+    # oracle: one dense causal pass over the whole prompt
+    pt_final = build_page_table_array(bt, heads, pad_to=total // 64)
+    want = ao.prefill_attention(pt_final, q_all.float().cpu().numpy(), kc.float().cpu().numpy(),
+                                vc.float().cpu().numpy(), [0] * S, [total] * S, cos, sin,
+                                causal=True)
+    err = np.abs(got - want)
+    assert err.max() <= 2e-2 and err.mean() <= 2e-3, (err.max(), err.mean())
