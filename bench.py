@@ -409,6 +409,97 @@ def _traffic_from_profile():
     return None
 
 
+PREFILL = dict(workload="chunked_prefill_llama3_8b_attention", prompts=8, prompt_len=4096,
+               chunk=512, q_heads=32, kv_heads=8, head_dim=128, dtype="bf16", rope_base=500000.0,
+               causal=True)
+
+
+def run_prefill(args):
+    """Chunked prefill: every 512-token chunk of 8 x 4096-token prompts, causal, GQA 32/8.
+
+    A step is one full pass (8 chunk launches, each over all 8 prompts) with the prompts' K/V
+    already resident in the paged cache; FLOPs = 4 * D * Hq * sum_p sum_i (i + 1).
+    """
+    import torch
+
+    from oracle import attention_oracle as ao  # RoPE table construction only
+    from src.block_table import BlockTable
+    from src.kernels.block_attention import PrefillCall
+
+    P = PREFILL
+    device = torch.device("cuda", 0)
+    S, T, C = P["prompts"], P["prompt_len"], P["chunk"]
+    hq, hkv, d = P["q_heads"], P["kv_heads"], P["head_dim"]
+    nbp = T // 64
+    pool = S * nbp + 16
+    bt = BlockTable(pool)
+    ids = [bt.allocate_block() for _ in range(pool)]
+    random.Random(4).shuffle(ids)
+    for i in ids:
+        bt.free_block(i)
+    heads = [bt.allocate_chain(nbp) for _ in range(S)]
+    pt = torch.from_numpy(bt.export_page_table(heads, nbp)).to(device)
+    g = torch.Generator(device=device).manual_seed(4)
+    k = (torch.randn(pool, hkv, 64, d, generator=g, device=device) * 0.5).bfloat16()
+    v = (torch.randn(pool, hkv, 64, d, generator=g, device=device) * 0.5).bfloat16()
+    q = (torch.randn(S, hq, T, d, generator=g, device=device) * 0.5).bfloat16()
+    cos, sin = ao.rope_tables(T, d, P["rope_base"])
+    cos, sin = torch.from_numpy(cos).to(device), torch.from_numpy(sin).to(device)
+    status = torch.zeros(1, dtype=torch.int32, device=device)
+    calls = []
+    for c in range(T // C):
+        qc = q[:, :, c * C:(c + 1) * C].contiguous()
+        starts = torch.full((S,), c * C, dtype=torch.int32, device=device)
+        lens = torch.full((S,), (c + 1) * C, dtype=torch.int32, device=device)
+        pt_c = pt.clone()  # the chains as they stand after chunk c was appended
+        pt_c[:, (c + 1) * C // 64:] = -1
+        calls.append(PrefillCall(pt_c, qc, k, v, starts, lens, cos, sin, causal=True,
+                                 kernel=args.kernel if args.kernel != "auto" else "auto",
+                                 status=status))
+    flops = 4.0 * d * hq * S * (T * (T + 1) / 2.0)
+    for _ in range(max(args.warmup, 3)):
+        for cl in calls:
+            cl.launch()
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream(device)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(0) as clk:
+        torch.cuda.synchronize()
+        e0.record(stream)
+        for _ in range(args.steps):
+            for cl in calls:
+                cl.launch()
+        e1.record(stream)
+        torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    tflops = flops / (ms / 1000.0) / 1e12
+    peak = None
+    pk = ROOT / "MEASURED_PEAKS.json"
+    if pk.exists():
+        peak = float(json.loads(pk.read_text())["bf16_tflops"])
+    # spot check: one head of two prompts' last chunk vs the oracle
+    want = ao.prefill_attention(pt[:2].cpu().numpy(), q[:2, :1, T - C:].float().cpu().numpy(),
+                                k[:, :1].float().cpu().numpy(), v[:, :1].float().cpu().numpy(),
+                                [T - C] * 2, [T] * 2, cos.cpu().numpy(), sin.cpu().numpy())
+    got = calls[-1].out[:2, :1].float().cpu().numpy()
+    err = abs(got - want)
+    line = {
+        "metric": "chunked-prefill attn TFLOP/s (causal, bf16)", "value": tflops,
+        "unit": "TFLOP/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": ms, "higher_is_better": True, "dtype": "bf16", "data": "synthetic",
+        "config": dict(P, chunk_launches=len(calls)),
+        "tokens_per_s": S * T / (ms / 1000.0),
+        "roofline": {"bound": "tensor", "achieved": tflops, "peak": peak, "unit": "TFLOP/s",
+                     "frac": (tflops / peak) if peak else None,
+                     "algorithmic_flops_per_step": flops},
+        "check": {"max_abs": float(err.max()), "mean_abs": float(err.mean()),
+                  "kernel_status": int(status.item())},
+        "clocks": clk.summary(),
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def main() -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -418,12 +509,16 @@ def main() -> int:
     ap.add_argument("--split-blocks", type=int, default=0)
     ap.add_argument("--kernel", default="auto", choices=["auto", "tc", "simt"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
+    ap.add_argument("--workload", choices=["decode", "prefill"], default="decode",
+                    help="decode (the headline metric) or the chunked-prefill tensor-core pass")
     ap.add_argument("--seqs", type=int, default=0,
                     help="sequences per GPU (default: the workload's 256); smaller values "
                          "make a profiling case of the same kernel")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)
+    if args.workload == "prefill":
+        return run_prefill(args)
     return run_ours(args)
 
 

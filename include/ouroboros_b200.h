@@ -200,8 +200,14 @@ typedef struct ouro_attention_args {
   int32_t max_blocks, num_phys_blocks, max_positions;
   int32_t dtype, causal, kernel; /* kernel: 0 auto, 1 CUDA cores, 2 tensor cores */
   float softmax_scale;        /* <= 0: 1/sqrt(D) */
+  void* workspace;            /* tensor-core path: rotated-key scratch, 16-B aligned */
+  size_t workspace_bytes;     /* >= ouro_attention_plan's bytes */
 } ouro_attention_args;
 
+/* Kernel choice and the workspace the tensor-core path needs
+ * (S * Hkv * max_blocks * 64 * D elements of the cache dtype; 0 on CUDA cores). */
+int ouro_attention_plan(const ouro_attention_args* args, size_t* workspace_bytes,
+                        int32_t* uses_tensor_cores);
 int ouro_paged_attention(const ouro_attention_args* args, void* stream);
 
 /* ------------------------------------------------------------------------

@@ -127,7 +127,7 @@ void plan(ouro::DecodeParams& p, const ouro_decode_args* a, bool* use_tc, size_t
   } else if (a->kernel != 1) {
     fail(OURO_EINVAL, "kernel selector must be 0 (auto), 1 (cuda cores) or 2 (tensor cores)");
   }
-  int split = a->split_blocks > 0 ? a->split_blocks : choose_split(p, tc, 16);
+  int split = a->split_blocks > 0 ? a->split_blocks : choose_split(p, tc, 24);
   split = std::min(split, std::max(p.max_blocks, 1));
   if (tc) split = std::min(split, 512);  // block list lives in shared memory
   p.split_blocks = split;
@@ -173,6 +173,8 @@ ouro::RowsParams to_rows(const ouro_attention_args* a) {
   const float scale = a->softmax_scale > 0.f ? a->softmax_scale
                                              : 1.0f / std::sqrt(static_cast<float>(a->head_dim));
   p.scale_log2 = scale * ouro::kLog2e;
+  p.workspace = a->workspace;
+  p.workspace_bytes = static_cast<int64_t>(a->workspace_bytes);
   if (dtype_bytes(a->dtype) == 0) fail(OURO_EUNSUPPORTED, "unsupported dtype code");
   if (p.S < 0 || p.Lq < 0) fail(OURO_EINVAL, "num_seqs and q_len must be >= 0");
   if (p.Hq <= 0 || p.Hkv <= 0 || p.Hq % p.Hkv != 0)
@@ -194,6 +196,18 @@ ouro::RowsParams to_rows(const ouro_attention_args* a) {
 
 extern "C" {
 
+int ouro_attention_plan(const ouro_attention_args* args, size_t* workspace_bytes,
+                        int32_t* uses_tensor_cores) {
+  OURO_CAPI_GUARD({
+    ouro::RowsParams p = to_rows(args);
+    const bool tc = args->kernel == 2 ||
+                    (args->kernel == 0 && ouro::prefill_tc_supported(p, args->dtype));
+    if (workspace_bytes)
+      *workspace_bytes = tc ? static_cast<size_t>(ouro::prefill_workspace_bytes(p)) : 0;
+    if (uses_tensor_cores) *uses_tensor_cores = tc ? 1 : 0;
+  })
+}
+
 int ouro_paged_attention(const ouro_attention_args* args, void* stream) {
   OURO_CAPI_GUARD({
     ouro::RowsParams p = to_rows(args);
@@ -205,8 +219,13 @@ int ouro_paged_attention(const ouro_attention_args* args, void* stream) {
            "tensor-core attention needs dense fp16/bf16 queries, head_dim 128, no bias or block "
            "mask, and a GQA group dividing 128");
     auto st = static_cast<cudaStream_t>(stream);
-    if (args->kernel == 2 || (args->kernel == 0 && tc_ok))
+    if (args->kernel == 2 || (args->kernel == 0 && tc_ok)) {
+      const int64_t need = ouro::prefill_workspace_bytes(p);
+      if (p.workspace == nullptr || p.workspace_bytes < need)
+        fail(OURO_EINVAL, "tensor-core attention workspace too small: need " +
+                              std::to_string(need) + " bytes");
       check_cuda(ouro::launch_prefill_tc(p, args->dtype, st), "paged attention (tensor cores)");
+    }
     else
       check_cuda(ouro::launch_attend_rows_simt(p, args->dtype, st), "paged attention (cuda cores)");
   })

@@ -7,12 +7,12 @@
 // The CTA walks 128-key tiles (two 64-token blocks resolved through the page
 // table) up to its causal limit:
 //   warp 8      TMA producer: K and V tiles into a 2-stage ring (128-byte
-//               swizzle, boxes of 64 keys x 64 columns, layout
-//               [64-column atom][128 keys][128 B])
-//   warps 4-7   RoPE: the query tile once (from global, scaled by
-//               softmax_scale * log2 e) and every K tile in place in shared
-//               memory (the d / d + 64 partners sit at the same swizzled
-//               offset of the two atoms)
+//               swizzle, layout [64-column atom][128 keys][128 B]); K comes
+//               already rotated from the dense scratch written by rope_k.cu
+//               (one box of 128 keys per atom), V from the paged cache
+//               (boxes of 64 keys, one per block)
+//   warps 4-7   RoPE on the query tile (from global, scaled by
+//               softmax_scale * log2 e), once per CTA
 //   warp 9      TMEM owner and MMA issuer: S_j = Q K_j^T into one of two
 //               128-column TMEM buffers, then O += P_{j-1} V_{j-1}
 //               (V as an MN-major operand), tcgen05.commit to mbarriers
@@ -49,13 +49,17 @@ constexpr float kRescaleLog2 = 8.0f;
 constexpr int kOffQ = 0;
 constexpr int kOffK = kOffQ + kTile;          // 2 stages
 constexpr int kOffV = kOffK + 2 * kTile;      // 2 stages
-constexpr int kOffP = kOffV + 2 * kTile;
-constexpr int kOffBar = kOffP + kTile;
+constexpr int kOffP = kOffV + 2 * kTile;      // 2 buffers
+constexpr int kOffBar = kOffP + 2 * kTile;
 constexpr int kSmemBytes = kOffBar + 256 + 1024;
 
+// Every ring barrier is per buffer: a parity wait is only valid while the
+// barrier is at most one phase past the awaited one, and per-buffer barriers
+// keep each waiter within that window (a shared PV barrier could run two
+// phases ahead once P is double-buffered).
 struct Bars {
-  uint64_t kv_full[2], kv_empty[2], k_rot[2], s_full[2], s_free[2];
-  uint64_t q_ready, p_ready, pv_done;
+  uint64_t kv_full[2], kv_empty[2], s_full[2], s_free[2], p_ready[2], pv_done[2];
+  uint64_t q_ready;
   uint32_t tmem_base;
 };
 
@@ -100,6 +104,13 @@ __device__ __forceinline__ void rope8(uint4& lo, uint4& hi, const float* c, cons
   }
 }
 
+// 2^x with the hardware approximation (relative error ~2^-22; -inf -> 0).
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 __device__ __forceinline__ uint32_t sw_off(int row, int chunk) {
   return static_cast<uint32_t>(row * 128 + ((chunk ^ (row & 7)) << 4));
 }
@@ -107,7 +118,8 @@ __device__ __forceinline__ uint32_t sw_off(int row, int chunk) {
 template <typename T>
 __global__ void __launch_bounds__(kThreads, 1)
     prefill_tc_kernel(const __grid_constant__ CUtensorMap tm_k,
-                      const __grid_constant__ CUtensorMap tm_v, const RowsParams p) {
+                      const __grid_constant__ CUtensorMap tm_v, const RowsParams p,
+                      int32_t krot_rows_per_head) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -138,13 +150,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int i = 0; i < 2; ++i) {
       mbar_init(&bars->kv_full[i], 1);
       mbar_init(&bars->kv_empty[i], 1);
-      mbar_init(&bars->k_rot[i], 128);
       mbar_init(&bars->s_full[i], 1);
       mbar_init(&bars->s_free[i], 128);
+      mbar_init(&bars->p_ready[i], 128);
+      mbar_init(&bars->pv_done[i], 1);
     }
     mbar_init(&bars->q_ready, 128);
-    mbar_init(&bars->p_ready, 128);
-    mbar_init(&bars->pv_done, 1);
     fence_barrier_init();
   }
   if (warp == 9) {
@@ -177,6 +188,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_arrive_expect_tx(&bars->kv_full[st], 2 * kTile);
         uint8_t* kd = smem + kOffK + st * kTile;
         uint8_t* vd = smem + kOffV + st * kTile;
+        // rotated keys: rows (s, kvh, 128 j .. 128 j + 127) of the scratch
+        const int ky = (s * p.Hkv + kvh) * krot_rows_per_head + j * kBN;
+        for (int a = 0; a < 2; ++a)
+          tma_load_2d(kd + a * kAtom, &tm_k, a * 64, ky, &bars->kv_full[st], pol);
         for (int blk = 0; blk < 2; ++blk) {
           const int b = 2 * j + blk;
           const int lb = b < nb ? b : 2 * j;  // a block past the keys repeats a valid one
@@ -186,12 +201,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             phys = 0;
           }
           const int y = (phys * p.Hkv + kvh) * kBlock;
-          for (int a = 0; a < 2; ++a) {
-            tma_load_2d(kd + a * kAtom + blk * (kAtom / 2), &tm_k, a * 64, y, &bars->kv_full[st],
-                        pol);
+          for (int a = 0; a < 2; ++a)
             tma_load_2d(vd + a * kAtom + blk * (kAtom / 2), &tm_v, a * 64, y, &bars->kv_full[st],
                         pol);
-          }
         }
       }
     }
@@ -227,46 +239,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       fence_proxy_async_smem();
       mbar_arrive(&bars->q_ready);
     }
-    for (int j = 0; j < n_tiles; ++j) {
-      const int st = j & 1;
-      if (!mbar_wait(&bars->kv_full[st], (j >> 1) & 1)) {
-        fail(kStatusWaitTimeout);
-        break;
-      }
-      uint8_t* kt = smem + kOffK + st * kTile;
-      const int pos = j * kBN + r;
-      const bool pos_ok = pos < p.max_pos;
-      const float4* crow = reinterpret_cast<const float4*>(p.cos + static_cast<int64_t>(pos) * half);
-      const float4* srow = reinterpret_cast<const float4*>(p.sin + static_cast<int64_t>(pos) * half);
-      for (int c = 0; c < 8; ++c) {
-        uint4 lo = *reinterpret_cast<uint4*>(kt + sw_off(r, c));
-        uint4 hi = *reinterpret_cast<uint4*>(kt + kAtom + sw_off(r, c));
-        float cs[8] = {1.f, 1.f, 1.f, 1.f, 1.f, 1.f, 1.f, 1.f}, sn[8] = {0.f};
-        if (pos_ok) {
-          const float4 c0 = crow[2 * c], c1 = crow[2 * c + 1];
-          const float4 s0 = srow[2 * c], s1 = srow[2 * c + 1];
-          cs[0] = c0.x; cs[1] = c0.y; cs[2] = c0.z; cs[3] = c0.w;
-          cs[4] = c1.x; cs[5] = c1.y; cs[6] = c1.z; cs[7] = c1.w;
-          sn[0] = s0.x; sn[1] = s0.y; sn[2] = s0.z; sn[3] = s0.w;
-          sn[4] = s1.x; sn[5] = s1.y; sn[6] = s1.z; sn[7] = s1.w;
-        }
-        rope8<T>(lo, hi, cs, sn, 1.f);
-        *reinterpret_cast<uint4*>(kt + sw_off(r, c)) = lo;
-        *reinterpret_cast<uint4*>(kt + kAtom + sw_off(r, c)) = hi;
-      }
-      fence_proxy_async_smem();
-      mbar_arrive(&bars->k_rot[st]);
-    }
   } else if (warp == 9) {
     // ------------------------------ MMA issuer ------------------------------
     if (lane == 0) {
       const uint32_t idesc_s = umma_idesc_f16(Elem<T>::kBf16, kBM, kBN, false, false);
       const uint32_t idesc_pv = umma_idesc_f16(Elem<T>::kBf16, kBM, kHD, false, true);
       const uint32_t q_addr = smem_u32(smem + kOffQ);
-      const uint32_t p_addr = smem_u32(smem + kOffP);
       auto issue_pv = [&](int jj) -> bool {
-        if (!mbar_wait(&bars->p_ready, jj & 1)) return false;
+        if (!mbar_wait(&bars->p_ready[jj & 1], (jj >> 1) & 1)) return false;
         tc_fence_after();
+        const uint32_t p_addr = smem_u32(smem + kOffP + (jj & 1) * kTile);
         const uint32_t v_addr = smem_u32(smem + kOffV + (jj & 1) * kTile);
 #pragma unroll
         for (int kk = 0; kk < kBN / 16; ++kk) {
@@ -275,7 +257,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint64_t bd = umma_desc_sw128(v_addr + kk * 2048, kAtom, 1024);
           umma_f16_ss(tmem + 256, ad, bd, idesc_pv, (jj > 0 || kk > 0) ? 1u : 0u);
         }
-        umma_commit(&bars->pv_done);
+        umma_commit(&bars->pv_done[jj & 1]);
         umma_commit(&bars->kv_empty[jj & 1]);
         return true;
       };
@@ -283,7 +265,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       for (int j = 0; j < n_tiles && ok; ++j) {
         const int st = j & 1;
-        if (!mbar_wait(&bars->k_rot[st], (j >> 1) & 1) ||
+        if (!mbar_wait(&bars->kv_full[st], (j >> 1) & 1) ||
             (j >= 2 && !mbar_wait(&bars->s_free[st], ((j >> 1) - 1) & 1))) {
           ok = false;
           break;
@@ -311,7 +293,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int kmax_row = !live ? 0 : (p.causal ? min(seq_len, pos + 1) : seq_len);
     const uint32_t lane_addr = tmem + (static_cast<uint32_t>(warp * 32) << 16);
     float m_ref = -INFINITY, l = 0.f;
-    uint8_t* pt = smem + kOffP;
     bool ok = true;
     for (int j = 0; j < n_tiles; ++j) {
       const int sb = j & 1;
@@ -335,14 +316,22 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       const bool grow = mx > m_ref + kRescaleLog2 || (m_ref == -INFINITY && mx != -INFINITY);
       const float m_new = grow ? mx : m_ref;
-      const float factor = (grow && m_ref != -INFINITY) ? exp2f(m_ref - m_new) : 1.f;
-      // P_j reuses the single P tile and O may be rescaled: PV_{j-1} must be done.
-      if (j >= 1 && !__all_sync(0xffffffffu, mbar_wait(&bars->pv_done, (j - 1) & 1))) {
+      const float factor = (grow && m_ref != -INFINITY) ? fast_exp2(m_ref - m_new) : 1.f;
+      // P_j goes to buffer j % 2, last read by PV_{j-2}; O may only be rescaled
+      // once PV_{j-1} is done.
+      if (j >= 2 &&
+          !__all_sync(0xffffffffu, mbar_wait(&bars->pv_done[sb], ((j >> 1) - 1) & 1))) {
+        ok = false;
+        break;
+      }
+      const bool rescale = j >= 1 && __any_sync(0xffffffffu, factor != 1.f);
+      if (rescale &&
+          !__all_sync(0xffffffffu, mbar_wait(&bars->pv_done[sb ^ 1], ((j - 1) >> 1) & 1))) {
         ok = false;
         break;
       }
       tc_fence_after();
-      if (j >= 1 && __any_sync(0xffffffffu, factor != 1.f)) {
+      if (rescale) {
 #pragma unroll
         for (int c4 = 0; c4 < 4; ++c4) {
           uint32_t raw[32];
@@ -369,7 +358,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int e = 0; e < 8; ++e) {
             const int c = c4 * 32 + q8 * 8 + e;
-            pv[e] = base_key + c < kmax_row ? exp2f(__uint_as_float(raw[q8 * 8 + e]) - base) : 0.f;
+            pv[e] = base_key + c < kmax_row ? fast_exp2(__uint_as_float(raw[q8 * 8 + e]) - base) : 0.f;
             l += pv[e];
           }
           uint4 w;
@@ -378,18 +367,25 @@ __global__ void __launch_bounds__(kThreads, 1)
           w.z = Elem<T>::from2(pv[4], pv[5]);
           w.w = Elem<T>::from2(pv[6], pv[7]);
           const int c8 = c4 * 4 + q8;  // 8-key chunk index, 0..15
-          *reinterpret_cast<uint4*>(pt + (c8 >> 3) * kAtom + sw_off(r, c8 & 7)) = w;
+          *reinterpret_cast<uint4*>(smem + kOffP + sb * kTile + (c8 >> 3) * kAtom +
+                                    sw_off(r, c8 & 7)) = w;
         }
       }
       tc_fence_before();
       mbar_arrive(&bars->s_free[sb]);
       fence_proxy_async_smem();
       tc_fence_before();
-      mbar_arrive(&bars->p_ready);
+      mbar_arrive(&bars->p_ready[sb]);
     }
     if (!ok) fail(kStatusWaitTimeout);
+    // O is final once the last two PV steps (one per P buffer) are done.
+    if (ok && n_tiles >= 2 &&
+        !__all_sync(0xffffffffu,
+                    mbar_wait(&bars->pv_done[(n_tiles - 2) & 1], ((n_tiles - 2) >> 1) & 1)))
+      ok = false;
     if (ok && n_tiles > 0 &&
-        __all_sync(0xffffffffu, mbar_wait(&bars->pv_done, (n_tiles - 1) & 1))) {
+        __all_sync(0xffffffffu,
+                   mbar_wait(&bars->pv_done[(n_tiles - 1) & 1], ((n_tiles - 1) >> 1) & 1))) {
       tc_fence_after();
       const float inv = l > 0.f ? 1.f / l : 0.f;
       T* orow = static_cast<T*>(p.out) +
@@ -446,12 +442,14 @@ EncodeTiledFn prefill_encode_fn() {
   return fn;
 }
 
-bool kv_map(CUtensorMap* m, const void* base, CUtensorMapDataType dt, uint64_t rows) {
+// Row-major [rows, 128] bf16/fp16 tensor, 128-byte-swizzled boxes of box_rows x 64 columns.
+bool kv_map(CUtensorMap* m, const void* base, CUtensorMapDataType dt, uint64_t rows,
+            uint32_t box_rows) {
   EncodeTiledFn enc = prefill_encode_fn();
   if (enc == nullptr) return false;
   cuuint64_t dims[2] = {static_cast<cuuint64_t>(kHD), rows};
   cuuint64_t strides[1] = {kHD * 2};
-  cuuint32_t box[2] = {64, 64};
+  cuuint32_t box[2] = {64, box_rows};
   cuuint32_t estr[2] = {1, 1};
   std::memset(m, 0, sizeof(*m));
   return enc(m, dt, 2, const_cast<void*>(base), dims, strides, box, estr,
@@ -471,31 +469,42 @@ bool prefill_tc_supported(const RowsParams& p, int dtype) {
       !aligned(p.sin))
     return false;
   if (static_cast<int64_t>(p.n_phys) * p.Hkv * kBlock >= (int64_t(1) << 31)) return false;
+  if (static_cast<int64_t>(p.S) * p.Hkv * p.max_blocks * kBlock >= (int64_t(1) << 31)) return false;
   return prefill_encode_fn() != nullptr;
+}
+
+int64_t prefill_workspace_bytes(const RowsParams& p) {
+  return static_cast<int64_t>(p.S) * p.Hkv * p.max_blocks * kBlock * kHD * 2;
 }
 
 cudaError_t launch_prefill_tc(const RowsParams& p, int dtype, cudaStream_t stream) {
   if (!prefill_tc_supported(p, dtype)) return cudaErrorNotSupported;
   if (p.S == 0 || p.Lq == 0) return cudaSuccess;
+  if (p.workspace == nullptr || p.workspace_bytes < prefill_workspace_bytes(p) ||
+      (reinterpret_cast<uintptr_t>(p.workspace) & 15u) != 0)
+    return cudaErrorInvalidValue;
   const CUtensorMapDataType dt =
       dtype == 2 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  const int32_t rows_per_head = p.max_blocks * kBlock;
   CUtensorMap mk, mv;
-  const uint64_t rows = static_cast<uint64_t>(p.n_phys) * p.Hkv * kBlock;
-  if (!kv_map(&mk, p.k, dt, rows) || !kv_map(&mv, p.v, dt, rows)) return cudaErrorInvalidValue;
+  const uint64_t v_rows = static_cast<uint64_t>(p.n_phys) * p.Hkv * kBlock;
+  const uint64_t k_rows = static_cast<uint64_t>(p.S) * p.Hkv * rows_per_head;
+  if (!kv_map(&mk, p.workspace, dt, k_rows, kBN) || !kv_map(&mv, p.v, dt, v_rows, kBlock))
+    return cudaErrorInvalidValue;
+  cudaError_t e = launch_rope_k(p, dtype, p.workspace, p.max_blocks, stream);
+  if (e != cudaSuccess) return e;
   const int ppt = kBM / p.G;
   dim3 grid((p.Lq + ppt - 1) / ppt, p.Hkv, p.S);
   if (dtype == 2) {
     auto kernel = prefill_tc_kernel<__nv_bfloat16>;
-    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         kSmemBytes);
+    e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
     if (e != cudaSuccess) return e;
-    kernel<<<grid, kThreads, kSmemBytes, stream>>>(mk, mv, p);
+    kernel<<<grid, kThreads, kSmemBytes, stream>>>(mk, mv, p, rows_per_head);
   } else {
     auto kernel = prefill_tc_kernel<__half>;
-    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         kSmemBytes);
+    e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
     if (e != cudaSuccess) return e;
-    kernel<<<grid, kThreads, kSmemBytes, stream>>>(mk, mv, p);
+    kernel<<<grid, kThreads, kSmemBytes, stream>>>(mk, mv, p, rows_per_head);
   }
   return cudaGetLastError();
 }

@@ -28,11 +28,19 @@ struct RowsParams {
   int32_t max_blocks, n_phys, max_pos;
   int32_t causal;
   float scale_log2;
+  void* workspace;            // tensor-core path: rotated-key scratch (prefill_workspace_bytes)
+  int64_t workspace_bytes;
 };
 
 cudaError_t launch_attend_rows_simt(const RowsParams& p, int dtype, cudaStream_t stream);
 // tcgen05 chunked prefill: dense fp16/bf16 queries, head_dim 128, no bias / block mask.
 bool prefill_tc_supported(const RowsParams& p, int dtype);
+// Scratch for the rotated keys: S * Hkv * max_blocks * 64 * D elements.
+int64_t prefill_workspace_bytes(const RowsParams& p);
 cudaError_t launch_prefill_tc(const RowsParams& p, int dtype, cudaStream_t stream);
+// Writes RoPE-rotated keys of every block below seq_len into `krot`
+// ([S, Hkv, blocks_per_seq * 64, 128], the cache dtype).
+cudaError_t launch_rope_k(const RowsParams& p, int dtype, void* krot, int32_t blocks_per_seq,
+                          cudaStream_t stream);
 
 }  // namespace ouro

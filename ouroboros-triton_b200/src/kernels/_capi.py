@@ -53,10 +53,14 @@ class AttentionArgs(ctypes.Structure):
         ("q_len", _i32), ("max_blocks", _i32), ("num_phys_blocks", _i32),
         ("max_positions", _i32), ("dtype", _i32), ("causal", _i32), ("kernel", _i32),
         ("softmax_scale", ctypes.c_float),
+        ("workspace", _vp), ("workspace_bytes", ctypes.c_size_t),
     ]
 
 
 _native.register("ouro_paged_attention", ctypes.c_int, [ctypes.POINTER(AttentionArgs), _vp])
+_native.register("ouro_attention_plan", ctypes.c_int,
+                 [ctypes.POINTER(AttentionArgs), ctypes.POINTER(ctypes.c_size_t),
+                  ctypes.POINTER(_i32)])
 _native.register("ouro_kv_append", ctypes.c_int,
                  [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _i32, _i32,
                   _vp, _vp])

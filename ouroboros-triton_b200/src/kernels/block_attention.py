@@ -497,6 +497,68 @@ def block_attention(page_table, q_cache, k_cache, v_cache, seq_lens, cos, sin, b
     return out
 
 
+class PrefillCall:
+    """A prepared chunked-prefill launch (checked once, then :meth:`launch` only enqueues)."""
+
+    def __init__(self, page_table, q, k_cache, v_cache, q_start, seq_lens, cos, sin, *,
+                 causal: bool = True, softmax_scale=None, out=None, validate: bool = True,
+                 kernel: str = "auto", status=None):
+        _require_cuda()
+        if kernel not in _KERNELS:
+            raise RuntimeError(f"kernel must be one of {sorted(_KERNELS)}, got {kernel!r}")
+        device = _device_of(k_cache, q, page_table)
+        k_cache, v_cache = _on(k_cache, device), _on(v_cache, device)
+        n_phys, Hkv, blk, D = k_cache.shape
+        if blk != BLOCK_SIZE:
+            raise RuntimeError(f"k_cache block dim must be {BLOCK_SIZE}, got {blk}")
+        if v_cache.shape != k_cache.shape or v_cache.dtype != k_cache.dtype:
+            raise RuntimeError("k/v caches must share the [n_phys, Hkv, 64, D] layout and dtype")
+        q = _on(q, device, k_cache.dtype)
+        if q.dim() != 4 or q.shape[3] != D:
+            raise RuntimeError(f"q must be [S, Hq, L, {D}], got {tuple(q.shape)}")
+        S, Hq, L = q.shape[0], q.shape[1], q.shape[2]
+        if Hq % Hkv != 0:
+            raise RuntimeError(f"query heads {Hq} must be a multiple of KV heads {Hkv}")
+        pt = _as_int32(_on(page_table, device), "page_table")
+        if pt.dim() != 2 or pt.shape[0] != S:
+            raise RuntimeError(f"page_table must be [S={S}, max_blocks]")
+        lens = _as_int32(_on(seq_lens, device), "seq_lens")
+        starts = _as_int32(_on(q_start, device), "q_start")
+        if tuple(lens.shape) != (S,) or tuple(starts.shape) != (S,):
+            raise RuntimeError(f"seq_lens and q_start must have shape [{S}]")
+        cos, sin = _on(cos, device, torch.float32), _on(sin, device, torch.float32)
+        if cos.dim() != 2 or cos.shape != sin.shape or cos.shape[1] != D // 2:
+            raise RuntimeError(f"rope tables must be [max_positions, {D // 2}]")
+        if cos.shape[0] < pt.shape[1] * BLOCK_SIZE:
+            raise RuntimeError(
+                f"rope tables must cover {pt.shape[1] * BLOCK_SIZE} positions, got {cos.shape[0]}")
+        if validate:
+            validate_page_table(pt, lens, n_phys)
+        if out is None:
+            out = torch.zeros((S, Hq, L, D), dtype=k_cache.dtype, device=device)
+        elif out.shape != (S, Hq, L, D) or out.dtype != k_cache.dtype or not out.is_contiguous():
+            raise RuntimeError(f"out must be a contiguous [S, Hq, L, D] {k_cache.dtype} tensor")
+        self.out = out
+        self.device = device
+        self.args = _rows_args(q, False, k_cache, v_cache, pt, lens, starts, cos, sin, None, None,
+                               out, status, Hq, L, causal, softmax_scale, kernel)
+        need, tc = ctypes.c_size_t(), ctypes.c_int32()
+        _native.check(_native.lib().ouro_attention_plan(ctypes.byref(self.args),
+                                                        ctypes.byref(need), ctypes.byref(tc)),
+                      "attention plan")
+        self.tensor_cores = bool(tc.value)
+        self.workspace = None
+        if need.value:  # rotated-key scratch of the tensor-core path
+            self.workspace = torch.empty(need.value, dtype=torch.uint8, device=device)
+            self.args.workspace = _ptr(self.workspace)
+            self.args.workspace_bytes = need.value
+        self._keep = (q, k_cache, v_cache, pt, lens, starts, cos, sin, status)
+
+    def launch(self):
+        _launch_rows(self.args, self.device)
+        return self.out
+
+
 def chunked_prefill_attention(page_table, q, k_cache, v_cache, q_start, seq_lens, cos, sin, *,
                               causal: bool = True, softmax_scale=None, out=None,
                               validate: bool = True, kernel: str = "auto", status=None):
@@ -505,47 +567,12 @@ def chunked_prefill_attention(page_table, q, k_cache, v_cache, q_start, seq_lens
     Keys are every paged token j < seq_lens[s] (the chunk's own K/V already
     written into the cache), j <= q_start[s] + i when ``causal``. Query head h
     reads KV head h // (Hq / Hkv). Rows whose position is >= seq_lens[s] stay
-    zero. Returns [S, Hq, L, D] in the cache dtype.
+    zero. fp16/bf16 with head_dim 128 run on the tcgen05 tensor-core kernel;
+    other shapes and fp32 on CUDA cores. Returns [S, Hq, L, D] in the cache dtype.
     """
-    _require_cuda()
-    if kernel not in _KERNELS:
-        raise RuntimeError(f"kernel must be one of {sorted(_KERNELS)}, got {kernel!r}")
-    device = _device_of(k_cache, q, page_table)
-    k_cache, v_cache = _on(k_cache, device), _on(v_cache, device)
-    n_phys, Hkv, blk, D = k_cache.shape
-    if blk != BLOCK_SIZE:
-        raise RuntimeError(f"k_cache block dim must be {BLOCK_SIZE}, got {blk}")
-    if v_cache.shape != k_cache.shape or v_cache.dtype != k_cache.dtype:
-        raise RuntimeError("k/v caches must share the [n_phys, Hkv, 64, D] layout and dtype")
-    q = _on(q, device, k_cache.dtype)
-    if q.dim() != 4 or q.shape[3] != D:
-        raise RuntimeError(f"q must be [S, Hq, L, {D}], got {tuple(q.shape)}")
-    S, Hq, L = q.shape[0], q.shape[1], q.shape[2]
-    if Hq % Hkv != 0:
-        raise RuntimeError(f"query heads {Hq} must be a multiple of KV heads {Hkv}")
-    pt = _as_int32(_on(page_table, device), "page_table")
-    if pt.dim() != 2 or pt.shape[0] != S:
-        raise RuntimeError(f"page_table must be [S={S}, max_blocks]")
-    lens = _as_int32(_on(seq_lens, device), "seq_lens")
-    starts = _as_int32(_on(q_start, device), "q_start")
-    if tuple(lens.shape) != (S,) or tuple(starts.shape) != (S,):
-        raise RuntimeError(f"seq_lens and q_start must have shape [{S}]")
-    cos, sin = _on(cos, device, torch.float32), _on(sin, device, torch.float32)
-    if cos.dim() != 2 or cos.shape != sin.shape or cos.shape[1] != D // 2:
-        raise RuntimeError(f"rope tables must be [max_positions, {D // 2}]")
-    if cos.shape[0] < pt.shape[1] * BLOCK_SIZE:
-        raise RuntimeError(
-            f"rope tables must cover {pt.shape[1] * BLOCK_SIZE} positions, got {cos.shape[0]}")
-    if validate:
-        validate_page_table(pt, lens, n_phys)
-    if out is None:
-        out = torch.zeros((S, Hq, L, D), dtype=k_cache.dtype, device=device)
-    elif out.shape != (S, Hq, L, D) or out.dtype != k_cache.dtype or not out.is_contiguous():
-        raise RuntimeError(f"out must be a contiguous [S, Hq, L, D] {k_cache.dtype} tensor")
-    args = _rows_args(q, False, k_cache, v_cache, pt, lens, starts, cos, sin, None, None, out,
-                      status, Hq, L, causal, softmax_scale, kernel)
-    _launch_rows(args, device)
-    return out
+    return PrefillCall(page_table, q, k_cache, v_cache, q_start, seq_lens, cos, sin,
+                       causal=causal, softmax_scale=softmax_scale, out=out, validate=validate,
+                       kernel=kernel, status=status).launch()
 
 
 def paged_kv_append(k_new, v_new, page_table, start, counts, k_cache, v_cache, *, status=None):
