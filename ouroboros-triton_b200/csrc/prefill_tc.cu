@@ -6,17 +6,17 @@
 // position q_start + tile * PPT + r % PPT), so every K/V tile feeds G heads.
 // The CTA walks 128-key tiles (two 64-token blocks resolved through the page
 // table) up to its causal limit:
-//   warp 8      TMA producer: K and V tiles into a 2-stage ring (128-byte
+//   warp 4      TMA producer: K and V tiles into a 2-stage ring (128-byte
 //               swizzle, layout [64-column atom][128 keys][128 B]); K comes
 //               already rotated from the dense scratch written by rope_k.cu
 //               (one box of 128 keys per atom), V from the paged cache
 //               (boxes of 64 keys, one per block)
-//   warps 4-7   RoPE on the query tile (from global, scaled by
-//               softmax_scale * log2 e), once per CTA
-//   warp 9      TMEM owner and MMA issuer: S_j = Q K_j^T into one of two
+//   warp 5      TMEM owner and MMA issuer: S_j = Q K_j^T into one of two
 //               128-column TMEM buffers, then O += P_{j-1} V_{j-1}
 //               (V as an MN-major operand), tcgen05.commit to mbarriers
-//   warps 0-3   softmax, one query row per thread (TMEM lane): S_j from TMEM,
+//   warps 0-3   RoPE on the query tile (each thread its own row, scaled by
+//               softmax_scale * log2 e), then softmax, one query row per
+//               thread (TMEM lane): S_j from TMEM in one pass,
 //               causal / length masks, running max with lazy rescaling of O
 //               (only when the max grows by more than 2^8), P_j as bf16/fp16
 //               into a swizzled shared tile, and the final O / l epilogue.
@@ -42,7 +42,7 @@ constexpr int kBM = 128;          // query rows per CTA
 constexpr int kBN = 128;          // keys per tile
 constexpr int kAtom = 128 * 128;  // one 64-column atom of a 128-row tile (bytes)
 constexpr int kTile = 2 * kAtom;  // 128 rows x 128 columns x 2 bytes
-constexpr int kThreads = 320;
+constexpr int kThreads = 192;  // warps 0-3 softmax (+ Q RoPE), 4 TMA, 5 MMA / TMEM
 constexpr float kRescaleLog2 = 8.0f;
 
 // Shared-memory map (offsets from a 1024-byte aligned base).
@@ -158,7 +158,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(&bars->q_ready, 128);
     fence_barrier_init();
   }
-  if (warp == 9) {
+  if (warp == 5) {
     tmem_alloc(&bars->tmem_base, 512);
     tmem_relinquish();
   }
@@ -172,7 +172,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     *s_abort = 1;
   };
 
-  if (warp == 8) {
+  if (warp == 4) {
     // ------------------------------ TMA producer ------------------------------
     if (lane == 0) {
       tma_prefetch_desc(&tm_k);
@@ -207,39 +207,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
-  } else if (warp >= 4 && warp < 8) {
-    // ------------------------------ RoPE warps ------------------------------
-    const int r = threadIdx.x - 128;  // row of the Q tile / key row of a K tile
-    const int half = kHD / 2;
-    {
-      // Query row r: head kvh*G + r / ppt at position q0 + r % ppt.
-      const int hl = r / ppt, i = r % ppt;
-      const int pos = q0 + i;
-      const bool live = i < rows_valid;
-      const T* qrow = static_cast<const T*>(p.q) +
-                      ((static_cast<int64_t>(s) * p.Hq + kvh * G + hl) * p.Lq + qt * ppt + i) * kHD;
-      uint8_t* qs = smem + kOffQ;
-      for (int c = 0; c < 8; ++c) {
-        uint4 lo = make_uint4(0, 0, 0, 0), hi = lo;
-        float cs[8], sn[8];
-        if (live) {
-          lo = *reinterpret_cast<const uint4*>(qrow + 8 * c);
-          hi = *reinterpret_cast<const uint4*>(qrow + half + 8 * c);
-          const bool pos_ok = pos < p.max_pos;
-#pragma unroll
-          for (int e = 0; e < 8; ++e) {
-            cs[e] = pos_ok ? p.cos[static_cast<int64_t>(pos) * half + 8 * c + e] : 1.f;
-            sn[e] = pos_ok ? p.sin[static_cast<int64_t>(pos) * half + 8 * c + e] : 0.f;
-          }
-          rope8<T>(lo, hi, cs, sn, p.scale_log2);
-        }
-        *reinterpret_cast<uint4*>(qs + sw_off(r, c)) = lo;
-        *reinterpret_cast<uint4*>(qs + kAtom + sw_off(r, c)) = hi;
-      }
-      fence_proxy_async_smem();
-      mbar_arrive(&bars->q_ready);
-    }
-  } else if (warp == 9) {
+  } else if (warp == 5) {
     // ------------------------------ MMA issuer ------------------------------
     if (lane == 0) {
       const uint32_t idesc_s = umma_idesc_f16(Elem<T>::kBf16, kBM, kBN, false, false);
@@ -290,6 +258,33 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int hl = r / ppt, i = r % ppt;
     const bool live = i < rows_valid;
     const int pos = q0 + i;
+    {
+      // Query row r (head kvh*G + r / ppt, position q0 + r % ppt), rotated and
+      // scaled by softmax_scale * log2(e), into the swizzled Q tile.
+      const int half = kHD / 2;
+      const T* qrow = static_cast<const T*>(p.q) +
+                      ((static_cast<int64_t>(s) * p.Hq + kvh * G + hl) * p.Lq + qt * ppt + i) * kHD;
+      uint8_t* qs = smem + kOffQ;
+      const bool pos_ok = pos < p.max_pos;
+      for (int c = 0; c < 8; ++c) {
+        uint4 lo = make_uint4(0, 0, 0, 0), hi = lo;
+        if (live) {
+          lo = *reinterpret_cast<const uint4*>(qrow + 8 * c);
+          hi = *reinterpret_cast<const uint4*>(qrow + half + 8 * c);
+          float cs[8], sn[8];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            cs[e] = pos_ok ? p.cos[static_cast<int64_t>(pos) * half + 8 * c + e] : 1.f;
+            sn[e] = pos_ok ? p.sin[static_cast<int64_t>(pos) * half + 8 * c + e] : 0.f;
+          }
+          rope8<T>(lo, hi, cs, sn, p.scale_log2);
+        }
+        *reinterpret_cast<uint4*>(qs + sw_off(r, c)) = lo;
+        *reinterpret_cast<uint4*>(qs + kAtom + sw_off(r, c)) = hi;
+      }
+      fence_proxy_async_smem();
+      mbar_arrive(&bars->q_ready);
+    }
     const int kmax_row = !live ? 0 : (p.causal ? min(seq_len, pos + 1) : seq_len);
     const uint32_t lane_addr = tmem + (static_cast<uint32_t>(warp * 32) << 16);
     float m_ref = -INFINITY, l = 0.f;
@@ -302,17 +297,32 @@ __global__ void __launch_bounds__(kThreads, 1)
         break;
       }
       tc_fence_after();
+      // One pass over TMEM: the whole 128-key score row into registers.
+      uint32_t sr[4][32];
+#pragma unroll
+      for (int c4 = 0; c4 < 4; ++c4) tmem_ld32(lane_addr + sb * 128 + c4 * 32, sr[c4]);
+      tmem_wait_ld();
+      tc_fence_before();
+      mbar_arrive(&bars->s_free[sb]);  // the S buffer can take S_{j+2} already
+
       const int base_key = j * kBN;
-      // Pass 1: row max over the keys this row may see.
+      // Tiles that lie wholly below every row's key limit skip the per-key masks.
+      const bool full = __all_sync(0xffffffffu, base_key + kBN <= kmax_row);
       float mx = -INFINITY;
+      if (full) {
 #pragma unroll
-      for (int c4 = 0; c4 < 4; ++c4) {
-        uint32_t raw[32];
-        tmem_ld32(lane_addr + sb * 128 + c4 * 32, raw);
-        tmem_wait_ld();
+        for (int c4 = 0; c4 < 4; ++c4)
 #pragma unroll
-        for (int e = 0; e < 32; ++e)
-          if (base_key + c4 * 32 + e < kmax_row) mx = fmaxf(mx, __uint_as_float(raw[e]));
+          for (int e = 0; e < 32; ++e) mx = fmaxf(mx, __uint_as_float(sr[c4][e]));
+      } else {
+#pragma unroll
+        for (int c4 = 0; c4 < 4; ++c4)
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            const bool ok_key = base_key + c4 * 32 + e < kmax_row;
+            if (!ok_key) sr[c4][e] = __float_as_uint(-INFINITY);
+            mx = fmaxf(mx, __uint_as_float(sr[c4][e]));
+          }
       }
       const bool grow = mx > m_ref + kRescaleLog2 || (m_ref == -INFINITY && mx != -INFINITY);
       const float m_new = grow ? mx : m_ref;
@@ -346,33 +356,23 @@ __global__ void __launch_bounds__(kThreads, 1)
       l *= factor;
       m_ref = m_new;
       const float base = m_ref == -INFINITY ? 0.f : m_ref;
-      // Pass 2: P = exp2(S - max) into the swizzled P tile, 32 keys at a time.
+      // P = exp2(S - max): masked keys hold -inf and give exactly 0.
+      uint8_t* pbuf = smem + kOffP + sb * kTile;
 #pragma unroll
-      for (int c4 = 0; c4 < 4; ++c4) {
-        uint32_t raw[32];
-        tmem_ld32(lane_addr + sb * 128 + c4 * 32, raw);
-        tmem_wait_ld();
+      for (int c8 = 0; c8 < 16; ++c8) {
+        float pv[8];
 #pragma unroll
-        for (int q8 = 0; q8 < 4; ++q8) {
-          float pv[8];
-#pragma unroll
-          for (int e = 0; e < 8; ++e) {
-            const int c = c4 * 32 + q8 * 8 + e;
-            pv[e] = base_key + c < kmax_row ? fast_exp2(__uint_as_float(raw[q8 * 8 + e]) - base) : 0.f;
-            l += pv[e];
-          }
-          uint4 w;
-          w.x = Elem<T>::from2(pv[0], pv[1]);
-          w.y = Elem<T>::from2(pv[2], pv[3]);
-          w.z = Elem<T>::from2(pv[4], pv[5]);
-          w.w = Elem<T>::from2(pv[6], pv[7]);
-          const int c8 = c4 * 4 + q8;  // 8-key chunk index, 0..15
-          *reinterpret_cast<uint4*>(smem + kOffP + sb * kTile + (c8 >> 3) * kAtom +
-                                    sw_off(r, c8 & 7)) = w;
+        for (int e = 0; e < 8; ++e) {
+          pv[e] = fast_exp2(__uint_as_float(sr[c8 >> 2][(c8 & 3) * 8 + e]) - base);
+          l += pv[e];
         }
+        uint4 w;
+        w.x = Elem<T>::from2(pv[0], pv[1]);
+        w.y = Elem<T>::from2(pv[2], pv[3]);
+        w.z = Elem<T>::from2(pv[4], pv[5]);
+        w.w = Elem<T>::from2(pv[6], pv[7]);
+        *reinterpret_cast<uint4*>(pbuf + (c8 >> 3) * kAtom + sw_off(r, c8 & 7)) = w;
       }
-      tc_fence_before();
-      mbar_arrive(&bars->s_free[sb]);
       fence_proxy_async_smem();
       tc_fence_before();
       mbar_arrive(&bars->p_ready[sb]);
@@ -418,7 +418,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 9) {
+  if (warp == 5) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
