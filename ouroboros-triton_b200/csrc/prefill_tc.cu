@@ -6,11 +6,12 @@
 // position q_start + tile * PPT + r % PPT), so every K/V tile feeds G heads.
 // The CTA walks 128-key tiles (two 64-token blocks resolved through the page
 // table) up to its causal limit:
-//   warp 4      TMA producer: K and V tiles into a 2-stage ring (128-byte
-//               swizzle, layout [64-column atom][128 keys][128 B]); K comes
-//               already rotated from the dense scratch written by rope_k.cu
-//               (one box of 128 keys per atom), V from the paged cache
-//               (boxes of 64 keys, one per block)
+//   warps 4, 6  TMA producers for two separate 2-stage rings (128-byte
+//               swizzle, layout [64-column atom][128 keys][128 B]): K tiles,
+//               already rotated, from the dense scratch written by rope_k.cu
+//               (one box of 128 keys per atom), refilled as soon as S_j is
+//               done; V tiles from the paged cache (boxes of 64 keys, one per
+//               block), refilled when PV_j is done
 //   warp 5      TMEM owner and MMA issuer: S_j = Q K_j^T into one of two
 //               128-column TMEM buffers, then O += P_{j-1} V_{j-1}
 //               (V as an MN-major operand), tcgen05.commit to mbarriers
@@ -42,7 +43,7 @@ constexpr int kBM = 128;          // query rows per CTA
 constexpr int kBN = 128;          // keys per tile
 constexpr int kAtom = 128 * 128;  // one 64-column atom of a 128-row tile (bytes)
 constexpr int kTile = 2 * kAtom;  // 128 rows x 128 columns x 2 bytes
-constexpr int kThreads = 192;  // warps 0-3 softmax (+ Q RoPE), 4 TMA, 5 MMA / TMEM
+constexpr int kThreads = 224;  // warps 0-3 softmax (+ Q RoPE), 4 K loads, 5 MMA / TMEM, 6 V loads
 constexpr float kRescaleLog2 = 8.0f;
 
 // Shared-memory map (offsets from a 1024-byte aligned base).
@@ -58,7 +59,8 @@ constexpr int kSmemBytes = kOffBar + 256 + 1024;
 // keep each waiter within that window (a shared PV barrier could run two
 // phases ahead once P is double-buffered).
 struct Bars {
-  uint64_t kv_full[2], kv_empty[2], s_full[2], s_free[2], p_ready[2], pv_done[2];
+  uint64_t k_full[2], k_empty[2], v_full[2], v_empty[2], s_full[2], s_free[2], p_ready[2],
+      pv_done[2];
   uint64_t q_ready;
   uint32_t tmem_base;
 };
@@ -148,8 +150,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0) {
     *s_abort = 0;
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&bars->kv_full[i], 1);
-      mbar_init(&bars->kv_empty[i], 1);
+      mbar_init(&bars->k_full[i], 1);
+      mbar_init(&bars->k_empty[i], 1);
+      mbar_init(&bars->v_full[i], 1);
+      mbar_init(&bars->v_empty[i], 1);
       mbar_init(&bars->s_full[i], 1);
       mbar_init(&bars->s_free[i], 128);
       mbar_init(&bars->p_ready[i], 128);
@@ -172,38 +176,41 @@ __global__ void __launch_bounds__(kThreads, 1)
     *s_abort = 1;
   };
 
-  if (warp == 4) {
-    // ------------------------------ TMA producer ------------------------------
+  if (warp == 4 || warp == 6) {
+    // --------------------------- TMA producers (K: warp 4, V: warp 6) ---------------------------
     if (lane == 0) {
-      tma_prefetch_desc(&tm_k);
-      tma_prefetch_desc(&tm_v);
-      const uint64_t pol = policy_evict_last();  // K/V tiles are re-read by other CTAs
+      const bool is_k = warp == 4;
+      tma_prefetch_desc(is_k ? &tm_k : &tm_v);
+      const uint64_t pol = policy_evict_last();  // tiles are re-read by other CTAs
       const int32_t* row = p.page_table + static_cast<int64_t>(s) * p.max_blocks;
+      uint64_t* full = is_k ? bars->k_full : bars->v_full;
+      uint64_t* empty = is_k ? bars->k_empty : bars->v_empty;
+      uint8_t* ring = smem + (is_k ? kOffK : kOffV);
       for (int j = 0; j < n_tiles && !*s_abort; ++j) {
         const int st = j & 1;
-        if (j >= 2 && !mbar_wait(&bars->kv_empty[st], ((j >> 1) - 1) & 1)) {
+        if (j >= 2 && !mbar_wait(&empty[st], ((j >> 1) - 1) & 1)) {
           fail(kStatusWaitTimeout);
           break;
         }
-        mbar_arrive_expect_tx(&bars->kv_full[st], 2 * kTile);
-        uint8_t* kd = smem + kOffK + st * kTile;
-        uint8_t* vd = smem + kOffV + st * kTile;
-        // rotated keys: rows (s, kvh, 128 j .. 128 j + 127) of the scratch
-        const int ky = (s * p.Hkv + kvh) * krot_rows_per_head + j * kBN;
-        for (int a = 0; a < 2; ++a)
-          tma_load_2d(kd + a * kAtom, &tm_k, a * 64, ky, &bars->kv_full[st], pol);
-        for (int blk = 0; blk < 2; ++blk) {
-          const int b = 2 * j + blk;
-          const int lb = b < nb ? b : 2 * j;  // a block past the keys repeats a valid one
-          int phys = lb < p.max_blocks ? row[lb] : -1;
-          if (phys < 0 || phys >= p.n_phys) {
-            if (p.status) atomicOr(p.status, kStatusBadPageEntry);
-            phys = 0;
+        mbar_arrive_expect_tx(&full[st], kTile);
+        uint8_t* dst = ring + st * kTile;
+        if (is_k) {
+          // rotated keys: rows (s, kvh, 128 j .. 128 j + 127) of the scratch
+          const int ky = (s * p.Hkv + kvh) * krot_rows_per_head + j * kBN;
+          for (int a = 0; a < 2; ++a) tma_load_2d(dst + a * kAtom, &tm_k, a * 64, ky, &full[st], pol);
+        } else {
+          for (int blk = 0; blk < 2; ++blk) {
+            const int b = 2 * j + blk;
+            const int lb = b < nb ? b : 2 * j;  // a block past the keys repeats a valid one
+            int phys = lb < p.max_blocks ? row[lb] : -1;
+            if (phys < 0 || phys >= p.n_phys) {
+              if (p.status) atomicOr(p.status, kStatusBadPageEntry);
+              phys = 0;
+            }
+            const int y = (phys * p.Hkv + kvh) * kBlock;
+            for (int a = 0; a < 2; ++a)
+              tma_load_2d(dst + a * kAtom + blk * (kAtom / 2), &tm_v, a * 64, y, &full[st], pol);
           }
-          const int y = (phys * p.Hkv + kvh) * kBlock;
-          for (int a = 0; a < 2; ++a)
-            tma_load_2d(vd + a * kAtom + blk * (kAtom / 2), &tm_v, a * 64, y, &bars->kv_full[st],
-                        pol);
         }
       }
     }
@@ -214,7 +221,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t idesc_pv = umma_idesc_f16(Elem<T>::kBf16, kBM, kHD, false, true);
       const uint32_t q_addr = smem_u32(smem + kOffQ);
       auto issue_pv = [&](int jj) -> bool {
-        if (!mbar_wait(&bars->p_ready[jj & 1], (jj >> 1) & 1)) return false;
+        if (!mbar_wait(&bars->p_ready[jj & 1], (jj >> 1) & 1) ||
+            !mbar_wait(&bars->v_full[jj & 1], (jj >> 1) & 1))
+          return false;
         tc_fence_after();
         const uint32_t p_addr = smem_u32(smem + kOffP + (jj & 1) * kTile);
         const uint32_t v_addr = smem_u32(smem + kOffV + (jj & 1) * kTile);
@@ -226,14 +235,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           umma_f16_ss(tmem + 256, ad, bd, idesc_pv, (jj > 0 || kk > 0) ? 1u : 0u);
         }
         umma_commit(&bars->pv_done[jj & 1]);
-        umma_commit(&bars->kv_empty[jj & 1]);
+        umma_commit(&bars->v_empty[jj & 1]);
         return true;
       };
       bool ok = mbar_wait(&bars->q_ready, 0);
       tc_fence_after();
       for (int j = 0; j < n_tiles && ok; ++j) {
         const int st = j & 1;
-        if (!mbar_wait(&bars->kv_full[st], (j >> 1) & 1) ||
+        if (!mbar_wait(&bars->k_full[st], (j >> 1) & 1) ||
             (j >= 2 && !mbar_wait(&bars->s_free[st], ((j >> 1) - 1) & 1))) {
           ok = false;
           break;
@@ -247,6 +256,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           umma_f16_ss(tmem + st * 128, ad, bd, idesc_s, kk > 0 ? 1u : 0u);
         }
         umma_commit(&bars->s_full[st]);
+        umma_commit(&bars->k_empty[st]);  // K_j is free as soon as S_j is done
         if (j >= 1 && !issue_pv(j - 1)) ok = false;
       }
       if (ok && n_tiles > 0) ok = issue_pv(n_tiles - 1);
