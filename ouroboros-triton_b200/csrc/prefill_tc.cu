@@ -318,22 +318,21 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int base_key = j * kBN;
       // Tiles that lie wholly below every row's key limit skip the per-key masks.
       const bool full = __all_sync(0xffffffffu, base_key + kBN <= kmax_row);
-      float mx = -INFINITY;
-      if (full) {
+      if (!full) {
 #pragma unroll
         for (int c4 = 0; c4 < 4; ++c4)
 #pragma unroll
-          for (int e = 0; e < 32; ++e) mx = fmaxf(mx, __uint_as_float(sr[c4][e]));
-      } else {
-#pragma unroll
-        for (int c4 = 0; c4 < 4; ++c4)
-#pragma unroll
-          for (int e = 0; e < 32; ++e) {
-            const bool ok_key = base_key + c4 * 32 + e < kmax_row;
-            if (!ok_key) sr[c4][e] = __float_as_uint(-INFINITY);
-            mx = fmaxf(mx, __uint_as_float(sr[c4][e]));
-          }
+          for (int e = 0; e < 32; ++e)
+            if (base_key + c4 * 32 + e >= kmax_row) sr[c4][e] = __float_as_uint(-INFINITY);
       }
+      // Row max with 8 independent partial maxima (short dependency chains).
+      float mp[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) mp[k] = __uint_as_float(sr[0][k]);
+#pragma unroll
+      for (int c = 8; c < kBN; ++c) mp[c & 7] = fmaxf(mp[c & 7], __uint_as_float(sr[c >> 5][c & 31]));
+      const float mx = fmaxf(fmaxf(fmaxf(mp[0], mp[1]), fmaxf(mp[2], mp[3])),
+                             fmaxf(fmaxf(mp[4], mp[5]), fmaxf(mp[6], mp[7])));
       const bool grow = mx > m_ref + kRescaleLog2 || (m_ref == -INFINITY && mx != -INFINITY);
       const float m_new = grow ? mx : m_ref;
       const float factor = (grow && m_ref != -INFINITY) ? fast_exp2(m_ref - m_new) : 1.f;
@@ -366,15 +365,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       l *= factor;
       m_ref = m_new;
       const float base = m_ref == -INFINITY ? 0.f : m_ref;
-      // P = exp2(S - max): masked keys hold -inf and give exactly 0.
+      // P = exp2(S - max): masked keys hold -inf and give exactly 0. The row sum
+      // uses 8 partial sums so the adds do not serialise behind each exp.
       uint8_t* pbuf = smem + kOffP + sb * kTile;
+      float lp[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int c8 = 0; c8 < 16; ++c8) {
         float pv[8];
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
           pv[e] = fast_exp2(__uint_as_float(sr[c8 >> 2][(c8 & 3) * 8 + e]) - base);
-          l += pv[e];
+          lp[e] += pv[e];
         }
         uint4 w;
         w.x = Elem<T>::from2(pv[0], pv[1]);
@@ -383,6 +384,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         w.w = Elem<T>::from2(pv[6], pv[7]);
         *reinterpret_cast<uint4*>(pbuf + (c8 >> 3) * kAtom + sw_off(r, c8 & 7)) = w;
       }
+      l += ((lp[0] + lp[1]) + (lp[2] + lp[3])) + ((lp[4] + lp[5]) + (lp[6] + lp[7]));
       fence_proxy_async_smem();
       tc_fence_before();
       mbar_arrive(&bars->p_ready[sb]);
