@@ -6,22 +6,29 @@
 // position q_start + tile * PPT + r % PPT), so every K/V tile feeds G heads.
 // The CTA walks 128-key tiles (two 64-token blocks resolved through the page
 // table) up to its causal limit:
-//   warps 4, 6  TMA producers for two separate 2-stage rings (128-byte
+//   warps 8, 10 TMA producers for two separate 2-stage rings (128-byte
 //               swizzle, layout [64-column atom][128 keys][128 B]): K tiles,
 //               already rotated, from the dense scratch written by rope_k.cu
 //               (one box of 128 keys per atom), refilled as soon as S_j is
 //               done; V tiles from the paged cache (boxes of 64 keys, one per
 //               block), refilled when PV_j is done
-//   warp 5      TMEM owner and MMA issuer: S_j = Q K_j^T into one of two
-//               128-column TMEM buffers, then O += P_{j-1} V_{j-1}
-//               (V as an MN-major operand), tcgen05.commit to mbarriers
-//   warps 0-3   RoPE on the query tile (each thread its own row, scaled by
-//               softmax_scale * log2 e), then softmax, one query row per
-//               thread (TMEM lane): S_j from TMEM in one pass,
-//               causal / length masks, running max with lazy rescaling of O
-//               (only when the max grows by more than 2^8), P_j as bf16/fp16
-//               into a swizzled shared tile, and the final O / l epilogue.
-// TMEM columns: S buffers at 0 and 128, O at 256 (512 allocated).
+//   warp 9      TMEM owner and MMA issuer: S_j = Q K_j^T into one of two
+//               128-column TMEM buffers, then O_h += P_{j-1,h} V_{j-1,h} for
+//               each key half h (V as an MN-major operand), tcgen05.commit to
+//               mbarriers
+//   warps 0-7   RoPE on the query tile (scaled by softmax_scale * log2 e),
+//               then softmax. Warp w owns TMEM lanes 32 (w % 4) .. +31 (one
+//               query row per thread) and key half h = w / 4 of every tile
+//               (64 keys): each half keeps its own running max m_h, row sum
+//               l_h and accumulator O_h, so the two warps sharing a row never
+//               wait on each other inside the key loop. Per tile: S from TMEM
+//               in one pass, causal / length masks, lazy rescaling of O_h
+//               (only when m_h grows by more than 2^8), P as bf16/fp16 into
+//               the half's atom of a swizzled shared tile. The epilogue merges
+//               the halves: O = (2^(m_0-m) O_0 + 2^(m_1-m) O_1) /
+//               (2^(m_0-m) l_0 + 2^(m_1-m) l_1), m = max(m_0, m_1), each warp
+//               writing 64 of the row's 128 output columns.
+// TMEM columns: S buffers at 0 and 128, O_0 at 256, O_1 at 384 (512 allocated).
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -43,27 +50,38 @@ constexpr int kBM = 128;          // query rows per CTA
 constexpr int kBN = 128;          // keys per tile
 constexpr int kAtom = 128 * 128;  // one 64-column atom of a 128-row tile (bytes)
 constexpr int kTile = 2 * kAtom;  // 128 rows x 128 columns x 2 bytes
-constexpr int kThreads = 224;  // warps 0-3 softmax (+ Q RoPE), 4 K loads, 5 MMA / TMEM, 6 V loads
+constexpr int kSoftmaxWarps = 8;                   // 4 lane quarters x 2 key halves
+constexpr int kSoftmaxThreads = kSoftmaxWarps * 32;
+constexpr int kWarpK = 8, kWarpMma = 9, kWarpV = 10;  // K loads, MMA / TMEM, V loads
+constexpr int kThreads = 11 * 32;
 constexpr float kRescaleLog2 = 8.0f;
+// Pairs of every 8 keys whose exponential goes through exp2_poly2 instead of
+// MUFU ex2 (0..4). Measured slower than ex2 alone on the config-4 workload
+// while the loop is bound by shared-memory traffic, so it is off.
+constexpr int kPolyPairs = 0;
 
-// Shared-memory map (offsets from a 1024-byte aligned base).
+constexpr int kStages = 3;  // K ring and V ring depth (tiles in flight cover the TMA latency)
+
+// Shared-memory map (offsets from a 1024-byte aligned base). P never touches
+// shared memory: it is written over its own S columns in TMEM and read from
+// there by the PV MMA, which leaves shared memory to Q, K and V alone.
 constexpr int kOffQ = 0;
-constexpr int kOffK = kOffQ + kTile;          // 2 stages
-constexpr int kOffV = kOffK + 2 * kTile;      // 2 stages
-constexpr int kOffP = kOffV + 2 * kTile;      // 2 buffers
-constexpr int kOffBar = kOffP + 2 * kTile;
+constexpr int kOffK = kOffQ + kTile;            // kStages K tiles
+constexpr int kOffV = kOffK + kStages * kTile;  // kStages V tiles
+constexpr int kOffBar = kOffV + kStages * kTile;
 constexpr int kSmemBytes = kOffBar + 256 + 1024;
 
 // Every ring barrier is per buffer: a parity wait is only valid while the
 // barrier is at most one phase past the awaited one, and per-buffer barriers
-// keep each waiter within that window (a shared PV barrier could run two
-// phases ahead once P is double-buffered).
+// keep each waiter within that window.
 struct Bars {
-  uint64_t k_full[2], k_empty[2], v_full[2], v_empty[2], s_full[2], s_free[2], p_ready[2],
-      pv_done[2];
-  uint64_t q_ready;
+  uint64_t k_full[kStages], k_empty[kStages], v_full[kStages], v_empty[kStages];
+  uint64_t s_full[2];
+  uint64_t p_ready[2][2], pv_done[2][2];  // [S/P buffer][key half]
+  uint64_t q_ready, merge;
   uint32_t tmem_base;
 };
+static_assert(sizeof(Bars) <= 256, "barrier block");
 
 template <typename T>
 struct Elem;
@@ -113,6 +131,27 @@ __device__ __forceinline__ float fast_exp2(float x) {
   return y;
 }
 
+// 2^x for a pair of x in [-126, 2^20] on the FMA pipes, so that part of the
+// softmax exponentials bypass the MUFU unit (which otherwise needs as many
+// cycles per tile as the tensor core). Cody-Waite split x = n + f with
+// n = round(x) (the 1.5 * 2^23 shift trick leaves n in the low mantissa bits
+// of t) and f in [-0.5, 0.5]; 2^f from a degree-3 polynomial fitted for
+// minimal maximum relative error on [-0.5, 0.5] (Remez exchange, 7.5e-5 in
+// fp32 Horner form, far below the bf16 / fp16 rounding of P); 2^n is added
+// into the exponent field as n << 23 (t's exponent bits shift out).
+__device__ __forceinline__ uint64_t exp2_poly2(uint64_t x) {
+  constexpr float kShift = 12582912.0f;  // 1.5 * 2^23
+  constexpr float c0 = 0.99992806f, c1 = 0.69326097f, c2 = 0.24261113f, c3 = 0.05517167f;
+  const uint64_t t = f2add(x, f2pack(kShift, kShift));
+  const uint64_t f = f2sub(x, f2sub(t, f2pack(kShift, kShift)));
+  uint64_t p = f2fma(f2pack(c3, c3), f, f2pack(c2, c2));
+  p = f2fma(p, f, f2pack(c1, c1));
+  p = f2fma(p, f, f2pack(c0, c0));
+  const float2 pf = f2unpack(p), tf = f2unpack(t);
+  return f2pack(__uint_as_float(__float_as_uint(pf.x) + (__float_as_uint(tf.x) << 23)),
+                __uint_as_float(__float_as_uint(pf.y) + (__float_as_uint(tf.y) << 23)));
+}
+
 __device__ __forceinline__ uint32_t sw_off(int row, int chunk) {
   return static_cast<uint32_t>(row * 128 + ((chunk ^ (row & 7)) << 4));
 }
@@ -149,20 +188,24 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (threadIdx.x == 0) {
     *s_abort = 0;
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < kStages; ++i) {
       mbar_init(&bars->k_full[i], 1);
       mbar_init(&bars->k_empty[i], 1);
       mbar_init(&bars->v_full[i], 1);
       mbar_init(&bars->v_empty[i], 1);
-      mbar_init(&bars->s_full[i], 1);
-      mbar_init(&bars->s_free[i], 128);
-      mbar_init(&bars->p_ready[i], 128);
-      mbar_init(&bars->pv_done[i], 1);
     }
-    mbar_init(&bars->q_ready, 128);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&bars->s_full[i], 1);
+      for (int h = 0; h < 2; ++h) {
+        mbar_init(&bars->p_ready[i][h], 128);
+        mbar_init(&bars->pv_done[i][h], 1);
+      }
+    }
+    mbar_init(&bars->q_ready, kSoftmaxThreads);
+    mbar_init(&bars->merge, kSoftmaxThreads);
     fence_barrier_init();
   }
-  if (warp == 5) {
+  if (warp == kWarpMma) {
     tmem_alloc(&bars->tmem_base, 512);
     tmem_relinquish();
   }
@@ -176,10 +219,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     *s_abort = 1;
   };
 
-  if (warp == 4 || warp == 6) {
-    // --------------------------- TMA producers (K: warp 4, V: warp 6) ---------------------------
+  if (warp == kWarpK || warp == kWarpV) {
+    // ------------------------------- TMA producers -------------------------------
     if (lane == 0) {
-      const bool is_k = warp == 4;
+      const bool is_k = warp == kWarpK;
       tma_prefetch_desc(is_k ? &tm_k : &tm_v);
       const uint64_t pol = policy_evict_last();  // tiles are re-read by other CTAs
       const int32_t* row = p.page_table + static_cast<int64_t>(s) * p.max_blocks;
@@ -187,8 +230,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint64_t* empty = is_k ? bars->k_empty : bars->v_empty;
       uint8_t* ring = smem + (is_k ? kOffK : kOffV);
       for (int j = 0; j < n_tiles && !*s_abort; ++j) {
-        const int st = j & 1;
-        if (j >= 2 && !mbar_wait(&empty[st], ((j >> 1) - 1) & 1)) {
+        const int st = j % kStages;
+        if (j >= kStages && !mbar_wait(&empty[st], ((j / kStages) - 1) & 1)) {
           fail(kStatusWaitTimeout);
           break;
         }
@@ -214,36 +257,44 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
-  } else if (warp == 5) {
+  } else if (warp == kWarpMma) {
     // ------------------------------ MMA issuer ------------------------------
     if (lane == 0) {
       const uint32_t idesc_s = umma_idesc_f16(Elem<T>::kBf16, kBM, kBN, false, false);
       const uint32_t idesc_pv = umma_idesc_f16(Elem<T>::kBf16, kBM, kHD, false, true);
       const uint32_t q_addr = smem_u32(smem + kOffQ);
+      // O_h += P_h V_h for both key halves of tile jj; each half starts as soon
+      // as its own softmax warps have stored P_h. P_h is the A operand in TMEM:
+      // 32 columns of packed pairs over the first half of the half's S columns.
       auto issue_pv = [&](int jj) -> bool {
-        if (!mbar_wait(&bars->p_ready[jj & 1], (jj >> 1) & 1) ||
-            !mbar_wait(&bars->v_full[jj & 1], (jj >> 1) & 1))
-          return false;
-        tc_fence_after();
-        const uint32_t p_addr = smem_u32(smem + kOffP + (jj & 1) * kTile);
-        const uint32_t v_addr = smem_u32(smem + kOffV + (jj & 1) * kTile);
+        const int b = jj & 1, vs = jj % kStages;
+        if (!mbar_wait(&bars->v_full[vs], (jj / kStages) & 1)) return false;
+        const uint32_t v_addr = smem_u32(smem + kOffV + vs * kTile);
+        for (int h = 0; h < 2; ++h) {
+          if (!mbar_wait(&bars->p_ready[b][h], (jj >> 1) & 1)) return false;
+          tc_fence_after();
 #pragma unroll
-        for (int kk = 0; kk < kBN / 16; ++kk) {
-          // A = P [128 rows x 16 keys] K-major; B = V [16 keys x 128 d] MN-major
-          const uint64_t ad = umma_desc_sw128(p_addr + (kk >> 2) * kAtom + (kk & 3) * 32, 16, 1024);
-          const uint64_t bd = umma_desc_sw128(v_addr + kk * 2048, kAtom, 1024);
-          umma_f16_ss(tmem + 256, ad, bd, idesc_pv, (jj > 0 || kk > 0) ? 1u : 0u);
+          for (int kk = 0; kk < 4; ++kk) {
+            // A = P [128 rows x 16 keys] (8 TMEM columns); B = V [16 keys x 128 d]
+            // MN-major, keys 64 h + 16 kk ..
+            const uint64_t bd = umma_desc_sw128(v_addr + (4 * h + kk) * 2048, kAtom, 1024);
+            umma_f16_ts(tmem + 256 + 128 * h, tmem + b * 128 + 64 * h + 8 * kk, bd, idesc_pv,
+                        (jj > 0 || kk > 0) ? 1u : 0u);
+          }
+          umma_commit(&bars->pv_done[b][h]);
         }
-        umma_commit(&bars->pv_done[jj & 1]);
-        umma_commit(&bars->v_empty[jj & 1]);
+        umma_commit(&bars->v_empty[vs]);
         return true;
       };
+      // Issue order S_0, S_1, PV_0, S_2, PV_1, ...: S_{j+2} overwrites the
+      // TMEM buffer of S_j / P_j only after PV_j was issued (which waited for
+      // both halves of P_j, hence for their loads of S_j), and tcgen05.mma
+      // operations of one thread execute in issue order.
       bool ok = mbar_wait(&bars->q_ready, 0);
       tc_fence_after();
       for (int j = 0; j < n_tiles && ok; ++j) {
-        const int st = j & 1;
-        if (!mbar_wait(&bars->k_full[st], (j >> 1) & 1) ||
-            (j >= 2 && !mbar_wait(&bars->s_free[st], ((j >> 1) - 1) & 1))) {
+        const int st = j % kStages;
+        if (!mbar_wait(&bars->k_full[st], (j / kStages) & 1)) {
           ok = false;
           break;
         }
@@ -253,9 +304,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int kk = 0; kk < kHD / 16; ++kk) {
           const uint64_t ad = umma_desc_sw128(q_addr + (kk >> 2) * kAtom + (kk & 3) * 32, 16, 1024);
           const uint64_t bd = umma_desc_sw128(k_addr + (kk >> 2) * kAtom + (kk & 3) * 32, 16, 1024);
-          umma_f16_ss(tmem + st * 128, ad, bd, idesc_s, kk > 0 ? 1u : 0u);
+          umma_f16_ss(tmem + (j & 1) * 128, ad, bd, idesc_s, kk > 0 ? 1u : 0u);
         }
-        umma_commit(&bars->s_full[st]);
+        umma_commit(&bars->s_full[j & 1]);
         umma_commit(&bars->k_empty[st]);  // K_j is free as soon as S_j is done
         if (j >= 1 && !issue_pv(j - 1)) ok = false;
       }
@@ -263,40 +314,59 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!ok) fail(kStatusWaitTimeout);
     }
   } else {
-    // ------------------------------ softmax warps 0-3 ------------------------------
-    const int r = threadIdx.x;  // TMEM lane == query row
-    const int hl = r / ppt, i = r % ppt;
+    // ------------------------------ softmax warps 0-7 ------------------------------
+    const int quarter = warp & 3, h = warp >> 2;  // TMEM lane quarter, key half
+    const int r = quarter * 32 + lane;            // TMEM lane == query row
+    const int i = r % ppt;
     const bool live = i < rows_valid;
     const int pos = q0 + i;
     {
-      // Query row r (head kvh*G + r / ppt, position q0 + r % ppt), rotated and
-      // scaled by softmax_scale * log2(e), into the swizzled Q tile.
+      // The query tile, rotated and scaled by softmax_scale * log2(e), into the
+      // swizzled Q buffer. Row R is head kvh*G + R / ppt at position
+      // q0 + R % ppt; unit u = (R, c) rotates the pairs (d, d + 64) for
+      // d in [8c, 8c + 8). Eight consecutive threads take the 8 units of one
+      // row, so each warp-wide load reads 4 contiguous row segments.
       const int half = kHD / 2;
-      const T* qrow = static_cast<const T*>(p.q) +
-                      ((static_cast<int64_t>(s) * p.Hq + kvh * G + hl) * p.Lq + qt * ppt + i) * kHD;
+      const int tid = threadIdx.x;  // 0 .. 255
       uint8_t* qs = smem + kOffQ;
-      const bool pos_ok = pos < p.max_pos;
-      for (int c = 0; c < 8; ++c) {
-        uint4 lo = make_uint4(0, 0, 0, 0), hi = lo;
-        if (live) {
-          lo = *reinterpret_cast<const uint4*>(qrow + 8 * c);
-          hi = *reinterpret_cast<const uint4*>(qrow + half + 8 * c);
-          float cs[8], sn[8];
+      uint4 lo[4], hi[4];
+      float4 cs[8], sn[8];
 #pragma unroll
-          for (int e = 0; e < 8; ++e) {
-            cs[e] = pos_ok ? p.cos[static_cast<int64_t>(pos) * half + 8 * c + e] : 1.f;
-            sn[e] = pos_ok ? p.sin[static_cast<int64_t>(pos) * half + 8 * c + e] : 0.f;
+      for (int k = 0; k < 4; ++k) {  // all loads first, so their latencies overlap
+        const int u = tid + kSoftmaxThreads * k, R = u >> 3, c = u & 7;
+        const int iR = R % ppt, posR = q0 + iR;
+        lo[k] = hi[k] = make_uint4(0, 0, 0, 0);
+        cs[2 * k] = cs[2 * k + 1] = make_float4(1.f, 1.f, 1.f, 1.f);
+        sn[2 * k] = sn[2 * k + 1] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (iR < rows_valid) {
+          const T* qrow = static_cast<const T*>(p.q) +
+                          ((static_cast<int64_t>(s) * p.Hq + kvh * G + R / ppt) * p.Lq + qt * ppt + iR) * kHD;
+          lo[k] = *reinterpret_cast<const uint4*>(qrow + 8 * c);
+          hi[k] = *reinterpret_cast<const uint4*>(qrow + half + 8 * c);
+          if (posR < p.max_pos) {
+            const float4* cr = reinterpret_cast<const float4*>(p.cos + static_cast<int64_t>(posR) * half + 8 * c);
+            const float4* sr = reinterpret_cast<const float4*>(p.sin + static_cast<int64_t>(posR) * half + 8 * c);
+            cs[2 * k] = cr[0];
+            cs[2 * k + 1] = cr[1];
+            sn[2 * k] = sr[0];
+            sn[2 * k + 1] = sr[1];
           }
-          rope8<T>(lo, hi, cs, sn, p.scale_log2);
         }
-        *reinterpret_cast<uint4*>(qs + sw_off(r, c)) = lo;
-        *reinterpret_cast<uint4*>(qs + kAtom + sw_off(r, c)) = hi;
+      }
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const int u = tid + kSoftmaxThreads * k, R = u >> 3, c = u & 7;
+        rope8<T>(lo[k], hi[k], reinterpret_cast<const float*>(&cs[2 * k]),
+                 reinterpret_cast<const float*>(&sn[2 * k]), p.scale_log2);
+        *reinterpret_cast<uint4*>(qs + sw_off(R, c)) = lo[k];
+        *reinterpret_cast<uint4*>(qs + kAtom + sw_off(R, c)) = hi[k];
       }
       fence_proxy_async_smem();
       mbar_arrive(&bars->q_ready);
     }
     const int kmax_row = !live ? 0 : (p.causal ? min(seq_len, pos + 1) : seq_len);
-    const uint32_t lane_addr = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+    const uint32_t lane_addr = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
+    const uint32_t o_col = 256 + 128 * h;  // this half's accumulator O_h
     float m_ref = -INFINITY, l = 0.f;
     bool ok = true;
     for (int j = 0; j < n_tiles; ++j) {
@@ -307,45 +377,39 @@ __global__ void __launch_bounds__(kThreads, 1)
         break;
       }
       tc_fence_after();
-      // One pass over TMEM: the whole 128-key score row into registers.
-      uint32_t sr[4][32];
-#pragma unroll
-      for (int c4 = 0; c4 < 4; ++c4) tmem_ld32(lane_addr + sb * 128 + c4 * 32, sr[c4]);
+      // One pass over TMEM: this half's 64 scores of the row.
+      uint32_t sr[2][32];
+      tmem_ld32(lane_addr + sb * 128 + 64 * h, sr[0]);
+      tmem_ld32(lane_addr + sb * 128 + 64 * h + 32, sr[1]);
       tmem_wait_ld();
-      tc_fence_before();
-      mbar_arrive(&bars->s_free[sb]);  // the S buffer can take S_{j+2} already
 
-      const int base_key = j * kBN;
-      // Tiles that lie wholly below every row's key limit skip the per-key masks.
-      const bool full = __all_sync(0xffffffffu, base_key + kBN <= kmax_row);
+      const int base_key = j * kBN + 64 * h;
+      // Halves that lie wholly below every row's key limit skip the per-key masks.
+      const bool full = __all_sync(0xffffffffu, base_key + 64 <= kmax_row);
       if (!full) {
 #pragma unroll
-        for (int c4 = 0; c4 < 4; ++c4)
+        for (int c2 = 0; c2 < 2; ++c2)
 #pragma unroll
           for (int e = 0; e < 32; ++e)
-            if (base_key + c4 * 32 + e >= kmax_row) sr[c4][e] = __float_as_uint(-INFINITY);
+            if (base_key + c2 * 32 + e >= kmax_row) sr[c2][e] = __float_as_uint(-INFINITY);
       }
-      // Row max with 8 independent partial maxima (short dependency chains).
-      float mp[8];
+      // Max over the 64 scores: three-input max in 4 independent chains.
+      float mp[4];
 #pragma unroll
-      for (int k = 0; k < 8; ++k) mp[k] = __uint_as_float(sr[0][k]);
+      for (int k = 0; k < 4; ++k) mp[k] = __uint_as_float(sr[0][k]);
 #pragma unroll
-      for (int c = 8; c < kBN; ++c) mp[c & 7] = fmaxf(mp[c & 7], __uint_as_float(sr[c >> 5][c & 31]));
-      const float mx = fmaxf(fmaxf(fmaxf(mp[0], mp[1]), fmaxf(mp[2], mp[3])),
-                             fmaxf(fmaxf(mp[4], mp[5]), fmaxf(mp[6], mp[7])));
+      for (int t = 0; t < 30; ++t)
+        mp[t & 3] = max3f(mp[t & 3], __uint_as_float(sr[(4 + 2 * t) >> 5][(4 + 2 * t) & 31]),
+                          __uint_as_float(sr[(5 + 2 * t) >> 5][(5 + 2 * t) & 31]));
+      const float mx = max3f(mp[0], mp[1], fmaxf(mp[2], mp[3]));
       const bool grow = mx > m_ref + kRescaleLog2 || (m_ref == -INFINITY && mx != -INFINITY);
       const float m_new = grow ? mx : m_ref;
       const float factor = (grow && m_ref != -INFINITY) ? fast_exp2(m_ref - m_new) : 1.f;
-      // P_j goes to buffer j % 2, last read by PV_{j-2}; O may only be rescaled
-      // once PV_{j-1} is done.
-      if (j >= 2 &&
-          !__all_sync(0xffffffffu, mbar_wait(&bars->pv_done[sb], ((j >> 1) - 1) & 1))) {
-        ok = false;
-        break;
-      }
+      // O_h may only be rescaled once PV_{j-1} is done. (PV_{j-2}, the last
+      // reader of this TMEM buffer, finished before S_j did.)
       const bool rescale = j >= 1 && __any_sync(0xffffffffu, factor != 1.f);
       if (rescale &&
-          !__all_sync(0xffffffffu, mbar_wait(&bars->pv_done[sb ^ 1], ((j - 1) >> 1) & 1))) {
+          !__all_sync(0xffffffffu, mbar_wait(&bars->pv_done[sb ^ 1][h], ((j - 1) >> 1) & 1))) {
         ok = false;
         break;
       }
@@ -354,83 +418,124 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int c4 = 0; c4 < 4; ++c4) {
           uint32_t raw[32];
-          tmem_ld32(lane_addr + 256 + c4 * 32, raw);
+          tmem_ld32(lane_addr + o_col + c4 * 32, raw);
           tmem_wait_ld();
 #pragma unroll
           for (int e = 0; e < 32; ++e) raw[e] = __float_as_uint(__uint_as_float(raw[e]) * factor);
-          tmem_st32(lane_addr + 256 + c4 * 32, raw);
+          tmem_st32(lane_addr + o_col + c4 * 32, raw);
         }
         tmem_wait_st();
       }
       l *= factor;
       m_ref = m_new;
       const float base = m_ref == -INFINITY ? 0.f : m_ref;
-      // P = exp2(S - max): masked keys hold -inf and give exactly 0. The row sum
-      // uses 8 partial sums so the adds do not serialise behind each exp.
-      uint8_t* pbuf = smem + kOffP + sb * kTile;
-      float lp[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      // P = exp2(S - max), packed to bf16/fp16 pairs and stored over the first
+      // 32 of this half's 64 S columns (already in registers), where the PV
+      // MMA reads it. In halves without masked keys kPolyPairs pairs of every
+      // 8 keys use the FMA-pipe polynomial; masked halves use ex2 throughout,
+      // so masked keys (-inf) give exactly 0. Packed f32x2 subtraction and 4
+      // partial row sums.
+      const uint64_t base2 = f2pack(base, base);
+      uint64_t lp[4] = {0, 0, 0, 0};
+      uint32_t pk[32];
 #pragma unroll
-      for (int c8 = 0; c8 < 16; ++c8) {
-        float pv[8];
+      for (int c8 = 0; c8 < 8; ++c8) {
 #pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          pv[e] = fast_exp2(__uint_as_float(sr[c8 >> 2][(c8 & 3) * 8 + e]) - base);
-          lp[e] += pv[e];
+        for (int e2 = 0; e2 < 4; ++e2) {
+          const uint32_t* v = &sr[c8 >> 2][(c8 & 3) * 8 + 2 * e2];
+          const uint64_t x = f2sub(f2pack(__uint_as_float(v[0]), __uint_as_float(v[1])), base2);
+          const float2 xf = f2unpack(x);
+          uint64_t pv;
+          if (full && e2 < kPolyPairs)
+            pv = exp2_poly2(f2pack(fmaxf(xf.x, -126.f), fmaxf(xf.y, -126.f)));
+          else
+            pv = f2pack(fast_exp2(xf.x), fast_exp2(xf.y));
+          lp[e2] = f2add(lp[e2], pv);
+          const float2 pf = f2unpack(pv);
+          pk[c8 * 4 + e2] = Elem<T>::from2(pf.x, pf.y);
         }
-        uint4 w;
-        w.x = Elem<T>::from2(pv[0], pv[1]);
-        w.y = Elem<T>::from2(pv[2], pv[3]);
-        w.z = Elem<T>::from2(pv[4], pv[5]);
-        w.w = Elem<T>::from2(pv[6], pv[7]);
-        *reinterpret_cast<uint4*>(pbuf + (c8 >> 3) * kAtom + sw_off(r, c8 & 7)) = w;
       }
-      l += ((lp[0] + lp[1]) + (lp[2] + lp[3])) + ((lp[4] + lp[5]) + (lp[6] + lp[7]));
-      fence_proxy_async_smem();
+      tmem_st32(lane_addr + sb * 128 + 64 * h, pk);
+      {
+        const float2 a = f2unpack(f2add(f2add(lp[0], lp[1]), f2add(lp[2], lp[3])));
+        l += a.x + a.y;
+      }
+      tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(&bars->p_ready[sb]);
+      mbar_arrive(&bars->p_ready[sb][h]);
     }
-    if (!ok) fail(kStatusWaitTimeout);
-    // O is final once the last two PV steps (one per P buffer) are done.
+    // O_h is final once this half's last two PV steps (one per P buffer) are done.
     if (ok && n_tiles >= 2 &&
         !__all_sync(0xffffffffu,
-                    mbar_wait(&bars->pv_done[(n_tiles - 2) & 1], ((n_tiles - 2) >> 1) & 1)))
+                    mbar_wait(&bars->pv_done[(n_tiles - 2) & 1][h], ((n_tiles - 2) >> 1) & 1)))
       ok = false;
-    if (ok && n_tiles > 0 &&
-        __all_sync(0xffffffffu,
-                   mbar_wait(&bars->pv_done[(n_tiles - 1) & 1], ((n_tiles - 1) >> 1) & 1))) {
+    if (ok && n_tiles >= 1 &&
+        !__all_sync(0xffffffffu,
+                    mbar_wait(&bars->pv_done[(n_tiles - 1) & 1][h], ((n_tiles - 1) >> 1) & 1)))
+      ok = false;
+    // Merge the halves. (m_h, l_h) go through the Q tile, which no MMA reads
+    // any more once the last S tile has been observed; every softmax thread
+    // arrives on the merge barrier exactly once, also after a failed wait.
+    float2* ml = reinterpret_cast<float2*>(smem + kOffQ);  // [half][row]
+    ml[h * kBM + r] = make_float2(m_ref, l);
+    tc_fence_before();
+    mbar_arrive(&bars->merge);
+    if (!ok) fail(kStatusWaitTimeout);
+    if (ok && __all_sync(0xffffffffu, mbar_wait(&bars->merge, 0))) {
       tc_fence_after();
-      const float inv = l > 0.f ? 1.f / l : 0.f;
-      T* orow = static_cast<T*>(p.out) +
-                ((static_cast<int64_t>(s) * p.Hq + kvh * G + hl) * p.Lq + qt * ppt + i) * kHD;
+      const float2 a0 = ml[r], a1 = ml[kBM + r];
+      const float m = fmaxf(a0.x, a1.x);
+      const float w0 = a0.x == -INFINITY ? 0.f : fast_exp2(a0.x - m);
+      const float w1 = a1.x == -INFINITY ? 0.f : fast_exp2(a1.x - m);
+      const float den = w0 * a0.y + w1 * a1.y;
+      const float inv = den > 0.f ? 1.f / den : 0.f;
+      const float s0 = w0 * inv, s1 = w1 * inv;
+      // Output columns [64 h, 64 h + 64) of this warp's 32 rows, staged in the
+      // first K stage (free: every S MMA is done) as [32 rows][8 x 16 B
+      // chunks] with an XOR swizzle, then stored 4 rows per warp-wide
+      // instruction.
+      uint8_t* stage = smem + kOffK + warp * (32 * 128);
 #pragma unroll
-      for (int c4 = 0; c4 < 4; ++c4) {
-        uint32_t raw[32];
-        tmem_ld32(lane_addr + 256 + c4 * 32, raw);
+      for (int c2 = 0; c2 < 2; ++c2) {
+        uint32_t o0[32], o1[32];
+        tmem_ld32(lane_addr + 256 + 64 * h + c2 * 32, o0);
+        tmem_ld32(lane_addr + 384 + 64 * h + c2 * 32, o1);
         tmem_wait_ld();
-        if (live) {
 #pragma unroll
-          for (int e8 = 0; e8 < 4; ++e8) {
-            uint4 w;
-            w.x = Elem<T>::from2(__uint_as_float(raw[e8 * 8 + 0]) * inv,
-                                 __uint_as_float(raw[e8 * 8 + 1]) * inv);
-            w.y = Elem<T>::from2(__uint_as_float(raw[e8 * 8 + 2]) * inv,
-                                 __uint_as_float(raw[e8 * 8 + 3]) * inv);
-            w.z = Elem<T>::from2(__uint_as_float(raw[e8 * 8 + 4]) * inv,
-                                 __uint_as_float(raw[e8 * 8 + 5]) * inv);
-            w.w = Elem<T>::from2(__uint_as_float(raw[e8 * 8 + 6]) * inv,
-                                 __uint_as_float(raw[e8 * 8 + 7]) * inv);
-            *reinterpret_cast<uint4*>(orow + c4 * 32 + e8 * 8) = w;
-          }
+        for (int e8 = 0; e8 < 4; ++e8) {
+          float o[8];
+#pragma unroll
+          for (int e = 0; e < 8; ++e)
+            o[e] = __uint_as_float(o0[e8 * 8 + e]) * s0 + __uint_as_float(o1[e8 * 8 + e]) * s1;
+          uint4 w;
+          w.x = Elem<T>::from2(o[0], o[1]);
+          w.y = Elem<T>::from2(o[2], o[3]);
+          w.z = Elem<T>::from2(o[4], o[5]);
+          w.w = Elem<T>::from2(o[6], o[7]);
+          const int chunk = c2 * 4 + e8;
+          *reinterpret_cast<uint4*>(stage + lane * 128 + ((chunk ^ (lane & 7)) << 4)) = w;
         }
       }
-    } else if (ok && n_tiles > 0) {
+      __syncwarp();
+#pragma unroll
+      for (int it = 0; it < 8; ++it) {
+        const int rl = it * 4 + (lane >> 3), chunk = lane & 7;
+        const int R = quarter * 32 + rl, iR = R % ppt;
+        if (iR < rows_valid) {
+          T* orow = static_cast<T*>(p.out) +
+                    ((static_cast<int64_t>(s) * p.Hq + kvh * G + R / ppt) * p.Lq + qt * ppt + iR) * kHD;
+          *reinterpret_cast<uint4*>(orow + 64 * h + chunk * 8) =
+              *reinterpret_cast<const uint4*>(stage + rl * 128 + ((chunk ^ (rl & 7)) << 4));
+        }
+      }
+    } else if (ok) {
       fail(kStatusWaitTimeout);
     }
   }
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 5) {
+  if (warp == kWarpMma) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
