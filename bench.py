@@ -251,7 +251,8 @@ def run_ours(args):
     world, rank, local = _dist_env()
     if world > 1:
         torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=120))
+        dist.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
     device = torch.device("cuda", local if world > 1 else 0)
     torch.cuda.set_device(device)
 
