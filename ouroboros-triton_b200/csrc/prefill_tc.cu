@@ -1,11 +1,15 @@
 // Chunked prefill on the 5th-generation tensor cores (tcgen05 + TMEM + TMA),
 // head_dim 128, fp16/bf16, any GQA group dividing 128, causal or not.
 //
-// CTA = 128 query rows x one KV head of one sequence: the G query heads of
-// the group times 128/G consecutive query positions (row r = head (r / PPT),
+// Work item = 128 query rows x one KV head of one sequence: the G query heads
+// of the group times 128/G consecutive query positions (row r = head (r / PPT),
 // position q_start + tile * PPT + r % PPT), so every K/V tile feeds G heads.
-// The CTA walks 128-key tiles (two 64-token blocks resolved through the page
-// table) up to its causal limit:
+// Persistent CTAs (one per SM) walk their items back to back; for each item the
+// CTA walks 128-key tiles (two 64-token blocks resolved through the page table)
+// up to its causal limit. Rings, TMEM buffers and barrier phases run on across
+// item boundaries, and the softmax warps load the next item's query tile while
+// they write the current item's output, so the tensor core starts on the next
+// item without waiting for the epilogue:
 //   warps 8, 10 TMA producers for two separate 2-stage rings (128-byte
 //               swizzle, layout [64-column atom][128 keys][128 B]): K tiles,
 //               already rotated, from the dense scratch written by rope_k.cu
@@ -60,26 +64,29 @@ constexpr float kRescaleLog2 = 8.0f;
 // while the loop is bound by shared-memory traffic, so it is off.
 constexpr int kPolyPairs = 0;
 
-constexpr int kStages = 3;  // K ring and V ring depth (tiles in flight cover the TMA latency)
+constexpr int kStagesK = 2, kStagesV = 2;  // ring depths (3 measured no faster)
 
 // Shared-memory map (offsets from a 1024-byte aligned base). P never touches
 // shared memory: it is written over its own S columns in TMEM and read from
-// there by the PV MMA, which leaves shared memory to Q, K and V alone.
+// there by the PV MMA.
 constexpr int kOffQ = 0;
-constexpr int kOffK = kOffQ + kTile;            // kStages K tiles
-constexpr int kOffV = kOffK + kStages * kTile;  // kStages V tiles
-constexpr int kOffBar = kOffV + kStages * kTile;
+constexpr int kOffK = kOffQ + kTile;             // kStagesK K tiles
+constexpr int kOffV = kOffK + kStagesK * kTile;  // kStagesV V tiles
+constexpr int kOffStage = kOffV + kStagesV * kTile;  // output staging, 4 KB per softmax warp
+constexpr int kOffMl = kOffStage + kSoftmaxWarps * 32 * 128;  // (m, l) per half and row
+constexpr int kOffBar = kOffMl + 2 * kBM * 8;
 constexpr int kSmemBytes = kOffBar + 256 + 1024;
 
 // Every ring barrier is per buffer: a parity wait is only valid while the
 // barrier is at most one phase past the awaited one, and per-buffer barriers
 // keep each waiter within that window.
 struct Bars {
-  uint64_t k_full[kStages], k_empty[kStages], v_full[kStages], v_empty[kStages];
+  uint64_t k_full[kStagesK], k_empty[kStagesK], v_full[kStagesV], v_empty[kStagesV];
   uint64_t s_full[2];
   uint64_t p_ready[2][2], pv_done[2][2];  // [S/P buffer][key half]
-  uint64_t q_ready, merge;
+  uint64_t q_ready, merge, o_free;        // once per item
   uint32_t tmem_base;
+  int32_t abort;
 };
 static_assert(sizeof(Bars) <= 256, "barrier block");
 
@@ -156,6 +163,93 @@ __device__ __forceinline__ uint32_t sw_off(int row, int chunk) {
   return static_cast<uint32_t>(row * 128 + ((chunk ^ (row & 7)) << 4));
 }
 
+// One work item: 128 query rows (G heads x ppt positions) of one KV head of one
+// sequence. Items are numbered so that the query tiles of one (sequence, KV
+// head) are consecutive, the latest (most keys) first; CTA c takes items
+// c, c + gridDim.x, ... (each CTA gets a mix of long and short items, and the
+// CTAs running at one time share a few sequences' K/V tiles in L2).
+struct Item {
+  int qt, kvh, s, q0, rows_valid, seq_len, n_tiles, nb;
+  bool bad;  // negative query position
+};
+
+__device__ __forceinline__ Item item_at(const RowsParams& p, int L, int n_qt, int ppt) {
+  Item it;
+  const int group = L / n_qt;
+  it.qt = n_qt - 1 - (L - group * n_qt);
+  it.kvh = group % p.Hkv;
+  it.s = group / p.Hkv;
+  it.seq_len = p.seq_lens[it.s];
+  it.q0 = (p.q_start ? p.q_start[it.s] : 0) + it.qt * ppt;
+  it.bad = it.q0 < 0;
+  // rows whose position lies in the chunk and the sequence
+  it.rows_valid = max(0, min(min(ppt, p.Lq - it.qt * ppt), it.seq_len - it.q0));
+  const int kmax = p.causal ? min(it.seq_len, it.q0 + it.rows_valid) : it.seq_len;
+  it.n_tiles = (it.bad || it.rows_valid <= 0 || kmax <= 0) ? 0 : (kmax + kBN - 1) / kBN;
+  it.nb = (kmax + kBlock - 1) / kBlock;
+  return it;
+}
+
+// Next item of this CTA at or after L that has work (L >= n_items: none).
+__device__ __forceinline__ int next_item(const RowsParams& p, int L, int n_items, int n_qt, int ppt,
+                                         Item& it) {
+  for (; L < n_items; L += gridDim.x) {
+    it = item_at(p, L, n_qt, ppt);
+    if (it.n_tiles > 0) return L;
+    if (it.bad && p.status) atomicOr(p.status, kStatusBadPosition);
+  }
+  return n_items;
+}
+
+// The query tile of one item, loaded into registers (16-byte vectors, all
+// loads issued together) and then rotated and scaled by softmax_scale * log2 e
+// into the swizzled Q buffer. Row R is head kvh*G + R / ppt at position
+// q0 + R % ppt; unit u = (R, c) covers the pairs (d, d + 64), d in [8c, 8c+8).
+// Eight consecutive threads take the 8 units of one row, so a warp-wide load
+// reads 4 contiguous row segments.
+template <typename T>
+struct QTile {
+  uint4 lo[4], hi[4];
+  float4 cs[8], sn[8];
+
+  __device__ __forceinline__ void load(const RowsParams& p, const Item& it, int ppt, int tid) {
+    const int half = kHD / 2;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int u = tid + kSoftmaxThreads * k, R = u >> 3, c = u & 7;
+      const int iR = R % ppt, posR = it.q0 + iR;
+      lo[k] = hi[k] = make_uint4(0, 0, 0, 0);
+      cs[2 * k] = cs[2 * k + 1] = make_float4(1.f, 1.f, 1.f, 1.f);
+      sn[2 * k] = sn[2 * k + 1] = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (iR < it.rows_valid) {
+        const T* qrow = static_cast<const T*>(p.q) +
+                        ((static_cast<int64_t>(it.s) * p.Hq + it.kvh * p.G + R / ppt) * p.Lq +
+                         it.qt * ppt + iR) * kHD;
+        lo[k] = *reinterpret_cast<const uint4*>(qrow + 8 * c);
+        hi[k] = *reinterpret_cast<const uint4*>(qrow + half + 8 * c);
+        if (posR < p.max_pos) {
+          const float4* cr = reinterpret_cast<const float4*>(p.cos + static_cast<int64_t>(posR) * half + 8 * c);
+          const float4* sr = reinterpret_cast<const float4*>(p.sin + static_cast<int64_t>(posR) * half + 8 * c);
+          cs[2 * k] = cr[0];
+          cs[2 * k + 1] = cr[1];
+          sn[2 * k] = sr[0];
+          sn[2 * k + 1] = sr[1];
+        }
+      }
+    }
+  }
+  __device__ __forceinline__ void store(uint8_t* qs, float scale, int tid) {
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int u = tid + kSoftmaxThreads * k, R = u >> 3, c = u & 7;
+      rope8<T>(lo[k], hi[k], reinterpret_cast<const float*>(&cs[2 * k]),
+               reinterpret_cast<const float*>(&sn[2 * k]), scale);
+      *reinterpret_cast<uint4*>(qs + sw_off(R, c)) = lo[k];
+      *reinterpret_cast<uint4*>(qs + kAtom + sw_off(R, c)) = hi[k];
+    }
+  }
+};
+
 template <typename T>
 __global__ void __launch_bounds__(kThreads, 1)
     prefill_tc_kernel(const __grid_constant__ CUtensorMap tm_k,
@@ -165,32 +259,21 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   Bars* bars = reinterpret_cast<Bars*>(smem + kOffBar);
-  __shared__ int32_t s_abort_flag;
-  volatile int32_t* s_abort = &s_abort_flag;
+  volatile int32_t* s_abort = &bars->abort;
 
-  const int qt = blockIdx.x, kvh = blockIdx.y, s = blockIdx.z;
   const int G = p.G;
   const int ppt = kBM / G;  // positions per tile
+  const int n_qt = (p.Lq + ppt - 1) / ppt;
+  const int n_items = n_qt * p.Hkv * p.S;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int seq_len = p.seq_lens[s];
-  const int q0 = (p.q_start ? p.q_start[s] : 0) + qt * ppt;  // position of row-group start
-  // rows whose position lies in the chunk and the sequence
-  const int rows_valid = max(0, min(min(ppt, p.Lq - qt * ppt), seq_len - q0));
-  if (q0 < 0) {
-    if (threadIdx.x == 0 && p.status) atomicOr(p.status, kStatusBadPosition);
-    return;
-  }
-  if (rows_valid <= 0) return;
-  const int last_pos = q0 + rows_valid - 1;
-  const int kmax = p.causal ? min(seq_len, last_pos + 1) : seq_len;
-  const int n_tiles = (kmax + kBN - 1) / kBN;
-  const int nb = (kmax + kBlock - 1) / kBlock;
 
   if (threadIdx.x == 0) {
     *s_abort = 0;
-    for (int i = 0; i < kStages; ++i) {
+    for (int i = 0; i < kStagesK; ++i) {
       mbar_init(&bars->k_full[i], 1);
       mbar_init(&bars->k_empty[i], 1);
+    }
+    for (int i = 0; i < kStagesV; ++i) {
       mbar_init(&bars->v_full[i], 1);
       mbar_init(&bars->v_empty[i], 1);
     }
@@ -203,6 +286,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     mbar_init(&bars->q_ready, kSoftmaxThreads);
     mbar_init(&bars->merge, kSoftmaxThreads);
+    mbar_init(&bars->o_free, kSoftmaxThreads);
     fence_barrier_init();
   }
   if (warp == kWarpMma) {
@@ -219,40 +303,49 @@ __global__ void __launch_bounds__(kThreads, 1)
     *s_abort = 1;
   };
 
+  // Every role walks the same item sequence and counts tiles globally: ring
+  // slots and TMEM buffers rotate across item boundaries, and every barrier
+  // phase follows from the global tile index g (or the item count done).
   if (warp == kWarpK || warp == kWarpV) {
     // ------------------------------- TMA producers -------------------------------
     if (lane == 0) {
       const bool is_k = warp == kWarpK;
       tma_prefetch_desc(is_k ? &tm_k : &tm_v);
       const uint64_t pol = policy_evict_last();  // tiles are re-read by other CTAs
-      const int32_t* row = p.page_table + static_cast<int64_t>(s) * p.max_blocks;
       uint64_t* full = is_k ? bars->k_full : bars->v_full;
       uint64_t* empty = is_k ? bars->k_empty : bars->v_empty;
       uint8_t* ring = smem + (is_k ? kOffK : kOffV);
-      for (int j = 0; j < n_tiles && !*s_abort; ++j) {
-        const int st = j % kStages;
-        if (j >= kStages && !mbar_wait(&empty[st], ((j / kStages) - 1) & 1)) {
-          fail(kStatusWaitTimeout);
-          break;
-        }
-        mbar_arrive_expect_tx(&full[st], kTile);
-        uint8_t* dst = ring + st * kTile;
-        if (is_k) {
-          // rotated keys: rows (s, kvh, 128 j .. 128 j + 127) of the scratch
-          const int ky = (s * p.Hkv + kvh) * krot_rows_per_head + j * kBN;
-          for (int a = 0; a < 2; ++a) tma_load_2d(dst + a * kAtom, &tm_k, a * 64, ky, &full[st], pol);
-        } else {
-          for (int blk = 0; blk < 2; ++blk) {
-            const int b = 2 * j + blk;
-            const int lb = b < nb ? b : 2 * j;  // a block past the keys repeats a valid one
-            int phys = lb < p.max_blocks ? row[lb] : -1;
-            if (phys < 0 || phys >= p.n_phys) {
-              if (p.status) atomicOr(p.status, kStatusBadPageEntry);
-              phys = 0;
+      const uint32_t stages = is_k ? kStagesK : kStagesV;
+      uint32_t g = 0;
+      Item it;
+      for (int L = next_item(p, blockIdx.x, n_items, n_qt, ppt, it); L < n_items && !*s_abort;
+           L = next_item(p, L + gridDim.x, n_items, n_qt, ppt, it)) {
+        const int32_t* row = p.page_table + static_cast<int64_t>(it.s) * p.max_blocks;
+        for (int j = 0; j < it.n_tiles; ++j, ++g) {
+          const uint32_t st = g % stages;
+          if (g >= stages && !mbar_wait(&empty[st], ((g / stages) - 1) & 1)) {
+            fail(kStatusWaitTimeout);
+            break;
+          }
+          mbar_arrive_expect_tx(&full[st], kTile);
+          uint8_t* dst = ring + st * kTile;
+          if (is_k) {
+            // rotated keys: rows (s, kvh, 128 j .. 128 j + 127) of the scratch
+            const int ky = (it.s * p.Hkv + it.kvh) * krot_rows_per_head + j * kBN;
+            for (int a = 0; a < 2; ++a) tma_load_2d(dst + a * kAtom, &tm_k, a * 64, ky, &full[st], pol);
+          } else {
+            for (int blk = 0; blk < 2; ++blk) {
+              const int b = 2 * j + blk;
+              const int lb = b < it.nb ? b : 2 * j;  // a block past the keys repeats a valid one
+              int phys = lb < p.max_blocks ? row[lb] : -1;
+              if (phys < 0 || phys >= p.n_phys) {
+                if (p.status) atomicOr(p.status, kStatusBadPageEntry);
+                phys = 0;
+              }
+              const int y = (phys * p.Hkv + it.kvh) * kBlock;
+              for (int a = 0; a < 2; ++a)
+                tma_load_2d(dst + a * kAtom + blk * (kAtom / 2), &tm_v, a * 64, y, &full[st], pol);
             }
-            const int y = (phys * p.Hkv + kvh) * kBlock;
-            for (int a = 0; a < 2; ++a)
-              tma_load_2d(dst + a * kAtom + blk * (kAtom / 2), &tm_v, a * 64, y, &full[st], pol);
           }
         }
       }
@@ -263,15 +356,19 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t idesc_s = umma_idesc_f16(Elem<T>::kBf16, kBM, kBN, false, false);
       const uint32_t idesc_pv = umma_idesc_f16(Elem<T>::kBf16, kBM, kHD, false, true);
       const uint32_t q_addr = smem_u32(smem + kOffQ);
-      // O_h += P_h V_h for both key halves of tile jj; each half starts as soon
-      // as its own softmax warps have stored P_h. P_h is the A operand in TMEM:
-      // 32 columns of packed pairs over the first half of the half's S columns.
-      auto issue_pv = [&](int jj) -> bool {
-        const int b = jj & 1, vs = jj % kStages;
-        if (!mbar_wait(&bars->v_full[vs], (jj / kStages) & 1)) return false;
+      uint32_t g = 0, done = 0;
+      // O_h += P_h V_h for both key halves of global tile gg; each half starts
+      // as soon as its own softmax warps have stored P_h. P_h is the A operand
+      // in TMEM: 32 columns of packed pairs over the first half of the half's
+      // S columns. The first PV of an item overwrites O_h, so it waits until
+      // the previous item's epilogue has read O (o_free).
+      auto issue_pv = [&](uint32_t gg, bool first) -> bool {
+        const uint32_t b = gg & 1, vs = gg % kStagesV;
+        if (!mbar_wait(&bars->v_full[vs], (gg / kStagesV) & 1)) return false;
+        if (first && done > 0 && !mbar_wait(&bars->o_free, (done - 1) & 1)) return false;
         const uint32_t v_addr = smem_u32(smem + kOffV + vs * kTile);
         for (int h = 0; h < 2; ++h) {
-          if (!mbar_wait(&bars->p_ready[b][h], (jj >> 1) & 1)) return false;
+          if (!mbar_wait(&bars->p_ready[b][h], (gg >> 1) & 1)) return false;
           tc_fence_after();
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk) {
@@ -279,209 +376,195 @@ __global__ void __launch_bounds__(kThreads, 1)
             // MN-major, keys 64 h + 16 kk ..
             const uint64_t bd = umma_desc_sw128(v_addr + (4 * h + kk) * 2048, kAtom, 1024);
             umma_f16_ts(tmem + 256 + 128 * h, tmem + b * 128 + 64 * h + 8 * kk, bd, idesc_pv,
-                        (jj > 0 || kk > 0) ? 1u : 0u);
+                        (first && kk == 0) ? 0u : 1u);
           }
           umma_commit(&bars->pv_done[b][h]);
         }
         umma_commit(&bars->v_empty[vs]);
         return true;
       };
-      // Issue order S_0, S_1, PV_0, S_2, PV_1, ...: S_{j+2} overwrites the
-      // TMEM buffer of S_j / P_j only after PV_j was issued (which waited for
-      // both halves of P_j, hence for their loads of S_j), and tcgen05.mma
-      // operations of one thread execute in issue order.
-      bool ok = mbar_wait(&bars->q_ready, 0);
-      tc_fence_after();
-      for (int j = 0; j < n_tiles && ok; ++j) {
-        const int st = j % kStages;
-        if (!mbar_wait(&bars->k_full[st], (j / kStages) & 1)) {
+      // Issue order S_0, S_1, PV_0, S_2, PV_1, ... across items: S_{g+2}
+      // overwrites the TMEM buffer of S_g / P_g only after PV_g was issued
+      // (which waited for both halves of P_g, hence for their loads of S_g),
+      // and tcgen05.mma operations of one thread execute in issue order.
+      bool ok = true;
+      Item it;
+      for (int L = next_item(p, blockIdx.x, n_items, n_qt, ppt, it); L < n_items && ok && !*s_abort;
+           L = next_item(p, L + gridDim.x, n_items, n_qt, ppt, it)) {
+        if (!mbar_wait(&bars->q_ready, done & 1)) {  // this item's Q tile is in shared memory
           ok = false;
           break;
         }
         tc_fence_after();
-        const uint32_t k_addr = smem_u32(smem + kOffK + st * kTile);
+        for (int j = 0; j < it.n_tiles && ok; ++j) {
+          const uint32_t gg = g + j, st = gg % kStagesK;
+          if (!mbar_wait(&bars->k_full[st], (gg / kStagesK) & 1)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t k_addr = smem_u32(smem + kOffK + st * kTile);
 #pragma unroll
-        for (int kk = 0; kk < kHD / 16; ++kk) {
-          const uint64_t ad = umma_desc_sw128(q_addr + (kk >> 2) * kAtom + (kk & 3) * 32, 16, 1024);
-          const uint64_t bd = umma_desc_sw128(k_addr + (kk >> 2) * kAtom + (kk & 3) * 32, 16, 1024);
-          umma_f16_ss(tmem + (j & 1) * 128, ad, bd, idesc_s, kk > 0 ? 1u : 0u);
+          for (int kk = 0; kk < kHD / 16; ++kk) {
+            const uint64_t ad = umma_desc_sw128(q_addr + (kk >> 2) * kAtom + (kk & 3) * 32, 16, 1024);
+            const uint64_t bd = umma_desc_sw128(k_addr + (kk >> 2) * kAtom + (kk & 3) * 32, 16, 1024);
+            umma_f16_ss(tmem + (gg & 1) * 128, ad, bd, idesc_s, kk > 0 ? 1u : 0u);
+          }
+          umma_commit(&bars->s_full[gg & 1]);
+          umma_commit(&bars->k_empty[st]);  // K is free as soon as S is done
+          if (j >= 1 && !issue_pv(gg - 1, j == 1)) ok = false;
         }
-        umma_commit(&bars->s_full[j & 1]);
-        umma_commit(&bars->k_empty[st]);  // K_j is free as soon as S_j is done
-        if (j >= 1 && !issue_pv(j - 1)) ok = false;
+        if (ok) ok = issue_pv(g + it.n_tiles - 1, it.n_tiles == 1);
+        g += it.n_tiles;
+        ++done;
       }
-      if (ok && n_tiles > 0) ok = issue_pv(n_tiles - 1);
       if (!ok) fail(kStatusWaitTimeout);
     }
   } else {
     // ------------------------------ softmax warps 0-7 ------------------------------
     const int quarter = warp & 3, h = warp >> 2;  // TMEM lane quarter, key half
     const int r = quarter * 32 + lane;            // TMEM lane == query row
-    const int i = r % ppt;
-    const bool live = i < rows_valid;
-    const int pos = q0 + i;
-    {
-      // The query tile, rotated and scaled by softmax_scale * log2(e), into the
-      // swizzled Q buffer. Row R is head kvh*G + R / ppt at position
-      // q0 + R % ppt; unit u = (R, c) rotates the pairs (d, d + 64) for
-      // d in [8c, 8c + 8). Eight consecutive threads take the 8 units of one
-      // row, so each warp-wide load reads 4 contiguous row segments.
-      const int half = kHD / 2;
-      const int tid = threadIdx.x;  // 0 .. 255
-      uint8_t* qs = smem + kOffQ;
-      uint4 lo[4], hi[4];
-      float4 cs[8], sn[8];
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {  // all loads first, so their latencies overlap
-        const int u = tid + kSoftmaxThreads * k, R = u >> 3, c = u & 7;
-        const int iR = R % ppt, posR = q0 + iR;
-        lo[k] = hi[k] = make_uint4(0, 0, 0, 0);
-        cs[2 * k] = cs[2 * k + 1] = make_float4(1.f, 1.f, 1.f, 1.f);
-        sn[2 * k] = sn[2 * k + 1] = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (iR < rows_valid) {
-          const T* qrow = static_cast<const T*>(p.q) +
-                          ((static_cast<int64_t>(s) * p.Hq + kvh * G + R / ppt) * p.Lq + qt * ppt + iR) * kHD;
-          lo[k] = *reinterpret_cast<const uint4*>(qrow + 8 * c);
-          hi[k] = *reinterpret_cast<const uint4*>(qrow + half + 8 * c);
-          if (posR < p.max_pos) {
-            const float4* cr = reinterpret_cast<const float4*>(p.cos + static_cast<int64_t>(posR) * half + 8 * c);
-            const float4* sr = reinterpret_cast<const float4*>(p.sin + static_cast<int64_t>(posR) * half + 8 * c);
-            cs[2 * k] = cr[0];
-            cs[2 * k + 1] = cr[1];
-            sn[2 * k] = sr[0];
-            sn[2 * k + 1] = sr[1];
-          }
-        }
-      }
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        const int u = tid + kSoftmaxThreads * k, R = u >> 3, c = u & 7;
-        rope8<T>(lo[k], hi[k], reinterpret_cast<const float*>(&cs[2 * k]),
-                 reinterpret_cast<const float*>(&sn[2 * k]), p.scale_log2);
-        *reinterpret_cast<uint4*>(qs + sw_off(R, c)) = lo[k];
-        *reinterpret_cast<uint4*>(qs + kAtom + sw_off(R, c)) = hi[k];
-      }
+    const int tid = threadIdx.x;                  // 0 .. 255
+    const uint32_t lane_addr = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
+    const uint32_t o_col = 256 + 128 * h;  // this half's accumulator O_h
+    float2* ml = reinterpret_cast<float2*>(smem + kOffMl);  // [half][row]: (m_h, l_h)
+    uint8_t* stage = smem + kOffStage + warp * (32 * 128);
+    uint32_t g = 0, done = 0;
+    bool ok = true;
+    Item it, nx;
+    int L = next_item(p, blockIdx.x, n_items, n_qt, ppt, it);
+    QTile<T> qn;
+    if (L < n_items) {
+      qn.load(p, it, ppt, tid);
+      qn.store(smem + kOffQ, p.scale_log2, tid);
       fence_proxy_async_smem();
       mbar_arrive(&bars->q_ready);
     }
-    const int kmax_row = !live ? 0 : (p.causal ? min(seq_len, pos + 1) : seq_len);
-    const uint32_t lane_addr = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
-    const uint32_t o_col = 256 + 128 * h;  // this half's accumulator O_h
-    float m_ref = -INFINITY, l = 0.f;
-    bool ok = true;
-    for (int j = 0; j < n_tiles; ++j) {
-      const int sb = j & 1;
-      // Waits before warp-collective tcgen05 loads are made warp-uniform.
-      if (!__all_sync(0xffffffffu, mbar_wait(&bars->s_full[sb], (j >> 1) & 1))) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      // One pass over TMEM: this half's 64 scores of the row.
-      uint32_t sr[2][32];
-      tmem_ld32(lane_addr + sb * 128 + 64 * h, sr[0]);
-      tmem_ld32(lane_addr + sb * 128 + 64 * h + 32, sr[1]);
-      tmem_wait_ld();
+    while (L < n_items) {
+      const int i = r % ppt;
+      const bool live = i < it.rows_valid;
+      const int pos = it.q0 + i;
+      const int kmax_row = !live ? 0 : (p.causal ? min(it.seq_len, pos + 1) : it.seq_len);
+      const int n = it.n_tiles;
+      float m_ref = -INFINITY, l = 0.f;
+      for (int j = 0; j < n && ok; ++j) {
+        const uint32_t gg = g + j, sb = gg & 1;
+        // Waits before warp-collective tcgen05 loads are made warp-uniform.
+        if (!__all_sync(0xffffffffu, mbar_wait(&bars->s_full[sb], (gg >> 1) & 1))) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        // One pass over TMEM: this half's 64 scores of the row.
+        uint32_t sr[2][32];
+        tmem_ld32(lane_addr + sb * 128 + 64 * h, sr[0]);
+        tmem_ld32(lane_addr + sb * 128 + 64 * h + 32, sr[1]);
+        tmem_wait_ld();
 
-      const int base_key = j * kBN + 64 * h;
-      // Halves that lie wholly below every row's key limit skip the per-key masks.
-      const bool full = __all_sync(0xffffffffu, base_key + 64 <= kmax_row);
-      if (!full) {
+        const int base_key = j * kBN + 64 * h;
+        // Halves that lie wholly below every row's key limit skip the per-key masks.
+        const bool full = __all_sync(0xffffffffu, base_key + 64 <= kmax_row);
+        if (!full) {
 #pragma unroll
-        for (int c2 = 0; c2 < 2; ++c2)
+          for (int c2 = 0; c2 < 2; ++c2)
 #pragma unroll
-          for (int e = 0; e < 32; ++e)
-            if (base_key + c2 * 32 + e >= kmax_row) sr[c2][e] = __float_as_uint(-INFINITY);
-      }
-      // Max over the 64 scores: three-input max in 4 independent chains.
-      float mp[4];
+            for (int e = 0; e < 32; ++e)
+              if (base_key + c2 * 32 + e >= kmax_row) sr[c2][e] = __float_as_uint(-INFINITY);
+        }
+        // Max over the 64 scores: three-input max in 4 independent chains.
+        float mp[4];
 #pragma unroll
-      for (int k = 0; k < 4; ++k) mp[k] = __uint_as_float(sr[0][k]);
+        for (int k = 0; k < 4; ++k) mp[k] = __uint_as_float(sr[0][k]);
 #pragma unroll
-      for (int t = 0; t < 30; ++t)
-        mp[t & 3] = max3f(mp[t & 3], __uint_as_float(sr[(4 + 2 * t) >> 5][(4 + 2 * t) & 31]),
-                          __uint_as_float(sr[(5 + 2 * t) >> 5][(5 + 2 * t) & 31]));
-      const float mx = max3f(mp[0], mp[1], fmaxf(mp[2], mp[3]));
-      const bool grow = mx > m_ref + kRescaleLog2 || (m_ref == -INFINITY && mx != -INFINITY);
-      const float m_new = grow ? mx : m_ref;
-      const float factor = (grow && m_ref != -INFINITY) ? fast_exp2(m_ref - m_new) : 1.f;
-      // O_h may only be rescaled once PV_{j-1} is done. (PV_{j-2}, the last
-      // reader of this TMEM buffer, finished before S_j did.)
-      const bool rescale = j >= 1 && __any_sync(0xffffffffu, factor != 1.f);
-      if (rescale &&
-          !__all_sync(0xffffffffu, mbar_wait(&bars->pv_done[sb ^ 1][h], ((j - 1) >> 1) & 1))) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      if (rescale) {
+        for (int t = 0; t < 30; ++t)
+          mp[t & 3] = max3f(mp[t & 3], __uint_as_float(sr[(4 + 2 * t) >> 5][(4 + 2 * t) & 31]),
+                            __uint_as_float(sr[(5 + 2 * t) >> 5][(5 + 2 * t) & 31]));
+        const float mx = max3f(mp[0], mp[1], fmaxf(mp[2], mp[3]));
+        const bool grow = mx > m_ref + kRescaleLog2 || (m_ref == -INFINITY && mx != -INFINITY);
+        const float m_new = grow ? mx : m_ref;
+        const float factor = (grow && m_ref != -INFINITY) ? fast_exp2(m_ref - m_new) : 1.f;
+        // O_h may only be rescaled once PV of the previous tile is done. (PV of
+        // tile gg - 2, the last reader of this TMEM buffer, finished before S
+        // of tile gg did.)
+        const bool rescale = j >= 1 && __any_sync(0xffffffffu, factor != 1.f);
+        if (rescale &&
+            !__all_sync(0xffffffffu, mbar_wait(&bars->pv_done[sb ^ 1][h], ((gg - 1) >> 1) & 1))) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        if (rescale) {
 #pragma unroll
-        for (int c4 = 0; c4 < 4; ++c4) {
-          uint32_t raw[32];
-          tmem_ld32(lane_addr + o_col + c4 * 32, raw);
-          tmem_wait_ld();
+          for (int c4 = 0; c4 < 4; ++c4) {
+            uint32_t raw[32];
+            tmem_ld32(lane_addr + o_col + c4 * 32, raw);
+            tmem_wait_ld();
 #pragma unroll
-          for (int e = 0; e < 32; ++e) raw[e] = __float_as_uint(__uint_as_float(raw[e]) * factor);
-          tmem_st32(lane_addr + o_col + c4 * 32, raw);
+            for (int e = 0; e < 32; ++e) raw[e] = __float_as_uint(__uint_as_float(raw[e]) * factor);
+            tmem_st32(lane_addr + o_col + c4 * 32, raw);
+          }
+          tmem_wait_st();
+        }
+        l *= factor;
+        m_ref = m_new;
+        const float base = m_ref == -INFINITY ? 0.f : m_ref;
+        // P = exp2(S - max), packed to bf16/fp16 pairs and stored over the first
+        // 32 of this half's 64 S columns (already in registers), where the PV
+        // MMA reads it. In halves without masked keys kPolyPairs pairs of every
+        // 8 keys use the FMA-pipe polynomial; masked halves use ex2 throughout,
+        // so masked keys (-inf) give exactly 0. Packed f32x2 subtraction and 4
+        // partial row sums.
+        const uint64_t base2 = f2pack(base, base);
+        uint64_t lp[4] = {0, 0, 0, 0};
+        uint32_t pk[32];
+#pragma unroll
+        for (int c8 = 0; c8 < 8; ++c8) {
+#pragma unroll
+          for (int e2 = 0; e2 < 4; ++e2) {
+            const uint32_t* v = &sr[c8 >> 2][(c8 & 3) * 8 + 2 * e2];
+            const uint64_t x = f2sub(f2pack(__uint_as_float(v[0]), __uint_as_float(v[1])), base2);
+            const float2 xf = f2unpack(x);
+            uint64_t pv;
+            if (full && e2 < kPolyPairs)
+              pv = exp2_poly2(f2pack(fmaxf(xf.x, -126.f), fmaxf(xf.y, -126.f)));
+            else
+              pv = f2pack(fast_exp2(xf.x), fast_exp2(xf.y));
+            lp[e2] = f2add(lp[e2], pv);
+            const float2 pf = f2unpack(pv);
+            pk[c8 * 4 + e2] = Elem<T>::from2(pf.x, pf.y);
+          }
+        }
+        tmem_st32(lane_addr + sb * 128 + 64 * h, pk);
+        {
+          const float2 a = f2unpack(f2add(f2add(lp[0], lp[1]), f2add(lp[2], lp[3])));
+          l += a.x + a.y;
         }
         tmem_wait_st();
+        tc_fence_before();
+        mbar_arrive(&bars->p_ready[sb][h]);
       }
-      l *= factor;
-      m_ref = m_new;
-      const float base = m_ref == -INFINITY ? 0.f : m_ref;
-      // P = exp2(S - max), packed to bf16/fp16 pairs and stored over the first
-      // 32 of this half's 64 S columns (already in registers), where the PV
-      // MMA reads it. In halves without masked keys kPolyPairs pairs of every
-      // 8 keys use the FMA-pipe polynomial; masked halves use ex2 throughout,
-      // so masked keys (-inf) give exactly 0. Packed f32x2 subtraction and 4
-      // partial row sums.
-      const uint64_t base2 = f2pack(base, base);
-      uint64_t lp[4] = {0, 0, 0, 0};
-      uint32_t pk[32];
-#pragma unroll
-      for (int c8 = 0; c8 < 8; ++c8) {
-#pragma unroll
-        for (int e2 = 0; e2 < 4; ++e2) {
-          const uint32_t* v = &sr[c8 >> 2][(c8 & 3) * 8 + 2 * e2];
-          const uint64_t x = f2sub(f2pack(__uint_as_float(v[0]), __uint_as_float(v[1])), base2);
-          const float2 xf = f2unpack(x);
-          uint64_t pv;
-          if (full && e2 < kPolyPairs)
-            pv = exp2_poly2(f2pack(fmaxf(xf.x, -126.f), fmaxf(xf.y, -126.f)));
-          else
-            pv = f2pack(fast_exp2(xf.x), fast_exp2(xf.y));
-          lp[e2] = f2add(lp[e2], pv);
-          const float2 pf = f2unpack(pv);
-          pk[c8 * 4 + e2] = Elem<T>::from2(pf.x, pf.y);
-        }
+      if (!ok) break;
+      // Next item's query tile: issue its loads now, so they land while this
+      // item's epilogue runs. Without a next item nothing is loaded, and the
+      // store below only fills the free Q buffer with zeros (no MMA reads it).
+      const int Ln = next_item(p, L + gridDim.x, n_items, n_qt, ppt, nx);
+      if (Ln >= n_items) nx.rows_valid = 0;
+      qn.load(p, nx, ppt, tid);
+
+      // ---- epilogue: O_h is final once this half's last two PV steps are done.
+      for (int t = n >= 2 ? n - 2 : n - 1; t < n && ok; ++t) {
+        const uint32_t gg = g + t;
+        if (!__all_sync(0xffffffffu, mbar_wait(&bars->pv_done[gg & 1][h], (gg >> 1) & 1))) ok = false;
       }
-      tmem_st32(lane_addr + sb * 128 + 64 * h, pk);
-      {
-        const float2 a = f2unpack(f2add(f2add(lp[0], lp[1]), f2add(lp[2], lp[3])));
-        l += a.x + a.y;
-      }
-      tmem_wait_st();
+      // Merge the halves: every softmax thread arrives exactly once per item,
+      // also after a failed wait, so the other warps' bounded waits end.
+      ml[h * kBM + r] = make_float2(m_ref, l);
       tc_fence_before();
-      mbar_arrive(&bars->p_ready[sb][h]);
-    }
-    // O_h is final once this half's last two PV steps (one per P buffer) are done.
-    if (ok && n_tiles >= 2 &&
-        !__all_sync(0xffffffffu,
-                    mbar_wait(&bars->pv_done[(n_tiles - 2) & 1][h], ((n_tiles - 2) >> 1) & 1)))
-      ok = false;
-    if (ok && n_tiles >= 1 &&
-        !__all_sync(0xffffffffu,
-                    mbar_wait(&bars->pv_done[(n_tiles - 1) & 1][h], ((n_tiles - 1) >> 1) & 1)))
-      ok = false;
-    // Merge the halves. (m_h, l_h) go through the Q tile, which no MMA reads
-    // any more once the last S tile has been observed; every softmax thread
-    // arrives on the merge barrier exactly once, also after a failed wait.
-    float2* ml = reinterpret_cast<float2*>(smem + kOffQ);  // [half][row]
-    ml[h * kBM + r] = make_float2(m_ref, l);
-    tc_fence_before();
-    mbar_arrive(&bars->merge);
-    if (!ok) fail(kStatusWaitTimeout);
-    if (ok && __all_sync(0xffffffffu, mbar_wait(&bars->merge, 0))) {
+      mbar_arrive(&bars->merge);
+      if (!ok || !__all_sync(0xffffffffu, mbar_wait(&bars->merge, done & 1))) {
+        ok = false;
+        break;
+      }
       tc_fence_after();
       const float2 a0 = ml[r], a1 = ml[kBM + r];
       const float m = fmaxf(a0.x, a1.x);
@@ -490,19 +573,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float den = w0 * a0.y + w1 * a1.y;
       const float inv = den > 0.f ? 1.f / den : 0.f;
       const float s0 = w0 * inv, s1 = w1 * inv;
-      // Output columns [64 h, 64 h + 64) of this warp's 32 rows, staged in the
-      // first K stage (free: every S MMA is done) as [32 rows][8 x 16 B
-      // chunks] with an XOR swizzle, then stored 4 rows per warp-wide
-      // instruction.
-      uint8_t* stage = smem + kOffK + warp * (32 * 128);
+      // Output columns [64 h, 64 h + 64) of this warp's 32 rows, staged as
+      // [32 rows][8 x 16 B chunks] with an XOR swizzle, then stored 4 rows per
+      // warp-wide instruction.
 #pragma unroll
-      for (int c2 = 0; c2 < 2; ++c2) {
-        uint32_t o0[32], o1[32];
-        tmem_ld32(lane_addr + 256 + 64 * h + c2 * 32, o0);
-        tmem_ld32(lane_addr + 384 + 64 * h + c2 * 32, o1);
+      for (int c4 = 0; c4 < 4; ++c4) {
+        uint32_t o0[16], o1[16];
+        tmem_ld16(lane_addr + 256 + 64 * h + c4 * 16, o0);
+        tmem_ld16(lane_addr + 384 + 64 * h + c4 * 16, o1);
         tmem_wait_ld();
 #pragma unroll
-        for (int e8 = 0; e8 < 4; ++e8) {
+        for (int e8 = 0; e8 < 2; ++e8) {
           float o[8];
 #pragma unroll
           for (int e = 0; e < 8; ++e)
@@ -512,25 +593,36 @@ __global__ void __launch_bounds__(kThreads, 1)
           w.y = Elem<T>::from2(o[2], o[3]);
           w.z = Elem<T>::from2(o[4], o[5]);
           w.w = Elem<T>::from2(o[6], o[7]);
-          const int chunk = c2 * 4 + e8;
+          const int chunk = c4 * 2 + e8;
           *reinterpret_cast<uint4*>(stage + lane * 128 + ((chunk ^ (lane & 7)) << 4)) = w;
         }
       }
+      tc_fence_before();
+      mbar_arrive(&bars->o_free);  // O may take the next item's first PV
       __syncwarp();
 #pragma unroll
-      for (int it = 0; it < 8; ++it) {
-        const int rl = it * 4 + (lane >> 3), chunk = lane & 7;
+      for (int itr = 0; itr < 8; ++itr) {
+        const int rl = itr * 4 + (lane >> 3), chunk = lane & 7;
         const int R = quarter * 32 + rl, iR = R % ppt;
-        if (iR < rows_valid) {
+        if (iR < it.rows_valid) {
           T* orow = static_cast<T*>(p.out) +
-                    ((static_cast<int64_t>(s) * p.Hq + kvh * G + R / ppt) * p.Lq + qt * ppt + iR) * kHD;
+                    ((static_cast<int64_t>(it.s) * p.Hq + it.kvh * G + R / ppt) * p.Lq +
+                     it.qt * ppt + iR) * kHD;
           *reinterpret_cast<uint4*>(orow + 64 * h + chunk * 8) =
               *reinterpret_cast<const uint4*>(stage + rl * 128 + ((chunk ^ (rl & 7)) << 4));
         }
       }
-    } else if (ok) {
-      fail(kStatusWaitTimeout);
+      __syncwarp();
+      g += n;
+      ++done;
+      L = Ln;
+      it = nx;
+      // Every S MMA of this item is done, so the Q buffer is free.
+      qn.store(smem + kOffQ, p.scale_log2, tid);
+      fence_proxy_async_smem();
+      mbar_arrive(&bars->q_ready);
     }
+    if (!ok) fail(kStatusWaitTimeout);
   }
 
   tc_fence_before();
@@ -610,8 +702,16 @@ cudaError_t launch_prefill_tc(const RowsParams& p, int dtype, cudaStream_t strea
     return cudaErrorInvalidValue;
   cudaError_t e = launch_rope_k(p, dtype, p.workspace, p.max_blocks, stream);
   if (e != cudaSuccess) return e;
+  // Persistent CTAs: one per SM (shared memory allows no second), each walking
+  // items c, c + grid, ...
   const int ppt = kBM / p.G;
-  dim3 grid((p.Lq + ppt - 1) / ppt, p.Hkv, p.S);
+  const int64_t n_items = static_cast<int64_t>((p.Lq + ppt - 1) / ppt) * p.Hkv * p.S;
+  if (n_items >= (int64_t(1) << 31)) return cudaErrorInvalidValue;
+  int dev = 0, sms = 0;
+  e = cudaGetDevice(&dev);
+  if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (e != cudaSuccess) return e;
+  dim3 grid(static_cast<unsigned>(std::min<int64_t>(n_items, sms)));
   if (dtype == 2) {
     auto kernel = prefill_tc_kernel<__nv_bfloat16>;
     e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
