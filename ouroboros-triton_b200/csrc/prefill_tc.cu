@@ -16,23 +16,23 @@
 //               (one box of 128 keys per atom), refilled as soon as S_j is
 //               done; V tiles from the paged cache (boxes of 64 keys, one per
 //               block), refilled when PV_j is done
-//   warp 9      TMEM owner and MMA issuer: S_j = Q K_j^T into one of two
-//               128-column TMEM buffers, then O_h += P_{j-1,h} V_{j-1,h} for
-//               each key half h (V as an MN-major operand), tcgen05.commit to
-//               mbarriers
-//   warps 0-7   RoPE on the query tile (scaled by softmax_scale * log2 e),
-//               then softmax. Warp w owns TMEM lanes 32 (w % 4) .. +31 (one
-//               query row per thread) and key half h = w / 4 of every tile
-//               (64 keys): each half keeps its own running max m_h, row sum
-//               l_h and accumulator O_h, so the two warps sharing a row never
-//               wait on each other inside the key loop. Per tile: S from TMEM
-//               in one pass, causal / length masks, lazy rescaling of O_h
-//               (only when m_h grows by more than 2^8), P as bf16/fp16 into
-//               the half's atom of a swizzled shared tile. The epilogue merges
-//               the halves: O = (2^(m_0-m) O_0 + 2^(m_1-m) O_1) /
-//               (2^(m_0-m) l_0 + 2^(m_1-m) l_1), m = max(m_0, m_1), each warp
-//               writing 64 of the row's 128 output columns.
-// TMEM columns: S buffers at 0 and 128, O_0 at 256, O_1 at 384 (512 allocated).
+//   warp 9      TMEM owner and MMA issuer: S_j = Q K_j^T into TMEM buffer
+//               j % 2, then O_{j%2} += P_j V_j with P_j read from TMEM (V as an
+//               MN-major operand), tcgen05.commit to mbarriers
+//   warps 0-7   softmax. Warp w owns TMEM lanes 32 (w % 4) .. +31 (one query
+//               row per thread) and the tiles of parity w / 4: each parity keeps
+//               its own running max m, row sum l and accumulator O, so the two
+//               warps of a row never wait on each other inside the key loop,
+//               and since S of tile j + 1 is ready half a period after S of
+//               tile j, one warp's max pass overlaps the other's exponentials
+//               on the shared MUFU. Per tile: max over the 128 scores (two TMEM
+//               passes), lazy rescaling of O (only when m grows by more than
+//               2^8), P = exp2(S - m) as bf16/fp16 pairs stored over the tile's
+//               own S columns. The epilogue merges the parities:
+//               O = (2^(m_0-m) O_0 + 2^(m_1-m) O_1) / (2^(m_0-m) l_0 + 2^(m_1-m) l_1),
+//               m = max(m_0, m_1), each warp writing 64 of the row's 128 output
+//               columns; it also rotates the next item's query tile.
+// TMEM columns: S/P buffers at 0 and 128, O_0 at 256, O_1 at 384 (512 allocated).
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -59,12 +59,17 @@ constexpr int kSoftmaxThreads = kSoftmaxWarps * 32;
 constexpr int kWarpK = 8, kWarpMma = 9, kWarpV = 10;  // K loads, MMA / TMEM, V loads
 constexpr int kThreads = 11 * 32;
 constexpr float kRescaleLog2 = 8.0f;
-// Pairs of every 8 keys whose exponential goes through exp2_poly2 instead of
-// MUFU ex2 (0..4). Measured slower than ex2 alone on the config-4 workload
-// while the loop is bound by shared-memory traffic, so it is off.
+// Pairs of every 4 key pairs whose exponential goes through exp2_poly2 instead
+// of MUFU ex2 (0..4).
 constexpr int kPolyPairs = 0;
 
-constexpr int kStagesK = 2, kStagesV = 2;  // ring depths (3 measured no faster)
+// Two-stage K and V rings (three measured no faster). With two stages the K
+// slot of tile j is free exactly when S_j is done and the V slot exactly when
+// PV_j is done, so the producers wait on s_full / pv_done instead of separate
+// "empty" barriers: every tcgen05.commit costs the MMA thread as much issue
+// time as an MMA.
+constexpr int kStagesK = 2, kStagesV = 2;
+static_assert(kStagesK == 2 && kStagesV == 2, "ring slots are tied to the S/P buffer parity");
 
 // Shared-memory map (offsets from a 1024-byte aligned base). P never touches
 // shared memory: it is written over its own S columns in TMEM and read from
@@ -81,9 +86,9 @@ constexpr int kSmemBytes = kOffBar + 256 + 1024;
 // barrier is at most one phase past the awaited one, and per-buffer barriers
 // keep each waiter within that window.
 struct Bars {
-  uint64_t k_full[kStagesK], k_empty[kStagesK], v_full[kStagesV], v_empty[kStagesV];
+  uint64_t k_full[kStagesK], v_full[kStagesV];
   uint64_t s_full[2];
-  uint64_t p_ready[2][2], pv_done[2][2];  // [S/P buffer][key half]
+  uint64_t p_ready[2], pv_done[2];       // per S/P buffer = tile parity
   uint64_t q_ready, merge, o_free;        // once per item
   uint32_t tmem_base;
   int32_t abort;
@@ -269,20 +274,14 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (threadIdx.x == 0) {
     *s_abort = 0;
-    for (int i = 0; i < kStagesK; ++i) {
+    for (int i = 0; i < 2; ++i) {
       mbar_init(&bars->k_full[i], 1);
-      mbar_init(&bars->k_empty[i], 1);
-    }
-    for (int i = 0; i < kStagesV; ++i) {
       mbar_init(&bars->v_full[i], 1);
-      mbar_init(&bars->v_empty[i], 1);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&bars->s_full[i], 1);
-      for (int h = 0; h < 2; ++h) {
-        mbar_init(&bars->p_ready[i][h], 128);
-        mbar_init(&bars->pv_done[i][h], 1);
-      }
+      mbar_init(&bars->p_ready[i], 128);
+      mbar_init(&bars->pv_done[i], 1);
     }
     mbar_init(&bars->q_ready, kSoftmaxThreads);
     mbar_init(&bars->merge, kSoftmaxThreads);
@@ -313,7 +312,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       tma_prefetch_desc(is_k ? &tm_k : &tm_v);
       const uint64_t pol = policy_evict_last();  // tiles are re-read by other CTAs
       uint64_t* full = is_k ? bars->k_full : bars->v_full;
-      uint64_t* empty = is_k ? bars->k_empty : bars->v_empty;
+      uint64_t* empty = is_k ? bars->s_full : bars->pv_done;  // slot g % 2 frees with tile g
       uint8_t* ring = smem + (is_k ? kOffK : kOffV);
       const uint32_t stages = is_k ? kStagesK : kStagesV;
       uint32_t g = 0;
@@ -355,38 +354,43 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       const uint32_t idesc_s = umma_idesc_f16(Elem<T>::kBf16, kBM, kBN, false, false);
       const uint32_t idesc_pv = umma_idesc_f16(Elem<T>::kBf16, kBM, kHD, false, true);
-      const uint32_t q_addr = smem_u32(smem + kOffQ);
+      // Shared-memory descriptors are computed once: a K step adds 32 B (K-major)
+      // or 2048 B (V, MN-major) to the 14-bit start-address field (units of 16 B),
+      // a ring slot adds kTile, an atom kAtom. Every tcgen05 instruction costs the
+      // issuing thread ~70 cycles, so nothing else sits between them.
+      const uint64_t q_desc = umma_desc_sw128(smem_u32(smem + kOffQ), 16, 1024);
+      const uint64_t k_desc = umma_desc_sw128(smem_u32(smem + kOffK), 16, 1024);
+      const uint64_t v_desc = umma_desc_sw128(smem_u32(smem + kOffV), kAtom, 1024);
+      constexpr uint64_t kSlot = kTile >> 4;
       uint32_t g = 0, done = 0;
-      // O_h += P_h V_h for both key halves of global tile gg; each half starts
-      // as soon as its own softmax warps have stored P_h. P_h is the A operand
-      // in TMEM: 32 columns of packed pairs over the first half of the half's
-      // S columns. The first PV of an item overwrites O_h, so it waits until
-      // the previous item's epilogue has read O (o_free).
-      auto issue_pv = [&](uint32_t gg, bool first) -> bool {
-        const uint32_t b = gg & 1, vs = gg % kStagesV;
-        if (!mbar_wait(&bars->v_full[vs], (gg / kStagesV) & 1)) return false;
-        if (first && done > 0 && !mbar_wait(&bars->o_free, (done - 1) & 1)) return false;
-        const uint32_t v_addr = smem_u32(smem + kOffV + vs * kTile);
-        for (int h = 0; h < 2; ++h) {
-          if (!mbar_wait(&bars->p_ready[b][h], (gg >> 1) & 1)) return false;
-          tc_fence_after();
+      // O_b += P V for global tile gg, b = gg % 2: the accumulator of the tile
+      // parity. P is the A operand in TMEM: 64 columns of packed pairs over the
+      // first half of the tile's S buffer. The first tile of each parity in an
+      // item overwrites its accumulator; the item's first PV waits until the
+      // previous item's epilogue has read O (o_free). The commit to pv_done also
+      // frees V slot b.
+      auto issue_pv = [&](uint32_t gg, uint32_t j) -> bool {
+        const uint32_t b = gg & 1;
+        if (!mbar_wait(&bars->v_full[b], (gg >> 1) & 1)) return false;
+        if (j == 0 && done > 0 && !mbar_wait(&bars->o_free, (done - 1) & 1)) return false;
+        if (!mbar_wait(&bars->p_ready[b], (gg >> 1) & 1)) return false;
+        tc_fence_after();  // P was stored to TMEM by the softmax threads
+        const uint64_t vd = v_desc + b * kSlot;
+        const uint32_t a_tmem = tmem + b * 128, d_tmem = tmem + 256 + 128 * b;
 #pragma unroll
-          for (int kk = 0; kk < 4; ++kk) {
-            // A = P [128 rows x 16 keys] (8 TMEM columns); B = V [16 keys x 128 d]
-            // MN-major, keys 64 h + 16 kk ..
-            const uint64_t bd = umma_desc_sw128(v_addr + (4 * h + kk) * 2048, kAtom, 1024);
-            umma_f16_ts(tmem + 256 + 128 * h, tmem + b * 128 + 64 * h + 8 * kk, bd, idesc_pv,
-                        (first && kk == 0) ? 0u : 1u);
-          }
-          umma_commit(&bars->pv_done[b][h]);
-        }
-        umma_commit(&bars->v_empty[vs]);
+        for (int kk = 0; kk < kBN / 16; ++kk)
+          // A = P [128 rows x 16 keys] (8 TMEM columns); B = V [16 keys x 128 d] MN-major
+          umma_f16_ts(d_tmem, a_tmem + 8 * kk, vd + kk * (2048 >> 4), idesc_pv,
+                      (j < 2 && kk == 0) ? 0u : 1u);
+        umma_commit(&bars->pv_done[b]);
         return true;
       };
       // Issue order S_0, S_1, PV_0, S_2, PV_1, ... across items: S_{g+2}
       // overwrites the TMEM buffer of S_g / P_g only after PV_g was issued
-      // (which waited for both halves of P_g, hence for their loads of S_g),
-      // and tcgen05.mma operations of one thread execute in issue order.
+      // (which waited for P_g, hence for the loads of S_g), and tcgen05.mma
+      // operations of one thread execute in issue order. Q and K reach the MMA
+      // through shared memory only (TMA, or stores fenced to the async proxy
+      // before q_ready), so their barrier waits need no tcgen05 fence.
       bool ok = true;
       Item it;
       for (int L = next_item(p, blockIdx.x, n_items, n_qt, ppt, it); L < n_items && ok && !*s_abort;
@@ -395,26 +399,22 @@ __global__ void __launch_bounds__(kThreads, 1)
           ok = false;
           break;
         }
-        tc_fence_after();
         for (int j = 0; j < it.n_tiles && ok; ++j) {
-          const uint32_t gg = g + j, st = gg % kStagesK;
-          if (!mbar_wait(&bars->k_full[st], (gg / kStagesK) & 1)) {
+          const uint32_t gg = g + j, b = gg & 1;
+          if (!mbar_wait(&bars->k_full[b], (gg >> 1) & 1)) {
             ok = false;
             break;
           }
-          tc_fence_after();
-          const uint32_t k_addr = smem_u32(smem + kOffK + st * kTile);
+          const uint64_t kd = k_desc + b * kSlot;
 #pragma unroll
           for (int kk = 0; kk < kHD / 16; ++kk) {
-            const uint64_t ad = umma_desc_sw128(q_addr + (kk >> 2) * kAtom + (kk & 3) * 32, 16, 1024);
-            const uint64_t bd = umma_desc_sw128(k_addr + (kk >> 2) * kAtom + (kk & 3) * 32, 16, 1024);
-            umma_f16_ss(tmem + (gg & 1) * 128, ad, bd, idesc_s, kk > 0 ? 1u : 0u);
+            const uint64_t step = (kk >> 2) * (kAtom >> 4) + (kk & 3) * (32 >> 4);
+            umma_f16_ss(tmem + b * 128, q_desc + step, kd + step, idesc_s, kk > 0 ? 1u : 0u);
           }
-          umma_commit(&bars->s_full[gg & 1]);
-          umma_commit(&bars->k_empty[st]);  // K is free as soon as S is done
-          if (j >= 1 && !issue_pv(gg - 1, j == 1)) ok = false;
+          umma_commit(&bars->s_full[b]);  // also frees K slot b
+          if (j >= 1 && !issue_pv(gg - 1, j - 1)) ok = false;
         }
-        if (ok) ok = issue_pv(g + it.n_tiles - 1, it.n_tiles == 1);
+        if (ok) ok = issue_pv(g + it.n_tiles - 1, it.n_tiles - 1);
         g += it.n_tiles;
         ++done;
       }
@@ -422,12 +422,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // ------------------------------ softmax warps 0-7 ------------------------------
-    const int quarter = warp & 3, h = warp >> 2;  // TMEM lane quarter, key half
-    const int r = quarter * 32 + lane;            // TMEM lane == query row
-    const int tid = threadIdx.x;                  // 0 .. 255
+    const int quarter = warp & 3, par = warp >> 2;  // TMEM lane quarter, tile parity
+    const int r = quarter * 32 + lane;              // TMEM lane == query row
+    const int tid = threadIdx.x;                    // 0 .. 255
     const uint32_t lane_addr = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
-    const uint32_t o_col = 256 + 128 * h;  // this half's accumulator O_h
-    float2* ml = reinterpret_cast<float2*>(smem + kOffMl);  // [half][row]: (m_h, l_h)
+    const uint32_t s_col = 128 * par;               // this parity's S / P buffer
+    const uint32_t o_col = 256 + 128 * par;         // this parity's accumulator
+    float2* ml = reinterpret_cast<float2*>(smem + kOffMl);  // [parity][row]: (m, l)
     uint8_t* stage = smem + kOffStage + warp * (32 * 128);
     uint32_t g = 0, done = 0;
     bool ok = true;
@@ -440,6 +441,44 @@ __global__ void __launch_bounds__(kThreads, 1)
       fence_proxy_async_smem();
       mbar_arrive(&bars->q_ready);
     }
+    // Masks 32 scores of keys key0 .. key0 + 31 and returns their max.
+    auto mask_max32 = [&](uint32_t (&v)[32], int key0, int kmax_row, bool full) -> float {
+      if (!full) {
+#pragma unroll
+        for (int e = 0; e < 32; ++e)
+          if (key0 + e >= kmax_row) v[e] = __float_as_uint(-INFINITY);
+      }
+      float mp[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) mp[k] = __uint_as_float(v[k]);
+#pragma unroll
+      for (int t = 0; t < 14; ++t)
+        mp[t & 3] = max3f(mp[t & 3], __uint_as_float(v[4 + 2 * t]), __uint_as_float(v[5 + 2 * t]));
+      return max3f(mp[0], mp[1], fmaxf(mp[2], mp[3]));
+    };
+    // P = exp2(S - base) for 64 keys held in two 32-column blocks, packed to
+    // bf16/fp16 pairs (32 TMEM columns); returns their sum. In tiles without
+    // masked keys kPolyPairs of every 4 pairs use the FMA-pipe polynomial;
+    // otherwise MUFU ex2 throughout, so masked keys (-inf) give exactly 0.
+    auto exp64 = [&](const uint32_t (&a)[32], const uint32_t (&b)[32], float base, bool full,
+                     uint32_t (&pk)[32]) -> float {
+      const uint64_t base2 = f2pack(base, base);
+      uint64_t lp[4] = {0, 0, 0, 0};
+#pragma unroll
+      for (int e2 = 0; e2 < 32; ++e2) {
+        const uint32_t* v = e2 < 16 ? &a[2 * e2] : &b[2 * e2 - 32];
+        const float2 xf =
+            f2unpack(f2sub(f2pack(__uint_as_float(v[0]), __uint_as_float(v[1])), base2));
+        const uint64_t pv = (full && (e2 & 3) < kPolyPairs)
+                                ? exp2_poly2(f2pack(fmaxf(xf.x, -126.f), fmaxf(xf.y, -126.f)))
+                                : f2pack(fast_exp2(xf.x), fast_exp2(xf.y));
+        lp[e2 & 3] = f2add(lp[e2 & 3], pv);
+        const float2 pf = f2unpack(pv);
+        pk[e2] = Elem<T>::from2(pf.x, pf.y);
+      }
+      const float2 t = f2unpack(f2add(f2add(lp[0], lp[1]), f2add(lp[2], lp[3])));
+      return t.x + t.y;
+    };
     while (L < n_items) {
       const int i = r % ppt;
       const bool live = i < it.rows_valid;
@@ -447,53 +486,36 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int kmax_row = !live ? 0 : (p.causal ? min(it.seq_len, pos + 1) : it.seq_len);
       const int n = it.n_tiles;
       float m_ref = -INFINITY, l = 0.f;
-      for (int j = 0; j < n && ok; ++j) {
-        const uint32_t gg = g + j, sb = gg & 1;
+      // This warp takes the item's tiles j with (g + j) % 2 == par.
+      const int j0 = static_cast<int>((g ^ static_cast<uint32_t>(par)) & 1);
+      for (int j = j0; j < n && ok; j += 2) {
+        const uint32_t gg = g + j;
         // Waits before warp-collective tcgen05 loads are made warp-uniform.
-        if (!__all_sync(0xffffffffu, mbar_wait(&bars->s_full[sb], (gg >> 1) & 1))) {
+        if (!__all_sync(0xffffffffu, mbar_wait(&bars->s_full[par], (gg >> 1) & 1))) {
           ok = false;
           break;
         }
         tc_fence_after();
-        // One pass over TMEM: this half's 64 scores of the row.
-        uint32_t sr[2][32];
-        tmem_ld32(lane_addr + sb * 128 + 64 * h, sr[0]);
-        tmem_ld32(lane_addr + sb * 128 + 64 * h + 32, sr[1]);
+        const int key0 = j * kBN;
+        // Tiles that lie wholly below every row's key limit skip the per-key masks.
+        const bool full = __all_sync(0xffffffffu, key0 + kBN <= kmax_row);
+        // Pass 1: row max over the 128 scores; keys 0..63 stay in registers.
+        uint32_t sa[32], sb[32];
+        tmem_ld32(lane_addr + s_col + 64, sa);
+        tmem_ld32(lane_addr + s_col + 96, sb);
         tmem_wait_ld();
-
-        const int base_key = j * kBN + 64 * h;
-        // Halves that lie wholly below every row's key limit skip the per-key masks.
-        const bool full = __all_sync(0xffffffffu, base_key + 64 <= kmax_row);
-        if (!full) {
-#pragma unroll
-          for (int c2 = 0; c2 < 2; ++c2)
-#pragma unroll
-            for (int e = 0; e < 32; ++e)
-              if (base_key + c2 * 32 + e >= kmax_row) sr[c2][e] = __float_as_uint(-INFINITY);
-        }
-        // Max over the 64 scores: three-input max in 4 independent chains.
-        float mp[4];
-#pragma unroll
-        for (int k = 0; k < 4; ++k) mp[k] = __uint_as_float(sr[0][k]);
-#pragma unroll
-        for (int t = 0; t < 30; ++t)
-          mp[t & 3] = max3f(mp[t & 3], __uint_as_float(sr[(4 + 2 * t) >> 5][(4 + 2 * t) & 31]),
-                            __uint_as_float(sr[(5 + 2 * t) >> 5][(5 + 2 * t) & 31]));
-        const float mx = max3f(mp[0], mp[1], fmaxf(mp[2], mp[3]));
+        float mx = fmaxf(mask_max32(sa, key0 + 64, kmax_row, full),
+                         mask_max32(sb, key0 + 96, kmax_row, full));
+        tmem_ld32(lane_addr + s_col, sa);
+        tmem_ld32(lane_addr + s_col + 32, sb);
+        tmem_wait_ld();
+        mx = max3f(mx, mask_max32(sa, key0, kmax_row, full), mask_max32(sb, key0 + 32, kmax_row, full));
         const bool grow = mx > m_ref + kRescaleLog2 || (m_ref == -INFINITY && mx != -INFINITY);
         const float m_new = grow ? mx : m_ref;
         const float factor = (grow && m_ref != -INFINITY) ? fast_exp2(m_ref - m_new) : 1.f;
-        // O_h may only be rescaled once PV of the previous tile is done. (PV of
-        // tile gg - 2, the last reader of this TMEM buffer, finished before S
-        // of tile gg did.)
-        const bool rescale = j >= 1 && __any_sync(0xffffffffu, factor != 1.f);
-        if (rescale &&
-            !__all_sync(0xffffffffu, mbar_wait(&bars->pv_done[sb ^ 1][h], ((gg - 1) >> 1) & 1))) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        if (rescale) {
+        // Rescale this parity's accumulator in TMEM. Its last PV (tile gg - 2)
+        // finished before S of tile gg did, so no wait is needed.
+        if (__any_sync(0xffffffffu, factor != 1.f)) {
 #pragma unroll
           for (int c4 = 0; c4 < 4; ++c4) {
             uint32_t raw[32];
@@ -503,45 +525,31 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int e = 0; e < 32; ++e) raw[e] = __float_as_uint(__uint_as_float(raw[e]) * factor);
             tmem_st32(lane_addr + o_col + c4 * 32, raw);
           }
-          tmem_wait_st();
         }
         l *= factor;
         m_ref = m_new;
         const float base = m_ref == -INFINITY ? 0.f : m_ref;
-        // P = exp2(S - max), packed to bf16/fp16 pairs and stored over the first
-        // 32 of this half's 64 S columns (already in registers), where the PV
-        // MMA reads it. In halves without masked keys kPolyPairs pairs of every
-        // 8 keys use the FMA-pipe polynomial; masked halves use ex2 throughout,
-        // so masked keys (-inf) give exactly 0. Packed f32x2 subtraction and 4
-        // partial row sums.
-        const uint64_t base2 = f2pack(base, base);
-        uint64_t lp[4] = {0, 0, 0, 0};
+        // Pass 2: P for keys 0..63 over S columns 0..31 (their scores are in
+        // registers), then keys 64..127 reloaded (columns 64..127, untouched)
+        // and stored over columns 32..63.
         uint32_t pk[32];
+        l += exp64(sa, sb, base, full, pk);
+        tmem_st32(lane_addr + s_col, pk);
+        tmem_ld32(lane_addr + s_col + 64, sa);
+        tmem_ld32(lane_addr + s_col + 96, sb);
+        tmem_wait_ld();
+        if (!full) {
 #pragma unroll
-        for (int c8 = 0; c8 < 8; ++c8) {
-#pragma unroll
-          for (int e2 = 0; e2 < 4; ++e2) {
-            const uint32_t* v = &sr[c8 >> 2][(c8 & 3) * 8 + 2 * e2];
-            const uint64_t x = f2sub(f2pack(__uint_as_float(v[0]), __uint_as_float(v[1])), base2);
-            const float2 xf = f2unpack(x);
-            uint64_t pv;
-            if (full && e2 < kPolyPairs)
-              pv = exp2_poly2(f2pack(fmaxf(xf.x, -126.f), fmaxf(xf.y, -126.f)));
-            else
-              pv = f2pack(fast_exp2(xf.x), fast_exp2(xf.y));
-            lp[e2] = f2add(lp[e2], pv);
-            const float2 pf = f2unpack(pv);
-            pk[c8 * 4 + e2] = Elem<T>::from2(pf.x, pf.y);
+          for (int e = 0; e < 32; ++e) {
+            if (key0 + 64 + e >= kmax_row) sa[e] = __float_as_uint(-INFINITY);
+            if (key0 + 96 + e >= kmax_row) sb[e] = __float_as_uint(-INFINITY);
           }
         }
-        tmem_st32(lane_addr + sb * 128 + 64 * h, pk);
-        {
-          const float2 a = f2unpack(f2add(f2add(lp[0], lp[1]), f2add(lp[2], lp[3])));
-          l += a.x + a.y;
-        }
+        l += exp64(sa, sb, base, full, pk);
+        tmem_st32(lane_addr + s_col + 32, pk);
         tmem_wait_st();
         tc_fence_before();
-        mbar_arrive(&bars->p_ready[sb][h]);
+        mbar_arrive(&bars->p_ready[par]);
       }
       if (!ok) break;
       // Next item's query tile: issue its loads now, so they land while this
@@ -551,14 +559,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (Ln >= n_items) nx.rows_valid = 0;
       qn.load(p, nx, ppt, tid);
 
-      // ---- epilogue: O_h is final once this half's last two PV steps are done.
-      for (int t = n >= 2 ? n - 2 : n - 1; t < n && ok; ++t) {
-        const uint32_t gg = g + t;
-        if (!__all_sync(0xffffffffu, mbar_wait(&bars->pv_done[gg & 1][h], (gg >> 1) & 1))) ok = false;
+      // ---- epilogue: this parity's accumulator is final once the PV of its
+      // last tile in the item is done (if it had one).
+      const int jl = ((n - 1 - j0) & 1) ? n - 2 : n - 1;  // last tile of this parity
+      if (jl >= 0) {
+        const uint32_t gg = g + jl;
+        if (!__all_sync(0xffffffffu, mbar_wait(&bars->pv_done[par], (gg >> 1) & 1))) ok = false;
       }
-      // Merge the halves: every softmax thread arrives exactly once per item,
+      // Merge the parities: every softmax thread arrives exactly once per item,
       // also after a failed wait, so the other warps' bounded waits end.
-      ml[h * kBM + r] = make_float2(m_ref, l);
+      ml[par * kBM + r] = make_float2(m_ref, l);
       tc_fence_before();
       mbar_arrive(&bars->merge);
       if (!ok || !__all_sync(0xffffffffu, mbar_wait(&bars->merge, done & 1))) {
@@ -568,26 +578,32 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const float2 a0 = ml[r], a1 = ml[kBM + r];
       const float m = fmaxf(a0.x, a1.x);
-      const float w0 = a0.x == -INFINITY ? 0.f : fast_exp2(a0.x - m);
-      const float w1 = a1.x == -INFINITY ? 0.f : fast_exp2(a1.x - m);
+      // A parity without tiles in this item (one-tile items) keeps m = -inf and
+      // l = 0; its accumulator holds an older item's values and is not read.
+      const bool has0 = a0.x != -INFINITY, has1 = a1.x != -INFINITY;
+      const float w0 = has0 ? fast_exp2(a0.x - m) : 0.f;
+      const float w1 = has1 ? fast_exp2(a1.x - m) : 0.f;
       const float den = w0 * a0.y + w1 * a1.y;
       const float inv = den > 0.f ? 1.f / den : 0.f;
       const float s0 = w0 * inv, s1 = w1 * inv;
-      // Output columns [64 h, 64 h + 64) of this warp's 32 rows, staged as
+      // Output columns [64 par, 64 par + 64) of this warp's 32 rows, staged as
       // [32 rows][8 x 16 B chunks] with an XOR swizzle, then stored 4 rows per
       // warp-wide instruction.
 #pragma unroll
       for (int c4 = 0; c4 < 4; ++c4) {
         uint32_t o0[16], o1[16];
-        tmem_ld16(lane_addr + 256 + 64 * h + c4 * 16, o0);
-        tmem_ld16(lane_addr + 384 + 64 * h + c4 * 16, o1);
+        tmem_ld16(lane_addr + 256 + 64 * par + c4 * 16, o0);
+        tmem_ld16(lane_addr + 384 + 64 * par + c4 * 16, o1);
         tmem_wait_ld();
 #pragma unroll
         for (int e8 = 0; e8 < 2; ++e8) {
           float o[8];
 #pragma unroll
-          for (int e = 0; e < 8; ++e)
-            o[e] = __uint_as_float(o0[e8 * 8 + e]) * s0 + __uint_as_float(o1[e8 * 8 + e]) * s1;
+          for (int e = 0; e < 8; ++e) {
+            const float v0 = has0 ? __uint_as_float(o0[e8 * 8 + e]) * s0 : 0.f;
+            const float v1 = has1 ? __uint_as_float(o1[e8 * 8 + e]) * s1 : 0.f;
+            o[e] = v0 + v1;
+          }
           uint4 w;
           w.x = Elem<T>::from2(o[0], o[1]);
           w.y = Elem<T>::from2(o[2], o[3]);
@@ -608,7 +624,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           T* orow = static_cast<T*>(p.out) +
                     ((static_cast<int64_t>(it.s) * p.Hq + it.kvh * G + R / ppt) * p.Lq +
                      it.qt * ppt + iR) * kHD;
-          *reinterpret_cast<uint4*>(orow + 64 * h + chunk * 8) =
+          *reinterpret_cast<uint4*>(orow + 64 * par + chunk * 8) =
               *reinterpret_cast<const uint4*>(stage + rl * 128 + ((chunk ^ (rl & 7)) << 4));
         }
       }
