@@ -72,6 +72,25 @@ def test_tensor_core_prefill_vs_oracle(cuda, hq, hkv, dtype, causal):
     assert (out[1, :, 300:].float() == 0).all()
 
 
+@pytest.mark.parametrize("hq,hkv,causal", [(32, 8, True), (16, 16, True), (32, 4, False)])
+def test_persistent_ctas_many_ragged_items(cuda, hq, hkv, causal):
+    """More work items than SMs, so each CTA walks several items back to back:
+    one-tile items, odd tile counts (the S/P buffer parity flips between
+    items), rows past the sequence end and chunks that start mid-sequence."""
+    rng = random.Random(hq * 7 + hkv + causal)
+    L = 256
+    totals = [rng.randint(1, 1700) for _ in range(7)] + [37, 300]
+    starts = [max(0, t - rng.randint(1, L + 64)) for t in totals]
+    pt, q, k, v, cos, sin = _case(100 + hq + hkv, totals, hq, hkv, L, torch.bfloat16)
+    out = _run(pt, q, k, v, starts, totals, cos, sin, causal=causal, kernel="tc")
+    want = ao.prefill_attention(pt, q.float().cpu().numpy(), k.float().cpu().numpy(),
+                                v.float().cpu().numpy(), starts, totals, cos, sin, causal=causal)
+    rows = [min(L, t - s) for s, t in zip(starts, totals)]
+    for i, n in enumerate(rows):     # only rows inside the sequence are written
+        _check(out[i:i + 1, :, :n], want[i:i + 1, :, :n], f"seq {i} ({starts[i]}+{n}/{totals[i]})")
+        assert (out[i, :, n:].float() == 0).all()
+
+
 def test_tensor_cores_agree_with_cuda_cores(cuda):
     L, starts, totals = 256, [64, 700], [320, 956]
     pt, q, k, v, cos, sin = _case(7, totals, 32, 8, L, torch.bfloat16)
