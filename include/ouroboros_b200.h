@@ -195,7 +195,8 @@ typedef struct ouro_attention_args {
   const int8_t* block_mask;   /* optional, element (s, qb, kb) at the strides below */
   int64_t mask_stride_s, mask_stride_q, mask_stride_k;
   void* out;                  /* [S, Hq, q_len, D], dtype */
-  int32_t* status;            /* optional device int32 (bit 1: bad page entry) */
+  int32_t* status;            /* optional device int32: bit 1 bad page entry, 2 wait
+                                 timeout, 4 bad query position, 8 device check failed */
   int32_t num_seqs, num_q_heads, num_kv_heads, head_dim, q_len;
   int32_t max_blocks, num_phys_blocks, max_positions;
   int32_t dtype, causal, kernel; /* kernel: 0 auto, 1 CUDA cores, 2 tensor cores */

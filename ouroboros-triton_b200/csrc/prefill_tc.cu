@@ -63,13 +63,14 @@ constexpr float kRescaleLog2 = 8.0f;
 // of MUFU ex2 (0..4).
 constexpr int kPolyPairs = 0;
 
-// Two-stage K and V rings (three measured no faster). With two stages the K
-// slot of tile j is free exactly when S_j is done and the V slot exactly when
-// PV_j is done, so the producers wait on s_full / pv_done instead of separate
-// "empty" barriers: every tcgen05.commit costs the MMA thread as much issue
-// time as an MMA.
-constexpr int kStagesK = 2, kStagesV = 2;
-static_assert(kStagesK == 2 && kStagesV == 2, "ring slots are tied to the S/P buffer parity");
+// Ring depths. K tile j + 3 may load once S_j is done (k_empty); three K slots
+// give the TMA the time of two tiles, which it needs when the MMA thread runs
+// at its issue rate. The V slot of tile j is free exactly when PV_j is done,
+// so with two V slots the V producer waits on pv_done and no separate "empty"
+// commit is issued: every tcgen05.commit costs the MMA thread about as much
+// issue time as an MMA.
+constexpr int kStagesK = 3, kStagesV = 2;
+static_assert(kStagesV == 2, "V slots are tied to the S/P buffer parity");
 
 // Shared-memory map (offsets from a 1024-byte aligned base). P never touches
 // shared memory: it is written over its own S columns in TMEM and read from
@@ -80,13 +81,16 @@ constexpr int kOffV = kOffK + kStagesK * kTile;  // kStagesV V tiles
 constexpr int kOffStage = kOffV + kStagesV * kTile;  // output staging, 4 KB per softmax warp
 constexpr int kOffMl = kOffStage + kSoftmaxWarps * 32 * 128;  // (m, l) per half and row
 constexpr int kOffBar = kOffMl + 2 * kBM * 8;
-constexpr int kSmemBytes = kOffBar + 256 + 1024;
+// The dynamic shared window starts 1024-byte aligned (after the 1 KB the
+// system reserves); the kernel checks this instead of padding for it.
+constexpr int kSmemBytes = kOffBar + 256;
+static_assert(kSmemBytes <= 232448, "shared memory");
 
 // Every ring barrier is per buffer: a parity wait is only valid while the
 // barrier is at most one phase past the awaited one, and per-buffer barriers
 // keep each waiter within that window.
 struct Bars {
-  uint64_t k_full[kStagesK], v_full[kStagesV];
+  uint64_t k_full[kStagesK], k_empty[kStagesK], v_full[kStagesV];
   uint64_t s_full[2];
   uint64_t p_ready[2], pv_done[2];       // per S/P buffer = tile parity
   uint64_t q_ready, merge, o_free;        // once per item
@@ -182,8 +186,8 @@ __device__ __forceinline__ Item item_at(const RowsParams& p, int L, int n_qt, in
   Item it;
   const int group = L / n_qt;
   it.qt = n_qt - 1 - (L - group * n_qt);
-  it.kvh = group % p.Hkv;
   it.s = group / p.Hkv;
+  it.kvh = group - it.s * p.Hkv;
   it.seq_len = p.seq_lens[it.s];
   it.q0 = (p.q_start ? p.q_start[it.s] : 0) + it.qt * ppt;
   it.bad = it.q0 < 0;
@@ -219,16 +223,17 @@ struct QTile {
 
   __device__ __forceinline__ void load(const RowsParams& p, const Item& it, int ppt, int tid) {
     const int half = kHD / 2;
+    const int lppt = 31 - __clz(ppt);
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
       const int u = tid + kSoftmaxThreads * k, R = u >> 3, c = u & 7;
-      const int iR = R % ppt, posR = it.q0 + iR;
+      const int iR = R & (ppt - 1), posR = it.q0 + iR;  // ppt = 128 / G is a power of 2
       lo[k] = hi[k] = make_uint4(0, 0, 0, 0);
       cs[2 * k] = cs[2 * k + 1] = make_float4(1.f, 1.f, 1.f, 1.f);
       sn[2 * k] = sn[2 * k + 1] = make_float4(0.f, 0.f, 0.f, 0.f);
       if (iR < it.rows_valid) {
         const T* qrow = static_cast<const T*>(p.q) +
-                        ((static_cast<int64_t>(it.s) * p.Hq + it.kvh * p.G + R / ppt) * p.Lq +
+                        ((static_cast<int64_t>(it.s) * p.Hq + it.kvh * p.G + (R >> lppt)) * p.Lq +
                          it.qt * ppt + iR) * kHD;
         lo[k] = *reinterpret_cast<const uint4*>(qrow + 8 * c);
         hi[k] = *reinterpret_cast<const uint4*>(qrow + half + 8 * c);
@@ -261,23 +266,28 @@ __global__ void __launch_bounds__(kThreads, 1)
                       const __grid_constant__ CUtensorMap tm_v, const RowsParams p,
                       int32_t krot_rows_per_head) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>(
-      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint8_t* smem = smem_raw;
+  if ((smem_u32(smem) & 1023u) != 0) {  // 128-byte-swizzled TMA / UMMA tiles need 1 KB alignment
+    if (threadIdx.x == 0 && p.status) atomicOr(p.status, kStatusUnsupported);
+    return;
+  }
   Bars* bars = reinterpret_cast<Bars*>(smem + kOffBar);
   volatile int32_t* s_abort = &bars->abort;
 
   const int G = p.G;
-  const int ppt = kBM / G;  // positions per tile
+  const int ppt = kBM / G;  // positions per tile (G divides 128, so a power of 2)
+  const int lppt = 31 - __clz(ppt);
   const int n_qt = (p.Lq + ppt - 1) / ppt;
   const int n_items = n_qt * p.Hkv * p.S;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
     *s_abort = 0;
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < kStagesK; ++i) {
       mbar_init(&bars->k_full[i], 1);
-      mbar_init(&bars->v_full[i], 1);
+      mbar_init(&bars->k_empty[i], 1);
     }
+    for (int i = 0; i < kStagesV; ++i) mbar_init(&bars->v_full[i], 1);
     for (int i = 0; i < 2; ++i) {
       mbar_init(&bars->s_full[i], 1);
       mbar_init(&bars->p_ready[i], 128);
@@ -312,7 +322,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       tma_prefetch_desc(is_k ? &tm_k : &tm_v);
       const uint64_t pol = policy_evict_last();  // tiles are re-read by other CTAs
       uint64_t* full = is_k ? bars->k_full : bars->v_full;
-      uint64_t* empty = is_k ? bars->s_full : bars->pv_done;  // slot g % 2 frees with tile g
+      uint64_t* empty = is_k ? bars->k_empty : bars->pv_done;  // V slot g % 2 frees with PV_g
       uint8_t* ring = smem + (is_k ? kOffK : kOffV);
       const uint32_t stages = is_k ? kStagesK : kStagesV;
       uint32_t g = 0;
@@ -400,18 +410,19 @@ __global__ void __launch_bounds__(kThreads, 1)
           break;
         }
         for (int j = 0; j < it.n_tiles && ok; ++j) {
-          const uint32_t gg = g + j, b = gg & 1;
-          if (!mbar_wait(&bars->k_full[b], (gg >> 1) & 1)) {
+          const uint32_t gg = g + j, b = gg & 1, st = gg % kStagesK;
+          if (!mbar_wait(&bars->k_full[st], (gg / kStagesK) & 1)) {
             ok = false;
             break;
           }
-          const uint64_t kd = k_desc + b * kSlot;
+          const uint64_t kd = k_desc + st * kSlot;
 #pragma unroll
           for (int kk = 0; kk < kHD / 16; ++kk) {
             const uint64_t step = (kk >> 2) * (kAtom >> 4) + (kk & 3) * (32 >> 4);
             umma_f16_ss(tmem + b * 128, q_desc + step, kd + step, idesc_s, kk > 0 ? 1u : 0u);
           }
-          umma_commit(&bars->s_full[b]);  // also frees K slot b
+          umma_commit(&bars->s_full[b]);
+          umma_commit(&bars->k_empty[st]);
           if (j >= 1 && !issue_pv(gg - 1, j - 1)) ok = false;
         }
         if (ok) ok = issue_pv(g + it.n_tiles - 1, it.n_tiles - 1);
@@ -480,7 +491,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       return t.x + t.y;
     };
     while (L < n_items) {
-      const int i = r % ppt;
+      const int i = r & (ppt - 1);
       const bool live = i < it.rows_valid;
       const int pos = it.q0 + i;
       const int kmax_row = !live ? 0 : (p.causal ? min(it.seq_len, pos + 1) : it.seq_len);
@@ -619,10 +630,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int itr = 0; itr < 8; ++itr) {
         const int rl = itr * 4 + (lane >> 3), chunk = lane & 7;
-        const int R = quarter * 32 + rl, iR = R % ppt;
+        const int R = quarter * 32 + rl, iR = R & (ppt - 1);
         if (iR < it.rows_valid) {
           T* orow = static_cast<T*>(p.out) +
-                    ((static_cast<int64_t>(it.s) * p.Hq + it.kvh * G + R / ppt) * p.Lq +
+                    ((static_cast<int64_t>(it.s) * p.Hq + it.kvh * G + (R >> lppt)) * p.Lq +
                      it.qt * ppt + iR) * kHD;
           *reinterpret_cast<uint4*>(orow + 64 * par + chunk * 8) =
               *reinterpret_cast<const uint4*>(stage + rl * 128 + ((chunk ^ (rl & 7)) << 4));

@@ -15,6 +15,7 @@ enum : int32_t {
   kStatusBadPageEntry = 1,  // a page-table entry was outside [0, n_phys)
   kStatusWaitTimeout = 2,   // an mbarrier wait gave up (never expected)
   kStatusBadPosition = 4,   // a query position outside the RoPE tables
+  kStatusUnsupported = 8,   // a launch-time check of the device failed (no work done)
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
