@@ -448,6 +448,7 @@ def run_prefill(args):
     cos, sin = torch.from_numpy(cos).to(device), torch.from_numpy(sin).to(device)
     status = torch.zeros(1, dtype=torch.int32, device=device)
     calls = []
+    workspace = None  # rotated keys: one scratch for the whole prefill, each key rotated once
     for c in range(T // C):
         qc = q[:, :, c * C:(c + 1) * C].contiguous()
         starts = torch.full((S,), c * C, dtype=torch.int32, device=device)
@@ -456,7 +457,9 @@ def run_prefill(args):
         pt_c[:, (c + 1) * C // 64:] = -1
         calls.append(PrefillCall(pt_c, qc, k, v, starts, lens, cos, sin, causal=True,
                                  kernel=args.kernel if args.kernel != "auto" else "auto",
-                                 status=status))
+                                 status=status, workspace=workspace,
+                                 krot_valid=torch.full((S,), c * C, dtype=torch.int32)))
+        workspace = calls[-1].workspace
     flops = 4.0 * d * hq * S * (T * (T + 1) / 2.0)
     for _ in range(max(args.warmup, 3)):
         for cl in calls:
@@ -488,7 +491,7 @@ def run_prefill(args):
         "metric": "chunked-prefill attn TFLOP/s (causal, bf16)", "value": tflops,
         "unit": "TFLOP/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": ms, "higher_is_better": True, "dtype": "bf16", "data": "synthetic",
-        "config": dict(P, chunk_launches=len(calls)),
+        "config": dict(P, chunk_launches=len(calls), rotated_keys="one workspace per prefill; each key rotated once (krot_valid)"),
         "tokens_per_s": S * T / (ms / 1000.0),
         "roofline": {"bound": "tensor", "achieved": tflops, "peak": peak, "unit": "TFLOP/s",
                      "frac": (tflops / peak) if peak else None,

@@ -203,6 +203,11 @@ typedef struct ouro_attention_args {
   float softmax_scale;        /* <= 0: 1/sqrt(D) */
   void* workspace;            /* tensor-core path: rotated-key scratch, 16-B aligned */
   size_t workspace_bytes;     /* >= ouro_attention_plan's bytes */
+  const int32_t* krot_valid;  /* tensor-core path, optional device [S]: keys
+                                 [0, krot_valid[s]) of sequence s are already rotated in
+                                 `workspace` by an earlier call with the same caches, page
+                                 tables, RoPE tables and max_blocks (chunked prefill reuses
+                                 the scratch chunk after chunk); NULL: rotate every key */
 } ouro_attention_args;
 
 /* Kernel choice and the workspace the tensor-core path needs

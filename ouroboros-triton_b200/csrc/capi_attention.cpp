@@ -175,6 +175,7 @@ ouro::RowsParams to_rows(const ouro_attention_args* a) {
   p.scale_log2 = scale * ouro::kLog2e;
   p.workspace = a->workspace;
   p.workspace_bytes = static_cast<int64_t>(a->workspace_bytes);
+  p.krot_valid = a->krot_valid;
   if (dtype_bytes(a->dtype) == 0) fail(OURO_EUNSUPPORTED, "unsupported dtype code");
   if (p.S < 0 || p.Lq < 0) fail(OURO_EINVAL, "num_seqs and q_len must be >= 0");
   if (p.Hq <= 0 || p.Hkv <= 0 || p.Hq % p.Hkv != 0)

@@ -11,6 +11,9 @@
 // be twice the bytes of the keys themselves). Rows past the
 // sequence are rotated too (their scores are masked later); rows past the
 // RoPE tables get the identity rotation. HBM-bound: 2 x 256 B per key and head.
+// With krot_valid (chunked prefill reusing one workspace), whole blocks below
+// krot_valid[s] are skipped, so each key is rotated once per prompt instead of
+// once per chunk launch.
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
@@ -71,6 +74,8 @@ __global__ void __launch_bounds__(256) rope_k_kernel(const RowsParams p, T* __re
   const int b = blockIdx.x, s = blockIdx.y, h0 = blockIdx.z * kRopeHeadsPerCta;
   const int seq_len = p.seq_lens[s];
   if (b * kBlock >= seq_len || b >= blocks_per_seq) return;
+  // Blocks rotated by an earlier call that shares this workspace are kept.
+  if (p.krot_valid != nullptr && (b + 1) * kBlock <= p.krot_valid[s]) return;
   const int phys = p.page_table[static_cast<int64_t>(s) * p.max_blocks + b];
   if (phys < 0 || phys >= p.n_phys) {
     if (threadIdx.x == 0 && p.status) atomicOr(p.status, kStatusBadPageEntry);

@@ -30,6 +30,7 @@ struct RowsParams {
   float scale_log2;
   void* workspace;            // tensor-core path: rotated-key scratch (prefill_workspace_bytes)
   int64_t workspace_bytes;
+  const int32_t* krot_valid;  // optional [S]: keys already rotated in the workspace
 };
 
 cudaError_t launch_attend_rows_simt(const RowsParams& p, int dtype, cudaStream_t stream);

@@ -53,7 +53,7 @@ class AttentionArgs(ctypes.Structure):
         ("q_len", _i32), ("max_blocks", _i32), ("num_phys_blocks", _i32),
         ("max_positions", _i32), ("dtype", _i32), ("causal", _i32), ("kernel", _i32),
         ("softmax_scale", ctypes.c_float),
-        ("workspace", _vp), ("workspace_bytes", ctypes.c_size_t),
+        ("workspace", _vp), ("workspace_bytes", ctypes.c_size_t), ("krot_valid", _vp),
     ]
 
 

@@ -502,7 +502,13 @@ class PrefillCall:
 
     def __init__(self, page_table, q, k_cache, v_cache, q_start, seq_lens, cos, sin, *,
                  causal: bool = True, softmax_scale=None, out=None, validate: bool = True,
-                 kernel: str = "auto", status=None):
+                 kernel: str = "auto", status=None, workspace=None, krot_valid=None):
+        """``workspace`` (optional uint8 device tensor) is the tensor-core path's
+        rotated-key scratch; pass the same tensor to the calls of one chunked
+        prefill together with ``krot_valid`` ([S] int32: keys [0, krot_valid[s])
+        already rotated there by an earlier call with the same caches, page-table
+        width and RoPE tables) and each key is rotated once instead of once per
+        chunk."""
         _require_cuda()
         if kernel not in _KERNELS:
             raise RuntimeError(f"kernel must be one of {sorted(_KERNELS)}, got {kernel!r}")
@@ -549,10 +555,21 @@ class PrefillCall:
         self.tensor_cores = bool(tc.value)
         self.workspace = None
         if need.value:  # rotated-key scratch of the tensor-core path
-            self.workspace = torch.empty(need.value, dtype=torch.uint8, device=device)
-            self.args.workspace = _ptr(self.workspace)
+            if workspace is None:
+                workspace = torch.empty(need.value, dtype=torch.uint8, device=device)
+            elif (workspace.dtype != torch.uint8 or workspace.device != device
+                  or workspace.numel() < need.value or not workspace.is_contiguous()):
+                raise RuntimeError(f"workspace must be a contiguous uint8 tensor on {device} "
+                                   f"of at least {need.value} bytes")
+            self.workspace = workspace
+            self.args.workspace = _ptr(workspace)
             self.args.workspace_bytes = need.value
-        self._keep = (q, k_cache, v_cache, pt, lens, starts, cos, sin, status)
+        if krot_valid is not None:
+            krot_valid = _as_int32(_on(krot_valid, device), "krot_valid")
+            if tuple(krot_valid.shape) != (S,):
+                raise RuntimeError(f"krot_valid must have shape [{S}]")
+            self.args.krot_valid = _ptr(krot_valid)
+        self._keep = (q, k_cache, v_cache, pt, lens, starts, cos, sin, status, krot_valid)
 
     def launch(self):
         _launch_rows(self.args, self.device)
@@ -561,7 +578,8 @@ class PrefillCall:
 
 def chunked_prefill_attention(page_table, q, k_cache, v_cache, q_start, seq_lens, cos, sin, *,
                               causal: bool = True, softmax_scale=None, out=None,
-                              validate: bool = True, kernel: str = "auto", status=None):
+                              validate: bool = True, kernel: str = "auto", status=None,
+                              workspace=None, krot_valid=None):
     """Chunked prefill: q [S, Hq, L, D] rows at positions q_start[s] + i.
 
     Keys are every paged token j < seq_lens[s] (the chunk's own K/V already
@@ -569,10 +587,13 @@ def chunked_prefill_attention(page_table, q, k_cache, v_cache, q_start, seq_lens
     reads KV head h // (Hq / Hkv). Rows whose position is >= seq_lens[s] stay
     zero. fp16/bf16 with head_dim 128 run on the tcgen05 tensor-core kernel;
     other shapes and fp32 on CUDA cores. Returns [S, Hq, L, D] in the cache dtype.
+    ``workspace`` / ``krot_valid``: reuse of the rotated-key scratch across the
+    chunks of one prefill (see :class:`PrefillCall`).
     """
     return PrefillCall(page_table, q, k_cache, v_cache, q_start, seq_lens, cos, sin,
                        causal=causal, softmax_scale=softmax_scale, out=out, validate=validate,
-                       kernel=kernel, status=status).launch()
+                       kernel=kernel, status=status, workspace=workspace,
+                       krot_valid=krot_valid).launch()
 
 
 def paged_kv_append(k_new, v_new, page_table, start, counts, k_cache, v_cache, *, status=None):

@@ -91,6 +91,40 @@ def test_persistent_ctas_many_ragged_items(cuda, hq, hkv, causal):
         assert (out[i, :, n:].float() == 0).all()
 
 
+def test_chunked_prefill_reuses_rotated_keys(cuda):
+    """One workspace across the chunks of a prefill with krot_valid = tokens
+    already rotated. After each chunk the K cache rows of those tokens are
+    overwritten with garbage: later chunks still match the oracle on the
+    original keys, so the rotated scratch (not the cache) serves them."""
+    hq, hkv, d, L, chunks = 32, 8, 128, 256, 4
+    totals = [L * chunks] * 3
+    pt, q_all, k, v, cos, sin = _case(55, totals, hq, hkv, L * chunks, torch.bfloat16)
+    k_orig = k.clone()
+    want = ao.prefill_attention(pt, q_all.float().cpu().numpy(), k_orig.float().cpu().numpy(),
+                                v.float().cpu().numpy(), [0] * 3, totals, cos, sin, causal=True)
+    ptd = torch.from_numpy(pt).cuda()
+    cos_d, sin_d = torch.from_numpy(cos).cuda(), torch.from_numpy(sin).cuda()
+    ws = None  # the first call allocates the workspace; the later ones reuse it
+    for c in range(chunks):
+        starts = torch.full((3,), c * L, dtype=torch.int32, device="cuda")
+        lens = torch.full((3,), (c + 1) * L, dtype=torch.int32, device="cuda")
+        status = torch.zeros(1, dtype=torch.int32, device="cuda")
+        pt_c = ptd.clone()  # the chains as they stand after chunk c (PAD past them)
+        pt_c[:, (c + 1) * L // 64:] = -1
+        call = ba.PrefillCall(pt_c, q_all[:, :, c * L:(c + 1) * L].contiguous(), k, v, starts, lens,
+                              cos_d, sin_d, kernel="tc", status=status, workspace=ws,
+                              krot_valid=torch.full((3,), c * L, dtype=torch.int32))
+        ws = call.workspace
+        out = call.launch()
+        torch.cuda.synchronize()
+        assert int(status.item()) == 0
+        _check(out, want[:, :, c * L:(c + 1) * L], f"chunk {c}")
+        # corrupt every key rotated so far (its blocks are not read again)
+        for s in range(3):
+            for b in range((c + 1) * L // 64):
+                k[pt[s, b]] = 7.0
+
+
 def test_tensor_cores_agree_with_cuda_cores(cuda):
     L, starts, totals = 256, [64, 700], [320, 956]
     pt, q, k, v, cos, sin = _case(7, totals, 32, 8, L, torch.bfloat16)
