@@ -419,16 +419,25 @@ def run_prefill(args):
     """Chunked prefill: every 512-token chunk of 8 x 4096-token prompts, causal, GQA 32/8.
 
     A step is one full pass (8 chunk launches, each over all 8 prompts) with the prompts' K/V
-    already resident in the paged cache; FLOPs = 4 * D * Hq * sum_p sum_i (i + 1).
+    already resident in the paged cache; FLOPs = 4 * D * Hq * sum_p sum_i (i + 1). Under
+    torchrun every rank prefills its own 8 prompts on its GPU (whole prompts shard, no
+    collective in the data path): weak scaling, time = max over ranks.
     """
     import torch
+    import torch.distributed as dist
 
     from oracle import attention_oracle as ao  # RoPE table construction only
     from src.block_table import BlockTable
     from src.kernels.block_attention import PrefillCall
 
     P = PREFILL
-    device = torch.device("cuda", 0)
+    world, rank, local = _dist_env()
+    if world > 1:
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    device = torch.device("cuda", local if world > 1 else 0)
+    torch.cuda.set_device(device)
     S, T, C = P["prompts"], P["prompt_len"], P["chunk"]
     hq, hkv, d = P["q_heads"], P["kv_heads"], P["head_dim"]
     nbp = T // 64
@@ -440,7 +449,7 @@ def run_prefill(args):
         bt.free_block(i)
     heads = [bt.allocate_chain(nbp) for _ in range(S)]
     pt = torch.from_numpy(bt.export_page_table(heads, nbp)).to(device)
-    g = torch.Generator(device=device).manual_seed(4)
+    g = torch.Generator(device=device).manual_seed(4 + rank)
     k = (torch.randn(pool, hkv, 64, d, generator=g, device=device) * 0.5).bfloat16()
     v = (torch.randn(pool, hkv, 64, d, generator=g, device=device) * 0.5).bfloat16()
     q = (torch.randn(S, hq, T, d, generator=g, device=device) * 0.5).bfloat16()
@@ -467,7 +476,9 @@ def run_prefill(args):
     torch.cuda.synchronize()
     stream = torch.cuda.current_stream(device)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(0) as clk:
+    with ClockSampler(device.index) as clk:
+        if world > 1:
+            dist.barrier()
         torch.cuda.synchronize()
         e0.record(stream)
         for _ in range(args.steps):
@@ -475,7 +486,14 @@ def run_prefill(args):
                 cl.launch()
         e1.record(stream)
         torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
     ms = e0.elapsed_time(e1) / args.steps
+    if world > 1:  # the job's step time is the slowest rank's
+        t = torch.tensor([ms], dtype=torch.float64, device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    flops *= world
     tflops = flops / (ms / 1000.0) / 1e12
     peak = None
     pk = ROOT / "MEASURED_PEAKS.json"
@@ -487,20 +505,126 @@ def run_prefill(args):
                                 [T - C] * 2, [T] * 2, cos.cpu().numpy(), sin.cpu().numpy())
     got = calls[-1].out[:2, :1].float().cpu().numpy()
     err = abs(got - want)
+    per_gpu = tflops / world
     line = {
         "metric": "chunked-prefill attn TFLOP/s (causal, bf16)", "value": tflops,
-        "unit": "TFLOP/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": ms, "higher_is_better": True, "dtype": "bf16", "data": "synthetic",
-        "config": dict(P, chunk_launches=len(calls), rotated_keys="one workspace per prefill; each key rotated once (krot_valid)"),
-        "tokens_per_s": S * T / (ms / 1000.0),
-        "roofline": {"bound": "tensor", "achieved": tflops, "peak": peak, "unit": "TFLOP/s",
-                     "frac": (tflops / peak) if peak else None,
-                     "algorithmic_flops_per_step": flops},
+        "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "dtype": "bf16",
+        "data": "synthetic",
+        "config": dict(P, prompts_per_gpu=S, chunk_launches=len(calls),
+                       parallelism=f"dp{world} (whole prompts per GPU)",
+                       rotated_keys="one workspace per prefill; each key rotated once (krot_valid)"),
+        "tokens_per_s": world * S * T / (ms / 1000.0),
+        "roofline": {"bound": "tensor", "achieved": per_gpu, "peak": peak, "unit": "TFLOP/s",
+                     "frac": (per_gpu / peak) if peak else None,
+                     "algorithmic_flops_per_step_per_gpu": flops / world},
         "check": {"max_abs": float(err.max()), "mean_abs": float(err.mean()),
                   "kernel_status": int(status.item())},
         "clocks": clk.summary(),
     }
-    print(json.dumps(line), flush=True)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+SERVING = dict(workload="serving_trace_llama3_8b_attention", requests=512, rate_per_s=64.0,
+               prompt_median=2048, prompt_sigma=1.0, prompt_min=128, prompt_max=16384,
+               output_tokens=256, q_heads=32, kv_heads=8, head_dim=128, hidden=4096, dtype="bf16",
+               rope_base=500000.0, chunk=2048, prefill_tokens_per_step=8192,
+               pool_fraction=0.25, seed=17)
+
+
+def run_serving(args):
+    """The serving trace: Poisson arrivals, lognormal prompts, 256 output tokens each,
+    continuous batching through the native allocator, token scopes from random segments.
+
+    Every rank builds the same seeded trace and serves its LPT shard of whole requests on
+    its own GPU (sequence-sharded KV; no collective on the data path). value = all ranks'
+    output tokens / the slowest rank's wall time (arrivals run on the wall clock, so the
+    trace's own 8 s of arrivals bound it from below).
+    """
+    import torch
+    import torch.distributed as dist
+
+    from src.engine import Engine, StandInBackend, make_trace, shard_requests
+    from src.serving import KVPool
+
+    P = SERVING
+    world, rank, local = _dist_env()
+    if world > 1:
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    device = torch.device("cuda", local if world > 1 else 0)
+    torch.cuda.set_device(device)
+    trace = make_trace(P["requests"], P["rate_per_s"], P["prompt_median"], P["prompt_sigma"],
+                       P["prompt_min"], P["prompt_max"], P["output_tokens"], P["seed"])
+    mine = shard_requests(trace, world)[rank]
+    max_total = P["prompt_max"] + P["output_tokens"]
+    blocks = sum(r.blocks for r in mine)
+    pool_blocks = max(-(-max_total // 64) + 1, int(blocks * P["pool_fraction"]))
+    pool = KVPool(device=device, num_blocks=pool_blocks, kv_heads=P["kv_heads"],
+                  head_dim=P["head_dim"], dtype=torch.bfloat16, max_positions=max_total,
+                  rope_base=P["rope_base"])
+    be = StandInBackend(pool, P["q_heads"], hidden=P["hidden"], max_total=max_total,
+                        slots=1024, seed=rank)
+    # warm-up: a short trace of its own through the same pool (all chains freed after)
+    warm = make_trace(8, 1000.0, 600, 0.5, 128, 2048, 8, seed=1000 + rank)
+    Engine(pool.table, be, chunk=P["chunk"], prefill_tokens=P["prefill_tokens_per_step"]).run(warm)
+    torch.cuda.synchronize(device)
+    be.kv_bytes = 0
+    be.attn_events = {"prefill": [], "decode": []}
+    eng = Engine(pool.table, be, chunk=P["chunk"], prefill_tokens=P["prefill_tokens_per_step"],
+                 slots=1024)
+    if world > 1:
+        dist.barrier()
+    with ClockSampler(device.index) as clk:
+        st = eng.run(mine, sync=None)
+        torch.cuda.synchronize(device)
+    dec_ms, pre_ms = be.attn_ms("decode"), be.attn_ms("prefill")
+    vals = torch.tensor([st["generated_tokens"], st["wall_s"], be.kv_bytes, dec_ms],
+                        dtype=torch.float64, device=device)
+    if world > 1:
+        tot = vals.clone()
+        dist.all_reduce(tot, op=dist.ReduceOp.SUM)
+        mx = vals.clone()
+        dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+        gen, wall, kv_total = float(tot[0]), float(mx[1]), float(tot[2])
+    else:
+        gen, wall, kv_total = float(vals[0]), float(vals[1]), float(vals[2])
+    peak = None
+    pk = ROOT / "MEASURED_PEAKS.json"
+    if pk.exists():
+        peak = float(json.loads(pk.read_text())["hbm_gbs"])
+    dec_gbs = be.kv_bytes / (dec_ms / 1000.0) / 1e9 if dec_ms > 0 else None
+    line = {
+        "metric": "serving trace output tokens/s (512 requests, Poisson 64/s, 256 output tokens)",
+        "value": gen / wall, "unit": "tokens/s", "n_gpus": world, "higher_is_better": True,
+        "scaling": "strong", "dtype": "bf16",
+        "data": "synthetic (seeded trace; random-init stand-in projections, no dataset)",
+        "config": dict(P, parallelism=f"dp{world} (whole requests per GPU, LPT)",
+                       pool_blocks_rank0=pool_blocks),
+        "wall_s": wall, "generated_tokens": gen,
+        "rank0": {"requests": st["requests"], "steps": st["steps"], "ttft_s": st["ttft_s"],
+                  "tpot_s": st["tpot_s"], "peak_running": st["peak_running"],
+                  "peak_blocks": st["peak_blocks"], "prompt_tokens": st["prompt_tokens"],
+                  "prefill_attention_ms": pre_ms},
+        "decode_attention": {"timing": "CUDA events around each decode call (decode + combine "
+                                       "kernels and the host gap between their launches)",
+                             "bytes_rank0": be.kv_bytes, "ms_rank0": dec_ms,
+                             "GB/s_rank0": dec_gbs, "peak_GB/s": peak,
+                             "frac": (dec_gbs / peak) if (dec_gbs and peak) else None,
+                             "bytes_all_ranks": kv_total},
+        "clocks": clk.summary(),
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
     return 0
 
 
@@ -513,8 +637,9 @@ def main() -> int:
     ap.add_argument("--split-blocks", type=int, default=0)
     ap.add_argument("--kernel", default="auto", choices=["auto", "tc", "simt"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
-    ap.add_argument("--workload", choices=["decode", "prefill"], default="decode",
-                    help="decode (the headline metric) or the chunked-prefill tensor-core pass")
+    ap.add_argument("--workload", choices=["decode", "prefill", "serving"], default="decode",
+                    help="decode (the headline metric), the chunked-prefill tensor-core pass, "
+                         "or the serving trace (continuous batching end to end)")
     ap.add_argument("--seqs", type=int, default=0,
                     help="sequences per GPU (default: the workload's 256); smaller values "
                          "make a profiling case of the same kernel")
@@ -523,6 +648,8 @@ def main() -> int:
         return run_reference(args)
     if args.workload == "prefill":
         return run_prefill(args)
+    if args.workload == "serving":
+        return run_serving(args)
     return run_ours(args)
 
 

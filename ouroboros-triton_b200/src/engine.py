@@ -1,0 +1,355 @@
+"""Continuous-batching serving loop: the Supervisor's per-GPU executor driving
+the paged attention path end to end on a serving trace (Poisson arrivals,
+lognormal prompt lengths, a fixed number of output tokens, token scopes from
+random segments).
+
+Per step, on one GPU's KV pool:
+
+1. admission: arrived requests, in arrival order, get one chain for their
+   prompt plus output tokens from the native allocator (all or nothing); a
+   request that does not fit waits, and the queue behind it waits too;
+2. prefill: up to ``prefill_tokens`` prompt tokens, at most ``chunk`` per
+   request: stand-in QKV projection, the chunk's K/V appended to the chain
+   (kv-append kernel), causal attention of the chunk over the chain
+   (tensor-core prefill kernel); a request whose prompt completes gets its
+   first output token from the prompt's last row;
+3. decode: every request past its prompt decodes one token: QKV projection of
+   its last token, K/V append, paged decode attention under the request's
+   token scope (decode kernel), output projection, next token;
+4. a request with all its output tokens frees its chain.
+
+The model around attention is a random-init stand-in (token embedding, fused
+QKV projection, output projection and an argmax over the first ``vocab``
+hidden units as the next token): the trace exercises the allocator and the
+attention kernels, not a language model. Prompt attention is causal without
+the token scope, because the tensor-core prefill kernel takes no scope input;
+decode applies it.
+
+The scheduler talks to a backend (``prefill`` / ``decode``), so it runs on
+the CPU against a stand-in backend in the tests.
+"""
+
+from __future__ import annotations
+
+import math
+import random
+import time
+from collections import deque
+from dataclasses import dataclass, field
+
+import numpy as np
+
+from .block_table import BLOCK_SIZE
+from .scoping_mask import GLOBAL, LOCAL, token_scope
+
+
+@dataclass
+class Request:
+    rid: int
+    arrival: float          # seconds after the trace starts
+    prompt_len: int
+    max_new: int            # output tokens (the first comes from the prefill)
+    spans: list             # [(start, end, scope)] partitioning [0, prompt_len + max_new)
+    head: int = -1          # chain head while admitted
+    slot: int = -1          # backend slot while admitted
+    done_prompt: int = 0    # prompt tokens whose K/V are in the cache
+    generated: int = 0      # output tokens produced
+    last_token: int = 0
+    admit_time: float | None = None
+    first_token_time: float | None = None
+    finish_time: float | None = None
+    tags: np.ndarray | None = field(default=None, repr=False)   # uint8 [total], 1 = GLOBAL
+    span_start: np.ndarray | None = field(default=None, repr=False)
+    span_end: np.ndarray | None = field(default=None, repr=False)
+
+    @property
+    def total(self) -> int:
+        return self.prompt_len + self.max_new
+
+    @property
+    def blocks(self) -> int:
+        return -(-self.total // BLOCK_SIZE)
+
+    def scope_span(self, pos: int) -> tuple[int, int]:
+        """(lo, hi) of the query at ``pos``: empty for a GLOBAL query."""
+        if self.tags[pos]:
+            return 0, 0
+        return int(self.span_start[pos]), int(self.span_end[pos])
+
+
+def random_segments(rng: random.Random, total: int, lo: int = 32, hi: int = 512) -> list:
+    """Segments of U[lo, hi] tokens covering [0, total) (the last one truncated):
+    the first GLOBAL, each later one LOCAL with probability 1/2, else GLOBAL."""
+    spans, s, k = [], 0, 0
+    while s < total:
+        e = min(total, s + rng.randint(lo, hi))
+        spans.append((s, e, GLOBAL if k == 0 or rng.random() >= 0.5 else LOCAL))
+        s, k = e, k + 1
+    return spans
+
+
+def make_trace(n: int, rate: float, median: float, sigma: float, lo: int, hi: int,
+               max_new: int, seed: int) -> list[Request]:
+    """Poisson arrivals at ``rate`` per second, prompt lengths lognormal with the
+    given median and sigma clipped to [lo, hi], ``max_new`` output tokens."""
+    rng = random.Random(seed)
+    t, out = 0.0, []
+    for i in range(n):
+        t += rng.expovariate(rate)
+        L = int(min(hi, max(lo, round(rng.lognormvariate(math.log(median), sigma)))))
+        out.append(Request(i, t, L, max_new, random_segments(rng, L + max_new)))
+    return out
+
+
+class Engine:
+    """Continuous batching over one pool's allocator (``table``) and a backend."""
+
+    def __init__(self, table, backend, *, chunk: int = 2048, prefill_tokens: int = 8192,
+                 slots: int = 1024):
+        self.table = table
+        self.backend = backend
+        self.chunk = chunk
+        self.prefill_tokens = prefill_tokens
+        self.waiting: deque[Request] = deque()
+        self.running: list[Request] = []
+        self.finished: list[Request] = []
+        self.free_slots = list(range(slots - 1, -1, -1))
+        self.steps = 0
+        self.peak_running = 0
+        self.peak_blocks = 0
+
+    def submit(self, reqs) -> None:
+        self.waiting.extend(sorted(reqs, key=lambda r: (r.arrival, r.rid)))
+
+    @property
+    def idle(self) -> bool:
+        return not self.waiting and not self.running
+
+    def _admit(self, now: float) -> None:
+        while self.waiting and self.waiting[0].arrival <= now and self.free_slots:
+            r = self.waiting[0]
+            if self.table.num_free < r.blocks:
+                break                       # arrival order: the queue waits behind r
+            r.head = self.table.allocate_chain(r.blocks)
+            r.slot = self.free_slots.pop()
+            r.tags, r.span_start, r.span_end = token_scope(r.spans)
+            r.admit_time = now
+            self.backend.admit(r)
+            self.running.append(r)
+            self.waiting.popleft()
+
+    def _page_table(self, reqs):
+        width = max(self.table.chain_len(r.head) for r in reqs)
+        return self.table.export_page_table([r.head for r in reqs], width)
+
+    def step(self, now: float) -> None:
+        """One scheduling step at time ``now``; a no-op when nothing is runnable."""
+        self._admit(now)
+        # prefill: oldest prompts first, at most `chunk` tokens each, `prefill_tokens` in all
+        pre, starts, counts, budget = [], [], [], self.prefill_tokens
+        for r in self.running:
+            left = r.prompt_len - r.done_prompt
+            if left > 0 and budget > 0:
+                c = min(left, self.chunk, budget)
+                pre.append(r)
+                starts.append(r.done_prompt)
+                counts.append(c)
+                budget -= c
+        dec = [r for r in self.running if r.done_prompt == r.prompt_len and 0 < r.generated < r.max_new]
+        if pre:
+            tokens = self.backend.prefill(pre, self._page_table(pre), np.asarray(starts, np.int32),
+                                          np.asarray(counts, np.int32))
+            for r, c, tok in zip(pre, counts, tokens):
+                r.done_prompt += c
+                if r.done_prompt == r.prompt_len:
+                    r.last_token = int(tok)
+                    r.generated = 1
+                    r.first_token_time = now
+        if dec:
+            pos = np.asarray([r.prompt_len + r.generated - 1 for r in dec], np.int32)
+            tokens = self.backend.decode(dec, self._page_table(dec), pos)
+            for r, tok in zip(dec, tokens):
+                r.last_token = int(tok)
+                r.generated += 1
+        if pre or dec:
+            self.steps += 1
+        self.peak_running = max(self.peak_running, len(self.running))
+        self.peak_blocks = max(self.peak_blocks, self.table.max_blocks - self.table.num_free)
+        keep = []
+        for r in self.running:
+            if r.generated >= r.max_new:
+                if r.first_token_time is None:
+                    r.first_token_time = now
+                r.finish_time = now
+                self.table.free_chain(r.head)
+                self.backend.release(r)
+                self.free_slots.append(r.slot)
+                r.head = r.slot = -1
+                self.finished.append(r)
+            else:
+                keep.append(r)
+        self.running = keep
+
+    def run(self, reqs, *, clock=time.perf_counter, sleep=time.sleep, sync=None,
+            max_steps: int = 10 ** 9) -> dict:
+        """Serves ``reqs`` with arrivals on ``clock`` (seconds since the call) and
+        returns the trace's statistics; ``sync`` (optional) waits for the
+        device before a timestamp is taken."""
+        self.submit(reqs)
+        t0 = clock()
+        while not self.idle and self.steps < max_steps:
+            now = clock() - t0
+            if not self.running and self.waiting and self.waiting[0].arrival > now:
+                sleep(min(0.001, self.waiting[0].arrival - now))
+                continue
+            self.step(now)
+            if sync is not None:
+                sync()
+        wall = clock() - t0
+        return self.stats(wall)
+
+    def stats(self, wall: float) -> dict:
+        done = self.finished
+        gen = sum(r.generated for r in done)
+        ttft = [r.first_token_time - r.arrival for r in done if r.first_token_time is not None]
+        tpot = [(r.finish_time - r.first_token_time) / (r.max_new - 1)
+                for r in done if r.max_new > 1 and r.first_token_time is not None]
+        q = lambda xs, p: float(np.percentile(xs, p)) if xs else None  # noqa: E731
+        return {
+            "requests": len(done), "generated_tokens": gen, "wall_s": wall, "steps": self.steps,
+            "prompt_tokens": sum(r.prompt_len for r in done),
+            "ttft_s": {"p50": q(ttft, 50), "p99": q(ttft, 99)},
+            "tpot_s": {"p50": q(tpot, 50), "p99": q(tpot, 99)},
+            "peak_running": self.peak_running, "peak_blocks": self.peak_blocks,
+        }
+
+
+def shard_requests(reqs, world: int) -> list[list[Request]]:
+    """Whole requests per GPU, longest-processing-time on total tokens (the
+    Supervisor's placement), in arrival order within each shard."""
+    loads = [0] * world
+    out = [[] for _ in range(world)]
+    for r in sorted(reqs, key=lambda r: (-r.total, r.rid)):
+        g = min(range(world), key=lambda i: (loads[i], i))
+        loads[g] += r.total
+        out[g].append(r)
+    return [sorted(s, key=lambda r: (r.arrival, r.rid)) for s in out]
+
+
+class StandInBackend:
+    """Random-init stand-in model on one GPU around the paged attention path.
+
+    Weights (bf16, N(0, 1/hidden)): token embedding [vocab, hidden], fused QKV
+    projection [hidden, (Hq + 2 Hkv) D], output projection [Hq D, hidden]. A
+    prompt token's id is a fixed hash of (request, position); the next token
+    is the argmax over the first ``vocab`` units of the projected attention
+    output. Decode attention reads every cached key of the running requests:
+    ``kv_bytes`` counts those bytes and ``attn_ms`` the attention kernels'
+    device time (CUDA events on the launching stream).
+    """
+
+    def __init__(self, pool, q_heads: int, *, hidden: int = 4096, vocab: int = 4096,
+                 max_total: int = 16640, slots: int = 1024, seed: int = 0):
+        import torch
+
+        self.torch = torch
+        self.pool = pool
+        self.device = pool.device
+        self.hq, self.hkv, self.d = q_heads, pool.kv_heads, pool.head_dim
+        self.vocab = vocab
+        g = torch.Generator(device=self.device).manual_seed(seed)
+        dt = pool.dtype
+        scale = 1.0 / math.sqrt(hidden)
+        self.emb = (torch.randn(vocab, hidden, generator=g, device=self.device)).to(dt)
+        self.w_qkv = (torch.randn(hidden, (self.hq + 2 * self.hkv) * self.d, generator=g,
+                                  device=self.device) * scale).to(dt)
+        self.w_o = (torch.randn(self.hq * self.d, hidden, generator=g, device=self.device)
+                    * (1.0 / math.sqrt(self.hq * self.d))).to(dt)
+        width = -(-max_total // 16) * 16
+        self.tags = torch.zeros(slots, width, dtype=torch.uint8, device=self.device)
+        self.kv_bytes = 0
+        self.attn_events = {"prefill": [], "decode": []}  # (start, end) CUDA event pairs
+
+    # ---- slots ------------------------------------------------------------
+    def admit(self, r: Request) -> None:
+        self.tags[r.slot, : r.total].copy_(self.torch.from_numpy(r.tags), non_blocking=False)
+
+    def release(self, r: Request) -> None:
+        pass
+
+    # ---- model pieces -------------------------------------------------------
+    def _qkv(self, tokens):
+        """tokens [...] int64 -> q [..., Hq, D], k / v [..., Hkv, D]."""
+        h = self.emb[tokens]
+        qkv = (h @ self.w_qkv).view(*tokens.shape, self.hq + 2 * self.hkv, self.d)
+        return qkv[..., : self.hq, :], qkv[..., self.hq: self.hq + self.hkv, :], qkv[..., self.hq + self.hkv:, :]
+
+    def _next(self, o):
+        """o [n, Hq, D] -> next token ids [n] (host)."""
+        h = o.reshape(o.shape[0], -1) @ self.w_o
+        return h[:, : self.vocab].float().argmax(dim=1).cpu().numpy()
+
+    def _timed(self, kind, fn):
+        torch = self.torch
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        out = fn()
+        e1.record()
+        self.attn_events[kind].append((e0, e1))
+        return out
+
+    def attn_ms(self, kind=None) -> float:
+        """Device time of the attention launches (``"prefill"``, ``"decode"`` or both)."""
+        self.torch.cuda.synchronize(self.device)
+        kinds = [kind] if kind else list(self.attn_events)
+        return sum(a.elapsed_time(b) for k in kinds for a, b in self.attn_events[k])
+
+    # ---- backend interface ---------------------------------------------------
+    def prefill(self, reqs, page_table, starts, counts):
+        from .kernels.block_attention import chunked_prefill_attention, paged_kv_append
+
+        torch = self.torch
+        dev = self.device
+        n, Lc = len(reqs), int(counts.max())
+        rid = torch.tensor([r.rid for r in reqs], device=dev)[:, None]
+        pos = torch.from_numpy(starts).to(dev)[:, None].long() + torch.arange(Lc, device=dev)[None, :]
+        tokens = (rid * 7919 + pos * 104729) % self.vocab
+        q, k, v = self._qkv(tokens)                          # [n, Lc, H, D]
+        q = q.permute(0, 2, 1, 3).contiguous()
+        k = k.permute(0, 2, 1, 3).contiguous()
+        v = v.permute(0, 2, 1, 3).contiguous()
+        pt = torch.from_numpy(page_table).to(dev)
+        st = torch.from_numpy(starts).to(dev)
+        ct = torch.from_numpy(counts).to(dev)
+        paged_kv_append(k, v, pt, st, ct, self.pool.k_cache, self.pool.v_cache)
+        out = self._timed("prefill", lambda: chunked_prefill_attention(
+            pt, q, self.pool.k_cache, self.pool.v_cache, st, st + ct, self.pool.cos,
+            self.pool.sin, causal=True, validate=False))
+        last = out[torch.arange(n, device=dev), :, ct.long() - 1]   # [n, Hq, D]
+        return self._next(last)
+
+    def decode(self, reqs, page_table, pos):
+        from .kernels.block_attention import block_attention_decode, paged_kv_append
+
+        torch = self.torch
+        dev = self.device
+        n = len(reqs)
+        tokens = torch.tensor([r.last_token for r in reqs], device=dev)
+        q, k, v = self._qkv(tokens)                          # [n, H, D]
+        pt = torch.from_numpy(page_table).to(dev)
+        start = torch.from_numpy(pos).to(dev)
+        paged_kv_append(k[:, :, None].contiguous(), v[:, :, None].contiguous(), pt, start,
+                        torch.ones(n, dtype=torch.int32, device=dev), self.pool.k_cache,
+                        self.pool.v_cache)
+        lens = start + 1
+        slots = torch.tensor([r.slot for r in reqs], device=dev)
+        tags = self.tags.index_select(0, slots)
+        span = torch.tensor([r.scope_span(int(p)) for r, p in zip(reqs, pos)],
+                            dtype=torch.int32).to(dev)
+        out = self._timed("decode", lambda: block_attention_decode(
+            pt, q.contiguous(), self.pool.k_cache, self.pool.v_cache, lens, self.pool.cos,
+            self.pool.sin, scope=(tags, span), validate=False))
+        self.kv_bytes += int(pos.astype(np.int64).sum() + n) * self.hkv * self.d * 2 * \
+            self.pool.k_cache.element_size()
+        self.last_decode = (pt, q, lens, tags, span, out)
+        return self._next(out)
