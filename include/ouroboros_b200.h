@@ -208,6 +208,12 @@ typedef struct ouro_attention_args {
                                  `workspace` by an earlier call with the same caches, page
                                  tables, RoPE tables and max_blocks (chunked prefill reuses
                                  the scratch chunk after chunk); NULL: rotate every key */
+  const uint8_t* scope_tags;  /* optional token scope (Table 1), [S, scope_stride]:
+                                 1 = GLOBAL token */
+  int64_t scope_stride;       /* multiple of 16 */
+  const int32_t* scope_lo;    /* [S, scope_stride]: LOCAL span [lo, hi) of the token at each */
+  const int32_t* scope_hi;    /* position; the query at position i keeps key j when tags[j]
+                                 or lo[i] <= j < hi[i] (both NULL with scope_tags NULL) */
 } ouro_attention_args;
 
 /* Kernel choice and the workspace the tensor-core path needs

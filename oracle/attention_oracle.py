@@ -202,11 +202,16 @@ def decode_attention(page_table, q, k_cache, v_cache, seq_lens, cos, sin, *, pos
 
 
 def prefill_attention(page_table, q, k_cache, v_cache, q_start, seq_lens, cos, sin, *,
-                      causal=True, softmax_scale=None, acc=np.float32):
+                      causal=True, softmax_scale=None, acc=np.float32, scope_tags=None,
+                      scope_lo=None, scope_hi=None):
     """Chunked prefill: q [S, Hq, L, D] at positions q_start[s] + i over keys 0..seq_len-1.
 
     Row i of sequence s attends to keys j <= q_start[s] + i when ``causal``.
-    Rows with q_start[s] + i >= seq_len[s] are left zero.
+    Rows with q_start[s] + i >= seq_len[s] are left zero. Token scope
+    (Table 1 of scoping_mask.py:148-161, per query position): ``scope_tags``
+    [S, >=T] (1 = GLOBAL key), ``scope_lo`` / ``scope_hi`` [S, >=T] the LOCAL
+    span of the token at each position; key j is kept for the query at
+    position i when tags[j] or lo[i] <= j < hi[i].
     """
     page_table = np.asarray(page_table)
     S, Hq, L, D = q.shape
@@ -229,9 +234,16 @@ def prefill_attention(page_table, q, k_cache, v_cache, q_start, seq_lens, cos, s
         qs = rope_half_split(q[s, :, :rows].astype(acc), cos[qpos], sin[qpos])  # [Hq,rows,D]
         qs = qs.reshape(Hkv, G, rows, D)
         scores = np.einsum("hgid,htd->hgit", qs, k) * scale
+        ok = np.ones((rows, T), dtype=bool)
         if causal:
-            ok = np.arange(T)[None, :] <= qpos[:, None]
-            scores = np.where(ok[None, None], scores, -np.inf)
+            ok &= np.arange(T)[None, :] <= qpos[:, None]
+        if scope_tags is not None:
+            tags = np.asarray(scope_tags)[s, :T] != 0
+            lo = np.asarray(scope_lo)[s, qpos][:, None]
+            hi = np.asarray(scope_hi)[s, qpos][:, None]
+            j = np.arange(T)[None, :]
+            ok &= tags[None, :] | ((j >= lo) & (j < hi))
+        scores = np.where(ok[None, None], scores, -np.inf)
         out[s, :, :rows] = np.einsum("hgit,htd->hgid", _softmax_rows(scores), v).reshape(Hq, rows, D)
     return out
 

@@ -4,9 +4,9 @@
 //
 // CTA = 8 query rows of one (sequence, query head); its 4 warps take the
 // sequence's KV blocks round-robin, lanes across head_dim. Per key: RoPE on K
-// in registers, one dot per row (warp all-reduce), additive bias, causal and
-// block-mask filtering, online softmax in base 2; warp states merge through
-// shared memory. Rows past the sequence end are not written.
+// in registers, one dot per row (warp all-reduce), additive bias, causal,
+// block-mask and token-scope filtering, online softmax in base 2; warp states
+// merge through shared memory. Rows past the sequence end are not written.
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
@@ -69,6 +69,14 @@ __global__ void __launch_bounds__(kWarps * 32) attend_rows_simt_kernel(const Row
   }
   if (max_pos < 0) return;
   const int kv_len = p.causal ? min(seq_len, max_pos + 1) : seq_len;
+  // Token scope: the row at position i keeps key j when tags[j] or lo[i] <= j < hi[i].
+  int sc_lo[kRows], sc_hi[kRows];
+  const uint8_t* sc_tags = p.scope_tags ? p.scope_tags + s * p.scope_stride : nullptr;
+#pragma unroll
+  for (int r = 0; r < kRows; ++r) {
+    sc_lo[r] = (sc_tags && live[r]) ? p.scope_lo[s * p.scope_stride + pos[r]] : 0;
+    sc_hi[r] = (sc_tags && live[r]) ? p.scope_hi[s * p.scope_stride + pos[r]] : 0;
+  }
 
   float* q_s = smem;                         // [rows][D]
   float* m_s = q_s + kRows * D;              // [warps][rows]
@@ -154,9 +162,11 @@ __global__ void __launch_bounds__(kWarps * 32) attend_rows_simt_kernel(const Row
         vv[2 * e] = v0;
         vv[2 * e + 1] = v1;
       }
+      const bool global_key = sc_tags == nullptr || sc_tags[j] != 0;
 #pragma unroll
       for (int r = 0; r < kRows; ++r) {
         if (!live[r] || (p.causal && j > pos[r])) continue;
+        if (!global_key && (j < sc_lo[r] || j >= sc_hi[r])) continue;
         float dot = 0.f;
 #pragma unroll
         for (int e = 0; e < 2 * PAIRS; ++e) dot = fmaf(qreg[r][e], kk[e], dot);

@@ -176,6 +176,18 @@ ouro::RowsParams to_rows(const ouro_attention_args* a) {
   p.workspace = a->workspace;
   p.workspace_bytes = static_cast<int64_t>(a->workspace_bytes);
   p.krot_valid = a->krot_valid;
+  if (a->scope_tags != nullptr) {
+    if (a->scope_lo == nullptr || a->scope_hi == nullptr)
+      fail(OURO_EINVAL, "scope_tags needs scope_lo and scope_hi");
+    if (a->scope_stride <= 0 || (a->scope_stride & 15) != 0)
+      fail(OURO_EINVAL, "scope_stride must be a positive multiple of 16");
+    if ((reinterpret_cast<uintptr_t>(a->scope_tags) & 15u) != 0)
+      fail(OURO_EINVAL, "scope_tags must be 16-byte aligned");
+    p.scope_tags = a->scope_tags;
+    p.scope_stride = a->scope_stride;
+    p.scope_lo = a->scope_lo;
+    p.scope_hi = a->scope_hi;
+  }
   if (dtype_bytes(a->dtype) == 0) fail(OURO_EUNSUPPORTED, "unsupported dtype code");
   if (p.S < 0 || p.Lq < 0) fail(OURO_EINVAL, "num_seqs and q_len must be >= 0");
   if (p.Hq <= 0 || p.Hkv <= 0 || p.Hq % p.Hkv != 0)

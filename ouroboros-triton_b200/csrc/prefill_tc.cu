@@ -260,7 +260,7 @@ struct QTile {
   }
 };
 
-template <typename T>
+template <typename T, bool kScoped>
 __global__ void __launch_bounds__(kThreads, 1)
     prefill_tc_kernel(const __grid_constant__ CUtensorMap tm_k,
                       const __grid_constant__ CUtensorMap tm_v, const RowsParams p,
@@ -452,13 +452,44 @@ __global__ void __launch_bounds__(kThreads, 1)
       fence_proxy_async_smem();
       mbar_arrive(&bars->q_ready);
     }
-    // Masks 32 scores of keys key0 .. key0 + 31 and returns their max.
-    auto mask_max32 = [&](uint32_t (&v)[32], int key0, int kmax_row, bool full) -> float {
-      if (!full) {
+    // Token scope (optional): the row at position i keeps key j when tags[j] or
+    // lo[i] <= j < hi[i]; sc_lo / sc_hi are set per item below.
+    const uint8_t* sc_tags = nullptr;
+    int sc_lo = 0, sc_hi = 0;
+    // Sets masked scores of keys key0 .. key0 + 31 to -inf: past the row's key
+    // limit, or outside its scope (tags read as two 16-byte vectors, each one
+    // only if it starts inside the tag row).
+    auto mask32 = [&](uint32_t (&v)[32], int key0, int kmax_row) {
+      if (kScoped) {
+        // One bit per key: GLOBAL tags (bytes of 0 / 1 packed four at a time),
+        // or inside [sc_lo, sc_hi), and below the key limit.
+        const uint4 z = make_uint4(0, 0, 0, 0);
+        const uint4 a = key0 < p.scope_stride ? *reinterpret_cast<const uint4*>(sc_tags + key0) : z;
+        const uint4 b =
+            key0 + 16 < p.scope_stride ? *reinterpret_cast<const uint4*>(sc_tags + key0 + 16) : z;
+        auto pack4 = [](uint32_t w) {  // bytes b0..b3 in {0, 1} -> bits 0..3
+          return ((w & 0x01010101u) * 0x01020408u) >> 24;
+        };
+        const uint32_t tag_bits = pack4(a.x) | pack4(a.y) << 4 | pack4(a.z) << 8 | pack4(a.w) << 12 |
+                                  pack4(b.x) << 16 | pack4(b.y) << 20 | pack4(b.z) << 24 |
+                                  pack4(b.w) << 28;
+        auto below = [](int n) {  // bits 0 .. n-1, n clamped to [0, 32]
+          return n <= 0 ? 0u : (n >= 32 ? 0xffffffffu : (1u << n) - 1u);
+        };
+        const uint32_t span_bits = below(sc_hi - key0) & ~below(sc_lo - key0);
+        const uint32_t keep = (tag_bits | span_bits) & below(kmax_row - key0);
+#pragma unroll
+        for (int e = 0; e < 32; ++e)
+          if (!((keep >> e) & 1u)) v[e] = __float_as_uint(-INFINITY);
+      } else {
 #pragma unroll
         for (int e = 0; e < 32; ++e)
           if (key0 + e >= kmax_row) v[e] = __float_as_uint(-INFINITY);
       }
+    };
+    // Masks 32 scores of keys key0 .. key0 + 31 and returns their max.
+    auto mask_max32 = [&](uint32_t (&v)[32], int key0, int kmax_row, bool full) -> float {
+      if (!full) mask32(v, key0, kmax_row);
       float mp[4];
 #pragma unroll
       for (int k = 0; k < 4; ++k) mp[k] = __uint_as_float(v[k]);
@@ -496,6 +527,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int pos = it.q0 + i;
       const int kmax_row = !live ? 0 : (p.causal ? min(it.seq_len, pos + 1) : it.seq_len);
       const int n = it.n_tiles;
+      if (kScoped) {
+        sc_tags = p.scope_tags + static_cast<int64_t>(it.s) * p.scope_stride;
+        sc_lo = live ? p.scope_lo[static_cast<int64_t>(it.s) * p.scope_stride + pos] : 0;
+        sc_hi = live ? p.scope_hi[static_cast<int64_t>(it.s) * p.scope_stride + pos] : 0;
+      }
       float m_ref = -INFINITY, l = 0.f;
       // This warp takes the item's tiles j with (g + j) % 2 == par.
       const int j0 = static_cast<int>((g ^ static_cast<uint32_t>(par)) & 1);
@@ -508,8 +544,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         tc_fence_after();
         const int key0 = j * kBN;
-        // Tiles that lie wholly below every row's key limit skip the per-key masks.
-        const bool full = __all_sync(0xffffffffu, key0 + kBN <= kmax_row);
+        // Tiles that lie wholly below every row's key limit skip the per-key masks
+        // (never with a token scope).
+        const bool full = !kScoped && __all_sync(0xffffffffu, key0 + kBN <= kmax_row);
         // Pass 1: row max over the 128 scores; keys 0..63 stay in registers.
         uint32_t sa[32], sb[32];
         tmem_ld32(lane_addr + s_col + 64, sa);
@@ -550,11 +587,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_ld32(lane_addr + s_col + 96, sb);
         tmem_wait_ld();
         if (!full) {
-#pragma unroll
-          for (int e = 0; e < 32; ++e) {
-            if (key0 + 64 + e >= kmax_row) sa[e] = __float_as_uint(-INFINITY);
-            if (key0 + 96 + e >= kmax_row) sb[e] = __float_as_uint(-INFINITY);
-          }
+          mask32(sa, key0 + 64, kmax_row);
+          mask32(sb, key0 + 96, kmax_row);
         }
         l += exp64(sa, sb, base, full, pk);
         tmem_st32(lane_addr + s_col + 32, pk);
@@ -739,17 +773,15 @@ cudaError_t launch_prefill_tc(const RowsParams& p, int dtype, cudaStream_t strea
   if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   if (e != cudaSuccess) return e;
   dim3 grid(static_cast<unsigned>(std::min<int64_t>(n_items, sms)));
-  if (dtype == 2) {
-    auto kernel = prefill_tc_kernel<__nv_bfloat16>;
-    e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
-    if (e != cudaSuccess) return e;
-    kernel<<<grid, kThreads, kSmemBytes, stream>>>(mk, mv, p, rows_per_head);
-  } else {
-    auto kernel = prefill_tc_kernel<__half>;
-    e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
-    if (e != cudaSuccess) return e;
-    kernel<<<grid, kThreads, kSmemBytes, stream>>>(mk, mv, p, rows_per_head);
-  }
+  using Kernel = void (*)(const CUtensorMap, const CUtensorMap, const RowsParams, int32_t);
+  const bool scoped = p.scope_tags != nullptr;
+  Kernel kernel = dtype == 2 ? (scoped ? prefill_tc_kernel<__nv_bfloat16, true>
+                                       : prefill_tc_kernel<__nv_bfloat16, false>)
+                             : (scoped ? prefill_tc_kernel<__half, true>
+                                       : prefill_tc_kernel<__half, false>);
+  e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+  if (e != cudaSuccess) return e;
+  kernel<<<grid, kThreads, kSmemBytes, stream>>>(mk, mv, p, rows_per_head);
   return cudaGetLastError();
 }
 

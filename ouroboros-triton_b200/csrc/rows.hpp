@@ -31,6 +31,10 @@ struct RowsParams {
   void* workspace;            // tensor-core path: rotated-key scratch (prefill_workspace_bytes)
   int64_t workspace_bytes;
   const int32_t* krot_valid;  // optional [S]: keys already rotated in the workspace
+  const uint8_t* scope_tags;  // optional token scope [S, scope_stride], 1 = GLOBAL
+  int64_t scope_stride;
+  const int32_t* scope_lo;    // [S, scope_stride]: span [lo, hi) of the token at each position
+  const int32_t* scope_hi;
 };
 
 cudaError_t launch_attend_rows_simt(const RowsParams& p, int dtype, cudaStream_t stream);

@@ -10,9 +10,9 @@ Per step, on one GPU's KV pool:
    request that does not fit waits, and the queue behind it waits too;
 2. prefill: up to ``prefill_tokens`` prompt tokens, at most ``chunk`` per
    request: stand-in QKV projection, the chunk's K/V appended to the chain
-   (kv-append kernel), causal attention of the chunk over the chain
-   (tensor-core prefill kernel); a request whose prompt completes gets its
-   first output token from the prompt's last row;
+   (kv-append kernel), causal attention of the chunk over the chain under
+   the request's token scope (tensor-core prefill kernel); a request whose
+   prompt completes gets its first output token from the prompt's last row;
 3. decode: every request past its prompt decodes one token: QKV projection of
    its last token, K/V append, paged decode attention under the request's
    token scope (decode kernel), output projection, next token;
@@ -21,9 +21,7 @@ Per step, on one GPU's KV pool:
 The model around attention is a random-init stand-in (token embedding, fused
 QKV projection, output projection and an argmax over the first ``vocab``
 hidden units as the next token): the trace exercises the allocator and the
-attention kernels, not a language model. Prompt attention is causal without
-the token scope, because the tensor-core prefill kernel takes no scope input;
-decode applies it.
+attention kernels, not a language model.
 
 The scheduler talks to a backend (``prefill`` / ``decode``), so it runs on
 the CPU against a stand-in backend in the tests.
@@ -266,13 +264,21 @@ class StandInBackend:
         self.w_o = (torch.randn(self.hq * self.d, hidden, generator=g, device=self.device)
                     * (1.0 / math.sqrt(self.hq * self.d))).to(dt)
         width = -(-max_total // 16) * 16
+        # per-slot token scope: GLOBAL tags and the span of the token at each position
         self.tags = torch.zeros(slots, width, dtype=torch.uint8, device=self.device)
+        self.span_lo = torch.zeros(slots, width, dtype=torch.int32, device=self.device)
+        self.span_hi = torch.zeros(slots, width, dtype=torch.int32, device=self.device)
         self.kv_bytes = 0
         self.attn_events = {"prefill": [], "decode": []}  # (start, end) CUDA event pairs
+        self.last_prefill = self.last_decode = None        # inputs / outputs of the last call
 
     # ---- slots ------------------------------------------------------------
     def admit(self, r: Request) -> None:
-        self.tags[r.slot, : r.total].copy_(self.torch.from_numpy(r.tags), non_blocking=False)
+        torch = self.torch
+        self.tags[r.slot].zero_()
+        self.tags[r.slot, : r.total].copy_(torch.from_numpy(r.tags))
+        self.span_lo[r.slot, : r.total].copy_(torch.from_numpy(r.span_start))
+        self.span_hi[r.slot, : r.total].copy_(torch.from_numpy(r.span_end))
 
     def release(self, r: Request) -> None:
         pass
@@ -322,9 +328,13 @@ class StandInBackend:
         st = torch.from_numpy(starts).to(dev)
         ct = torch.from_numpy(counts).to(dev)
         paged_kv_append(k, v, pt, st, ct, self.pool.k_cache, self.pool.v_cache)
+        slots = torch.tensor([r.slot for r in reqs], device=dev)
+        scope = (self.tags.index_select(0, slots), self.span_lo.index_select(0, slots),
+                 self.span_hi.index_select(0, slots))
         out = self._timed("prefill", lambda: chunked_prefill_attention(
             pt, q, self.pool.k_cache, self.pool.v_cache, st, st + ct, self.pool.cos,
-            self.pool.sin, causal=True, validate=False))
+            self.pool.sin, causal=True, validate=False, scope=scope))
+        self.last_prefill = (pt, q, st, st + ct, scope, out)
         last = out[torch.arange(n, device=dev), :, ct.long() - 1]   # [n, Hq, D]
         return self._next(last)
 

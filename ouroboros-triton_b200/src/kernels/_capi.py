@@ -54,6 +54,8 @@ class AttentionArgs(ctypes.Structure):
         ("max_positions", _i32), ("dtype", _i32), ("causal", _i32), ("kernel", _i32),
         ("softmax_scale", ctypes.c_float),
         ("workspace", _vp), ("workspace_bytes", ctypes.c_size_t), ("krot_valid", _vp),
+        ("scope_tags", _vp), ("scope_stride", ctypes.c_int64), ("scope_lo", _vp),
+        ("scope_hi", _vp),
     ]
 
 

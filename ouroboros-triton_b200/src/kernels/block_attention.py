@@ -502,8 +502,14 @@ class PrefillCall:
 
     def __init__(self, page_table, q, k_cache, v_cache, q_start, seq_lens, cos, sin, *,
                  causal: bool = True, softmax_scale=None, out=None, validate: bool = True,
-                 kernel: str = "auto", status=None, workspace=None, krot_valid=None):
-        """``workspace`` (optional uint8 device tensor) is the tensor-core path's
+                 kernel: str = "auto", status=None, workspace=None, krot_valid=None,
+                 scope=None):
+        """``scope`` (optional) is the batch's token scope ``(tags, lo, hi)``, each
+        [S, W] with W a multiple of 16 covering seq_lens (from
+        :func:`src.scoping_mask.prefill_scope`): the query at position i keeps
+        key j when tags[s, j] or lo[s, i] <= j < hi[s, i] (Table 1).
+
+        ``workspace`` (optional uint8 device tensor) is the tensor-core path's
         rotated-key scratch; pass the same tensor to the calls of one chunked
         prefill together with ``krot_valid`` ([S] int32: keys [0, krot_valid[s])
         already rotated there by an earlier call with the same caches, page-table
@@ -548,6 +554,21 @@ class PrefillCall:
         self.device = device
         self.args = _rows_args(q, False, k_cache, v_cache, pt, lens, starts, cos, sin, None, None,
                                out, status, Hq, L, causal, softmax_scale, kernel)
+        scope_keep = None
+        if scope is not None:
+            tags, lo, hi = scope
+            tags = _on(torch.as_tensor(tags), device, torch.uint8).contiguous()
+            lo = _as_int32(_on(torch.as_tensor(lo), device), "scope lo")
+            hi = _as_int32(_on(torch.as_tensor(hi), device), "scope hi")
+            if tags.dim() != 2 or tags.shape[0] != S or tags.shape[1] % 16 != 0:
+                raise RuntimeError(f"scope tags must be [S={S}, W] with W a multiple of 16")
+            if lo.shape != tags.shape or hi.shape != tags.shape:
+                raise RuntimeError("scope lo / hi must have the shape of the tags")
+            if tags.shape[1] < int(lens.max().item()):
+                raise RuntimeError("scope arrays must cover every sequence length")
+            self.args.scope_tags, self.args.scope_stride = _ptr(tags), tags.shape[1]
+            self.args.scope_lo, self.args.scope_hi = _ptr(lo), _ptr(hi)
+            scope_keep = (tags, lo, hi)
         need, tc = ctypes.c_size_t(), ctypes.c_int32()
         _native.check(_native.lib().ouro_attention_plan(ctypes.byref(self.args),
                                                         ctypes.byref(need), ctypes.byref(tc)),
@@ -569,7 +590,8 @@ class PrefillCall:
             if tuple(krot_valid.shape) != (S,):
                 raise RuntimeError(f"krot_valid must have shape [{S}]")
             self.args.krot_valid = _ptr(krot_valid)
-        self._keep = (q, k_cache, v_cache, pt, lens, starts, cos, sin, status, krot_valid)
+        self._keep = (q, k_cache, v_cache, pt, lens, starts, cos, sin, status, krot_valid,
+                      scope_keep)
 
     def launch(self):
         _launch_rows(self.args, self.device)
@@ -579,7 +601,7 @@ class PrefillCall:
 def chunked_prefill_attention(page_table, q, k_cache, v_cache, q_start, seq_lens, cos, sin, *,
                               causal: bool = True, softmax_scale=None, out=None,
                               validate: bool = True, kernel: str = "auto", status=None,
-                              workspace=None, krot_valid=None):
+                              workspace=None, krot_valid=None, scope=None):
     """Chunked prefill: q [S, Hq, L, D] rows at positions q_start[s] + i.
 
     Keys are every paged token j < seq_lens[s] (the chunk's own K/V already
@@ -588,12 +610,12 @@ def chunked_prefill_attention(page_table, q, k_cache, v_cache, q_start, seq_lens
     zero. fp16/bf16 with head_dim 128 run on the tcgen05 tensor-core kernel;
     other shapes and fp32 on CUDA cores. Returns [S, Hq, L, D] in the cache dtype.
     ``workspace`` / ``krot_valid``: reuse of the rotated-key scratch across the
-    chunks of one prefill (see :class:`PrefillCall`).
+    chunks of one prefill; ``scope``: the token scope (see :class:`PrefillCall`).
     """
     return PrefillCall(page_table, q, k_cache, v_cache, q_start, seq_lens, cos, sin,
                        causal=causal, softmax_scale=softmax_scale, out=out, validate=validate,
                        kernel=kernel, status=status, workspace=workspace,
-                       krot_valid=krot_valid).launch()
+                       krot_valid=krot_valid, scope=scope).launch()
 
 
 def paged_kv_append(k_new, v_new, page_table, start, counts, k_cache, v_cache, *, status=None):

@@ -38,6 +38,7 @@ __all__ = [
     "decode_scope",
     "scope_allowed",
     "scope_bias",
+    "prefill_scope",
 ]
 
 GLOBAL = "global"
@@ -109,6 +110,31 @@ def decode_scope(spans, query_pos: int):
     if tags[query_pos]:
         return tags, 0, 0
     return tags, int(start[query_pos]), int(end[query_pos])
+
+
+def prefill_scope(spans_per_seq, width: int | None = None):
+    """Token scope of a batch for multi-row attention (chunked prefill).
+
+    Returns ``(tags uint8 [S, W], lo int32 [S, W], hi int32 [S, W])`` with W
+    the longest extent rounded up to 16 (or ``width``): tags[s, j] = 1 for a
+    GLOBAL token, and [lo, hi) the span of the token at each position. The
+    query at position i keeps key j when tags[j] or lo[i] <= j < hi[i]: its
+    Table-1 row (a GLOBAL query's own span holds only GLOBAL tokens).
+    """
+    enc = [token_scope(sp) for sp in spans_per_seq]
+    longest = max((t.shape[0] for t, _, _ in enc), default=0)
+    W = width if width is not None else max(16, -(-longest // 16) * 16)
+    if W < longest or W % 16:
+        raise ValueError(f"width {W} must be a multiple of 16 covering {longest} tokens")
+    S = len(enc)
+    tags = np.zeros((S, W), dtype=np.uint8)
+    lo = np.zeros((S, W), dtype=np.int32)
+    hi = np.zeros((S, W), dtype=np.int32)
+    for s, (t, a, b) in enumerate(enc):
+        tags[s, : t.shape[0]] = t
+        lo[s, : t.shape[0]] = a
+        hi[s, : t.shape[0]] = b
+    return tags, lo, hi
 
 
 def scope_allowed(spans) -> np.ndarray:

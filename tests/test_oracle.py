@@ -165,3 +165,50 @@ def test_prefill_restatement_equals_dense_rows_with_causal_bias():
     for s in range(2):
         n = min(86, lens[s] - 64)
         assert np.abs(got[s, :, :n] - full[s, :, 64:64 + n]).max() < 2e-5
+
+
+def test_prefill_restatement_with_scope_equals_dense_rows_with_table1_bias():
+    """Scoped prefill rows (tags / per-position spans) equal the dense restatement
+    with the Table-1 mask of scoping_mask plus causality as an additive bias."""
+    from src.scoping_mask import prefill_scope, scope_bias
+
+    c = cases.small_full_case(torch, BlockTable, 13, lens=(192, 150), num_heads=2, head_dim=32)
+    rows, lens = np.asarray(c["rows"]), c["lens"]
+    qc, kc, vc = _np(c["q_cache"]), _np(c["k_cache"]), _np(c["v_cache"])
+    cos, sin = _np(c["cos"]), _np(c["sin"])
+    spans = [[(0, 40, "global"), (40, 100, "local"), (100, 130, "global"), (130, 192, "local")],
+             [(0, 70, "local"), (70, 90, "global"), (90, 150, "local")]]
+    tags, lo, hi = prefill_scope(spans)
+    L = max(lens)
+    bias = np.full((2, 1, L, L), -np.inf, np.float32)
+    for s in range(2):
+        n = lens[s]
+        b = scope_bias(spans[s]) + np.where(np.tril(np.ones((n, n), bool)), 0.0, -np.inf)
+        bias[s, 0, :n, :n] = b
+    full = ao.dense_attention(rows, qc, kc, vc, lens, cos, sin, bias=bias)
+    q = np.zeros((2, 2, 86, 32), np.float32)
+    for s in range(2):
+        for i in range(86):
+            p = 64 + i
+            if p < lens[s]:
+                q[s, :, i] = qc[rows[s][p // 64], :, p % 64]
+    got = ao.prefill_attention(rows, q, kc, vc, [64, 64], lens, cos, sin, causal=True,
+                               scope_tags=tags, scope_lo=lo, scope_hi=hi)
+    for s in range(2):
+        n = min(86, lens[s] - 64)
+        assert np.abs(got[s, :, :n] - full[s, :, 64:64 + n]).max() < 2e-5
+
+
+def test_prefill_scope_arrays_follow_token_scope():
+    from src.scoping_mask import prefill_scope, token_scope
+
+    spans = [[(0, 5, "local"), (5, 9, "global")], [(0, 20, "global")]]
+    tags, lo, hi = prefill_scope(spans)
+    assert tags.shape == (2, 32) and tags.dtype == np.uint8 and lo.dtype == np.int32
+    for s, sp in enumerate(spans):
+        t, a, b = token_scope(sp)
+        n = t.shape[0]
+        assert (tags[s, :n] == t).all() and (lo[s, :n] == a).all() and (hi[s, :n] == b).all()
+        assert not tags[s, n:].any()
+    with pytest.raises(ValueError):
+        prefill_scope(spans, width=24)

@@ -125,6 +125,32 @@ def test_chunked_prefill_reuses_rotated_keys(cuda):
                 k[pt[s, b]] = 7.0
 
 
+@pytest.mark.parametrize("hq,hkv,dtype,kernel", [
+    (32, 8, torch.bfloat16, "tc"), (16, 2, torch.float16, "tc"), (8, 4, torch.float32, "simt")])
+def test_prefill_with_token_scope_vs_oracle(cuda, hq, hkv, dtype, kernel):
+    """Table-1 token scope (GLOBAL tags + each query position's LOCAL span) on
+    top of causality, chunks starting mid-sequence, ragged lengths."""
+    from src.scoping_mask import prefill_scope
+    from src.engine import random_segments
+
+    rng = random.Random(hq + hkv)
+    L = 384
+    totals = [1000, 400, 777, 1300]
+    starts = [600, 0, 700, 1000]
+    spans = [random_segments(rng, t) for t in totals]
+    tags, lo, hi = prefill_scope(spans)
+    d = 128 if kernel == "tc" else 64
+    pt, q, k, v, cos, sin = _case(77 + hq, totals, hq, hkv, L, dtype, d=d)
+    out = _run(pt, q, k, v, starts, totals, cos, sin, causal=True, kernel=kernel,
+               scope=(torch.from_numpy(tags), torch.from_numpy(lo), torch.from_numpy(hi)))
+    want = ao.prefill_attention(pt, q.float().cpu().numpy(), k.float().cpu().numpy(),
+                                v.float().cpu().numpy(), starts, totals, cos, sin, causal=True,
+                                scope_tags=tags, scope_lo=lo, scope_hi=hi)
+    tol = (2e-2, 2e-3) if dtype != torch.float32 else (1e-4, 1e-5)
+    err = np.abs(out.float().cpu().numpy() - want)
+    assert err.max() <= tol[0] and err.mean() <= tol[1], (err.max(), err.mean())
+
+
 def test_tensor_cores_agree_with_cuda_cores(cuda):
     L, starts, totals = 256, [64, 700], [320, 956]
     pt, q, k, v, cos, sin = _case(7, totals, 32, 8, L, torch.bfloat16)
