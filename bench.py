@@ -530,6 +530,105 @@ def run_prefill(args):
     return 0
 
 
+SCOPED = dict(workload="mha_paged_decode_fp16_scoped", seqs=32, heads=32, head_dim=128,
+              dtype="fp16", ctx_min=512, ctx_max=4096, pool_blocks=4096, rope_base=10000.0,
+              segment_min=32, segment_max=512, seed=2)
+
+
+def run_decode_scoped(args):
+    """Scoped MHA decode (fp16, 32 sequences, lens U[512, 4096], 4096-block pool, Table-1
+    scope from random segments: the first GLOBAL, later ones LOCAL with p = 1/2).
+
+    Times the scoped decode, then the same batch unscoped. A block with no allowed key for
+    the query is never loaded, so the scoped step reads only the blocks its scopes reach:
+    ``bytes_needed`` counts those, ``bytes_all_keys`` every cached key.
+    """
+    import numpy as np
+    import torch
+
+    from oracle import attention_oracle as ao  # RoPE tables and the spot check
+    from src.block_table import BlockTable
+    from src.engine import random_segments
+    from src.kernels.block_attention import DecodeCall
+    from src.scoping_mask import decode_scope
+
+    P = SCOPED
+    device = torch.device("cuda", 0)
+    rng = random.Random(P["seed"])
+    S, H, D = P["seqs"], P["heads"], P["head_dim"]
+    lens = [rng.randint(P["ctx_min"], P["ctx_max"]) for _ in range(S)]
+    bt = BlockTable(P["pool_blocks"])
+    ids = [bt.allocate_block() for _ in range(P["pool_blocks"])]
+    rng.shuffle(ids)
+    for i in ids:
+        bt.free_block(i)
+    heads = [bt.allocate_chain(-(-n // 64)) for n in lens]
+    pt = torch.from_numpy(bt.export_page_table(heads, -(-P["ctx_max"] // 64))).to(device)
+    g = torch.Generator(device=device).manual_seed(P["seed"])
+    k = (torch.randn(P["pool_blocks"], H, 64, D, generator=g, device=device) * 0.5).half()
+    v = (torch.randn(P["pool_blocks"], H, 64, D, generator=g, device=device) * 0.5).half()
+    q = (torch.randn(S, H, D, generator=g, device=device) * 0.5).half()
+    cos, sin = ao.rope_tables(P["ctx_max"], D, P["rope_base"])
+    cos_d, sin_d = torch.from_numpy(cos).to(device), torch.from_numpy(sin).to(device)
+    W = -(-P["ctx_max"] // 16) * 16
+    tags = np.zeros((S, W), np.uint8)
+    span = np.zeros((S, 2), np.int32)
+    needed_tok = 0
+    for s, n in enumerate(lens):
+        t, lo, hi = decode_scope(random_segments(rng, n, P["segment_min"], P["segment_max"]), n - 1)
+        tags[s, :n] = t
+        span[s] = (lo, hi)
+        for b in range(-(-n // 64)):
+            a, e = b * 64, min(n, b * 64 + 64)
+            if t[a:e].any() or (a < hi and e > lo):
+                needed_tok += e - a
+    lens_d = torch.tensor(lens, dtype=torch.int32, device=device)
+    status = torch.zeros(1, dtype=torch.int32, device=device)
+    scope = (torch.from_numpy(tags).to(device), torch.from_numpy(span).to(device))
+    calls = {"scoped": DecodeCall(pt, q, k, v, lens_d, cos_d, sin_d, scope=scope, status=status),
+             "unscoped": DecodeCall(pt, q, k, v, lens_d, cos_d, sin_d, status=status)}
+    per_tok = H * D * 2 * 2
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=device)
+    res = {}
+    for name, call in calls.items():
+        for _ in range(max(args.warmup, 3)):
+            call.launch()
+        torch.cuda.synchronize()
+        total = 0.0
+        for _ in range(args.steps):
+            flush.zero_()  # the batch (1.2 GB) exceeds L2 anyway; flushed so no step starts warm
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            call.launch()
+            e1.record()
+            torch.cuda.synchronize()
+            total += e0.elapsed_time(e1)
+        res[name] = total / args.steps
+    out = calls["scoped"].out
+    want = ao.decode_attention(pt[:4].cpu().numpy(), q[:4].float().cpu().numpy(),
+                               k.float().cpu().numpy(), v.float().cpu().numpy(), lens[:4], cos,
+                               sin, scope_tags=tags[:4], scope_span=span[:4])
+    err = np.abs(out[:4].float().cpu().numpy() - want)
+    hbm, src = _peaks()
+    ms = res["scoped"]
+    gbs = needed_tok * per_tok / (ms / 1000.0) / 1e9
+    line = {
+        "metric": "scoped MHA paged-decode tokens/s (fp16, Table-1 scope)", "value": S / (ms / 1000.0),
+        "unit": "tokens/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": ms, "higher_is_better": True, "dtype": "fp16",
+        "data": "synthetic (seeded; random K/V/Q and segments)", "config": P,
+        "bytes_all_keys": sum(lens) * per_tok, "bytes_needed": needed_tok * per_tok,
+        "unscoped_ms_per_step": res["unscoped"],
+        "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm, "unit": "GB/s",
+                     "frac": gbs / hbm, "peak_source": src,
+                     "note": "bytes of the blocks the scopes reach / scoped step time"},
+        "check": {"rows": 4, "max_abs": float(err.max()), "mean_abs": float(err.mean()),
+                  "kernel_status": int(status.item())},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 SERVING = dict(workload="serving_trace_llama3_8b_attention", requests=512, rate_per_s=64.0,
                prompt_median=2048, prompt_sigma=1.0, prompt_min=128, prompt_max=16384,
                output_tokens=256, q_heads=32, kv_heads=8, head_dim=128, hidden=4096, dtype="bf16",
@@ -637,9 +736,11 @@ def main() -> int:
     ap.add_argument("--split-blocks", type=int, default=0)
     ap.add_argument("--kernel", default="auto", choices=["auto", "tc", "simt"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
-    ap.add_argument("--workload", choices=["decode", "prefill", "serving"], default="decode",
+    ap.add_argument("--workload", choices=["decode", "prefill", "serving", "decode-scoped"],
+                    default="decode",
                     help="decode (the headline metric), the chunked-prefill tensor-core pass, "
-                         "or the serving trace (continuous batching end to end)")
+                         "the serving trace (continuous batching end to end) or the scoped "
+                         "MHA decode")
     ap.add_argument("--seqs", type=int, default=0,
                     help="sequences per GPU (default: the workload's 256); smaller values "
                          "make a profiling case of the same kernel")
@@ -650,6 +751,8 @@ def main() -> int:
         return run_prefill(args)
     if args.workload == "serving":
         return run_serving(args)
+    if args.workload == "decode-scoped":
+        return run_decode_scoped(args)
     return run_ours(args)
 
 

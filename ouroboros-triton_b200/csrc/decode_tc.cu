@@ -3,8 +3,9 @@
 //
 // Work: one CTA per (split-K chunk, group of HPC KV heads, sequence), 2 warps
 // per KV head.
-//   * Warp 0 builds the chunk's block list from the page table and the block
-//     mask (masked blocks are skipped, never loaded) and primes a STAGES-deep
+//   * Warp 0 builds the chunk's block list from the page table, the block
+//     mask and the token scope (blocks without an allowed key are skipped,
+//     never loaded) and primes a STAGES-deep
 //     ring of 16-token stages: for every KV head the K and V rows of the 16
 //     tokens (each a contiguous 4 KB run of the [n_phys, Hkv, 64, D] cache)
 //     plus the cos/sin rows of their positions, all TMA tiles with 128-byte
@@ -163,7 +164,18 @@ __global__ void __launch_bounds__(HPC * kWph * 32, 1)
   const int last_sub = min(4, (g.kv_len - (g.nb - 1) * kBlock + kTok - 1) / kTok);
 
   if (warp == 0) {
-    // Block list: allowed blocks of this chunk with their physical ids.
+    // Block list: allowed blocks of this chunk with their physical ids. With a
+    // token scope, a block with no GLOBAL token that does not meet the query's
+    // span holds no allowed key and is skipped too (its K/V are never loaded).
+    int sc_lo = 0, sc_hi = 0;
+    const uint8_t* sc_row = nullptr;
+    if (p.scope_tags != nullptr) {
+      sc_row = p.scope_tags + static_cast<int64_t>(s) * p.scope_stride;
+      if (p.scope_span) {
+        sc_lo = p.scope_span[2 * s];
+        sc_hi = p.scope_span[2 * s + 1];
+      }
+    }
     int n = 0;
     for (int base = b_begin; base < b_end; base += 32) {
       const int b = base + lane;
@@ -171,6 +183,18 @@ __global__ void __launch_bounds__(HPC * kWph * 32, 1)
       int phys = 0;
       if (keep && p.block_mask != nullptr)
         keep = p.block_mask[s * p.mask_s + qb * p.mask_q + b * p.mask_k] != 0;
+      if (keep && sc_row != nullptr && !(b * kBlock < sc_hi && (b + 1) * kBlock > sc_lo)) {
+        uint32_t any = 0;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const int64_t off = static_cast<int64_t>(b) * kBlock + 16 * c;
+          if (off < p.scope_stride) {
+            const uint4 t = *reinterpret_cast<const uint4*>(sc_row + off);
+            any |= t.x | t.y | t.z | t.w;
+          }
+        }
+        keep = any != 0;
+      }
       if (keep) {
         phys = p.page_table[static_cast<int64_t>(s) * p.max_blocks + b];
         if (phys < 0 || phys >= p.n_phys) {

@@ -263,3 +263,42 @@ def test_tc_pipeline_under_load_reports_clean_status(cuda):
                                        v.index_select(0, sel).float().cpu().numpy(), [lens[s]],
                                        cos, sin)
             _close_half(out[s:s + 1], want, f"stress seq {s} split {split}")
+
+
+@pytest.mark.parametrize("split_blocks", [0, 3])
+def test_scope_skips_disallowed_blocks_vs_oracle(cuda, split_blocks):
+    """Scopes that leave most blocks without an allowed key (long LOCAL
+    segments away from the query, sparse GLOBAL tokens): the tensor-core
+    kernel drops those blocks before loading them, split-K chunks can end up
+    empty, and the rows still match the oracle."""
+    rng = random.Random(21)
+    lens = [5000, 3100, 64, 900, 7777, 130]
+    pool = sum(-(-n // 64) for n in lens) + 5
+    bt = BlockTable(pool)
+    heads = [bt.allocate_chain(-(-n // 64)) for n in lens]
+    pt = build_page_table_array(bt, heads)
+    g = torch.Generator(device="cuda").manual_seed(21)
+    k = (torch.randn(pool, 8, 64, 128, generator=g, device="cuda") * 0.5).to(torch.bfloat16)
+    v = (torch.randn(pool, 8, 64, 128, generator=g, device="cuda") * 0.5).to(torch.bfloat16)
+    q = (torch.randn(len(lens), 32, 128, generator=g, device="cuda") * 0.5).to(torch.bfloat16)
+    W = -(-max(lens) // 16) * 16
+    tags = np.zeros((len(lens), W), np.uint8)
+    span = np.zeros((len(lens), 2), np.int32)
+    for s, n in enumerate(lens):
+        for j in rng.sample(range(n), max(1, n // 700)):   # a few GLOBAL tokens
+            tags[s, j] = 1
+        if s % 2 == 0:                                     # LOCAL query: its own segment
+            span[s] = (max(0, n - rng.randint(1, 300)), n)
+        else:                                              # GLOBAL query: itself GLOBAL
+            tags[s, n - 1] = 1
+    cos, sin = ao.rope_tables(pt.shape[1] * 64, 128, 500000.0)
+    out = ba.block_attention_decode(torch.from_numpy(pt).cuda(), q, k, v,
+                                    torch.tensor(lens).cuda(), torch.from_numpy(cos).cuda(),
+                                    torch.from_numpy(sin).cuda(),
+                                    scope=(torch.from_numpy(tags), torch.from_numpy(span)),
+                                    kernel="tc", split_blocks=split_blocks)
+    want = ao.decode_attention(pt, q.float().cpu().numpy(), k.float().cpu().numpy(),
+                               v.float().cpu().numpy(), lens, cos, sin, scope_tags=tags,
+                               scope_span=span)
+    err = np.abs(out.float().cpu().numpy() - want)
+    assert err.max() <= 2e-2 and err.mean() <= 2e-3, (err.max(), err.mean())
