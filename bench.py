@@ -681,7 +681,8 @@ def run_serving(args):
     if world > 1:
         dist.barrier()
     with ClockSampler(device.index) as clk:
-        st = eng.run(mine, sync=None)
+        # one synchronize per step: token times are completion times
+        st = eng.run(mine, sync=lambda: torch.cuda.synchronize(device))
         torch.cuda.synchronize(device)
     dec_ms, pre_ms = be.attn_ms("decode"), be.attn_ms("prefill")
     vals = torch.tensor([st["generated_tokens"], st["wall_s"], be.kv_bytes, dec_ms],

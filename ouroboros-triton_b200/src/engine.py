@@ -23,8 +23,12 @@ QKV projection, output projection and an argmax over the first ``vocab``
 hidden units as the next token): the trace exercises the allocator and the
 attention kernels, not a language model.
 
-The scheduler talks to a backend (``prefill`` / ``decode``), so it runs on
-the CPU against a stand-in backend in the tests.
+The scheduler talks to a backend (``admit`` / ``prefill`` / ``decode`` /
+``release``), so it runs on the CPU against a stand-in backend in the tests.
+It needs token counts, never token values, and hands the backend each chain
+once, at admission: the GPU backend keeps page-table rows, scopes and last
+tokens resident per slot, so a step costs one small host-to-device copy of
+its indices and no page-table rebuild.
 """
 
 from __future__ import annotations
@@ -132,11 +136,12 @@ class Engine:
             r.slot = self.free_slots.pop()
             r.tags, r.span_start, r.span_end = token_scope(r.spans)
             r.admit_time = now
-            self.backend.admit(r)
+            self.backend.admit(r, list(self.table.walk(r.head)))
             self.running.append(r)
             self.waiting.popleft()
 
-    def _page_table(self, reqs):
+    def page_table(self, reqs):
+        """Host page table of ``reqs`` (one native export; the GPU backend keeps its own)."""
         width = max(self.table.chain_len(r.head) for r in reqs)
         return self.table.export_page_table([r.head for r in reqs], width)
 
@@ -155,19 +160,21 @@ class Engine:
                 budget -= c
         dec = [r for r in self.running if r.done_prompt == r.prompt_len and 0 < r.generated < r.max_new]
         if pre:
-            tokens = self.backend.prefill(pre, self._page_table(pre), np.asarray(starts, np.int32),
+            tokens = self.backend.prefill(pre, np.asarray(starts, np.int32),
                                           np.asarray(counts, np.int32))
-            for r, c, tok in zip(pre, counts, tokens):
+            for i, (r, c) in enumerate(zip(pre, counts)):
                 r.done_prompt += c
                 if r.done_prompt == r.prompt_len:
-                    r.last_token = int(tok)
+                    if tokens is not None:
+                        r.last_token = int(tokens[i])
                     r.generated = 1
                     r.first_token_time = now
         if dec:
             pos = np.asarray([r.prompt_len + r.generated - 1 for r in dec], np.int32)
-            tokens = self.backend.decode(dec, self._page_table(dec), pos)
-            for r, tok in zip(dec, tokens):
-                r.last_token = int(tok)
+            tokens = self.backend.decode(dec, pos)
+            for i, r in enumerate(dec):
+                if tokens is not None:
+                    r.last_token = int(tokens[i])
                 r.generated += 1
         if pre or dec:
             self.steps += 1
@@ -241,8 +248,11 @@ class StandInBackend:
     projection [hidden, (Hq + 2 Hkv) D], output projection [Hq D, hidden]. A
     prompt token's id is a fixed hash of (request, position); the next token
     is the argmax over the first ``vocab`` units of the projected attention
-    output. Decode attention reads every cached key of the running requests:
-    ``kv_bytes`` counts those bytes and ``attn_ms`` the attention kernels'
+    output. Per slot, on the device: the chain's page-table row (written at
+    admission, PAD past it), the token scope (tags and per-position spans)
+    and the last token. A step uploads its indices once (pinned buffer,
+    asynchronous copy) and reads nothing back. ``kv_bytes`` counts the cached
+    bytes decode attention covers and ``attn_ms`` the attention launches'
     device time (CUDA events on the launching stream).
     """
 
@@ -264,17 +274,30 @@ class StandInBackend:
         self.w_o = (torch.randn(self.hq * self.d, hidden, generator=g, device=self.device)
                     * (1.0 / math.sqrt(self.hq * self.d))).to(dt)
         width = -(-max_total // 16) * 16
-        # per-slot token scope: GLOBAL tags and the span of the token at each position
-        self.tags = torch.zeros(slots, width, dtype=torch.uint8, device=self.device)
-        self.span_lo = torch.zeros(slots, width, dtype=torch.int32, device=self.device)
-        self.span_hi = torch.zeros(slots, width, dtype=torch.int32, device=self.device)
+        self.max_blocks = -(-max_total // BLOCK_SIZE)
+        dev = self.device
+        # per-slot state: page-table row, token scope (GLOBAL tags, span of the token at each
+        # position), last token
+        self.pt = torch.full((slots, self.max_blocks), -1, dtype=torch.int32, device=dev)
+        self.tags = torch.zeros(slots, width, dtype=torch.uint8, device=dev)
+        self.span_lo = torch.zeros(slots, width, dtype=torch.int32, device=dev)
+        self.span_hi = torch.zeros(slots, width, dtype=torch.int32, device=dev)
+        self.last_tok = torch.zeros(slots, dtype=torch.int64, device=dev)
+        # per-step indices: two pinned staging buffers, each reused once the copy that
+        # last read it has completed
+        self._stage = [torch.empty(8 * slots, dtype=torch.int32, pin_memory=True) for _ in range(2)]
+        self._stage_done = [None, None]
+        self._flip = 0
         self.kv_bytes = 0
         self.attn_events = {"prefill": [], "decode": []}  # (start, end) CUDA event pairs
         self.last_prefill = self.last_decode = None        # inputs / outputs of the last call
 
     # ---- slots ------------------------------------------------------------
-    def admit(self, r: Request) -> None:
+    def admit(self, r: Request, blocks) -> None:
         torch = self.torch
+        row = torch.full((self.max_blocks,), -1, dtype=torch.int32)
+        row[: len(blocks)] = torch.tensor(blocks, dtype=torch.int32)
+        self.pt[r.slot].copy_(row)
         self.tags[r.slot].zero_()
         self.tags[r.slot, : r.total].copy_(torch.from_numpy(r.tags))
         self.span_lo[r.slot, : r.total].copy_(torch.from_numpy(r.span_start))
@@ -282,6 +305,23 @@ class StandInBackend:
 
     def release(self, r: Request) -> None:
         pass
+
+    def _upload(self, cols):
+        """int32 host columns of equal length -> device [len(cols), n] in one async copy."""
+        torch = self.torch
+        n = len(cols[0])
+        buf = self._stage[self._flip]
+        if self._stage_done[self._flip] is not None:
+            self._stage_done[self._flip].synchronize()
+        host = buf[: len(cols) * n].view(len(cols), n)
+        for i, c in enumerate(cols):
+            host[i].copy_(torch.from_numpy(np.ascontiguousarray(c, dtype=np.int32)))
+        dev = host.to(self.device, non_blocking=True)
+        ev = torch.cuda.Event()
+        ev.record()
+        self._stage_done[self._flip] = ev
+        self._flip ^= 1
+        return dev
 
     # ---- model pieces -------------------------------------------------------
     def _qkv(self, tokens):
@@ -291,9 +331,9 @@ class StandInBackend:
         return qkv[..., : self.hq, :], qkv[..., self.hq: self.hq + self.hkv, :], qkv[..., self.hq + self.hkv:, :]
 
     def _next(self, o):
-        """o [n, Hq, D] -> next token ids [n] (host)."""
+        """o [n, Hq, D] -> next token ids [n] (device)."""
         h = o.reshape(o.shape[0], -1) @ self.w_o
-        return h[:, : self.vocab].float().argmax(dim=1).cpu().numpy()
+        return h[:, : self.vocab].float().argmax(dim=1)
 
     def _timed(self, kind, fn):
         torch = self.torch
@@ -311,24 +351,23 @@ class StandInBackend:
         return sum(a.elapsed_time(b) for k in kinds for a, b in self.attn_events[k])
 
     # ---- backend interface ---------------------------------------------------
-    def prefill(self, reqs, page_table, starts, counts):
+    def prefill(self, reqs, starts, counts):
         from .kernels.block_attention import chunked_prefill_attention, paged_kv_append
 
         torch = self.torch
         dev = self.device
         n, Lc = len(reqs), int(counts.max())
-        rid = torch.tensor([r.rid for r in reqs], device=dev)[:, None]
-        pos = torch.from_numpy(starts).to(dev)[:, None].long() + torch.arange(Lc, device=dev)[None, :]
-        tokens = (rid * 7919 + pos * 104729) % self.vocab
+        done = np.asarray([s + c == r.prompt_len for r, s, c in zip(reqs, starts, counts)], np.int32)
+        idx = self._upload([[r.slot for r in reqs], [r.rid for r in reqs], starts, counts, done])
+        slots, rids, st, ct, fin = idx[0], idx[1], idx[2], idx[3], idx[4]
+        pos = st[:, None].long() + torch.arange(Lc, device=dev)[None, :]
+        tokens = (rids[:, None].long() * 7919 + pos * 104729) % self.vocab
         q, k, v = self._qkv(tokens)                          # [n, Lc, H, D]
         q = q.permute(0, 2, 1, 3).contiguous()
         k = k.permute(0, 2, 1, 3).contiguous()
         v = v.permute(0, 2, 1, 3).contiguous()
-        pt = torch.from_numpy(page_table).to(dev)
-        st = torch.from_numpy(starts).to(dev)
-        ct = torch.from_numpy(counts).to(dev)
+        pt = self.pt.index_select(0, slots)
         paged_kv_append(k, v, pt, st, ct, self.pool.k_cache, self.pool.v_cache)
-        slots = torch.tensor([r.slot for r in reqs], device=dev)
         scope = (self.tags.index_select(0, slots), self.span_lo.index_select(0, slots),
                  self.span_hi.index_select(0, slots))
         out = self._timed("prefill", lambda: chunked_prefill_attention(
@@ -336,30 +375,35 @@ class StandInBackend:
             self.pool.sin, causal=True, validate=False, scope=scope))
         self.last_prefill = (pt, q, st, st + ct, scope, out)
         last = out[torch.arange(n, device=dev), :, ct.long() - 1]   # [n, Hq, D]
-        return self._next(last)
+        nxt = self._next(last)
+        # requests whose prompt is complete take their first output token
+        self.last_tok.index_copy_(0, slots.long(),
+                                  torch.where(fin != 0, nxt, self.last_tok.index_select(0, slots)))
+        return None
 
-    def decode(self, reqs, page_table, pos):
+    def decode(self, reqs, pos):
         from .kernels.block_attention import block_attention_decode, paged_kv_append
 
         torch = self.torch
         dev = self.device
         n = len(reqs)
-        tokens = torch.tensor([r.last_token for r in reqs], device=dev)
-        q, k, v = self._qkv(tokens)                          # [n, H, D]
-        pt = torch.from_numpy(page_table).to(dev)
-        start = torch.from_numpy(pos).to(dev)
+        spans = [r.scope_span(int(p)) for r, p in zip(reqs, pos)]
+        idx = self._upload([[r.slot for r in reqs], pos, [a for a, _ in spans],
+                            [b for _, b in spans]])
+        slots, start = idx[0], idx[1]
+        span = idx[2:4].t().contiguous()
+        q, k, v = self._qkv(self.last_tok.index_select(0, slots))   # [n, H, D]
+        pt = self.pt.index_select(0, slots)
         paged_kv_append(k[:, :, None].contiguous(), v[:, :, None].contiguous(), pt, start,
                         torch.ones(n, dtype=torch.int32, device=dev), self.pool.k_cache,
                         self.pool.v_cache)
         lens = start + 1
-        slots = torch.tensor([r.slot for r in reqs], device=dev)
         tags = self.tags.index_select(0, slots)
-        span = torch.tensor([r.scope_span(int(p)) for r, p in zip(reqs, pos)],
-                            dtype=torch.int32).to(dev)
         out = self._timed("decode", lambda: block_attention_decode(
             pt, q.contiguous(), self.pool.k_cache, self.pool.v_cache, lens, self.pool.cos,
             self.pool.sin, scope=(tags, span), validate=False))
         self.kv_bytes += int(pos.astype(np.int64).sum() + n) * self.hkv * self.d * 2 * \
             self.pool.k_cache.element_size()
         self.last_decode = (pt, q, lens, tags, span, out)
-        return self._next(out)
+        self.last_tok.index_copy_(0, slots.long(), self._next(out))
+        return None

@@ -18,13 +18,15 @@ from src.scoping_mask import GLOBAL, LOCAL, token_scope
 
 
 class RecordingBackend:
-    def __init__(self, table):
+    def __init__(self, table, engine=None):
         self.table = table
+        self.engine = engine
         self.admitted, self.released = [], []
         self.pos = {}            # rid -> next position expected
         self.prefill_calls = self.decode_calls = 0
 
-    def admit(self, r):
+    def admit(self, r, blocks):
+        assert blocks == list(self.table.walk(r.head)) and len(blocks) == r.blocks
         self.admitted.append(r.rid)
         self.pos[r.rid] = 0
 
@@ -37,17 +39,17 @@ class RecordingBackend:
             assert row == list(self.table.walk(r.head))
             assert len(row) * BLOCK_SIZE >= e, (r.rid, len(row), e)
 
-    def prefill(self, reqs, pt, starts, counts):
+    def prefill(self, reqs, starts, counts):
         self.prefill_calls += 1
-        self._rows_cover(reqs, pt, starts + counts)
+        self._rows_cover(reqs, self.engine.page_table(reqs), starts + counts)
         for r, s, c in zip(reqs, starts, counts):
             assert s == self.pos[r.rid] and 0 < c
             self.pos[r.rid] = s + c
         return [(r.rid * 31 + int(s)) % 97 for r, s in zip(reqs, starts)]
 
-    def decode(self, reqs, pt, pos):
+    def decode(self, reqs, pos):
         self.decode_calls += 1
-        self._rows_cover(reqs, pt, pos + 1)
+        self._rows_cover(reqs, self.engine.page_table(reqs), pos + 1)
         for r, p in zip(reqs, pos):
             assert p == self.pos[r.rid] == r.prompt_len + r.generated - 1
             assert p < r.total
@@ -96,6 +98,7 @@ def test_engine_serves_every_request_and_frees_every_block(pool_blocks, chunk, b
     table = BlockTable(pool_blocks)
     be = RecordingBackend(table)
     eng = Engine(table, be, chunk=chunk, prefill_tokens=budget, slots=64)
+    be.engine = eng
     clock = FakeClock(0.002)
     st = eng.run(tr, clock=clock, sleep=clock.sleep)
     assert st["requests"] == 40 and st["generated_tokens"] == sum(r.max_new for r in tr)
@@ -115,11 +118,13 @@ def test_engine_prefill_respects_chunk_and_budget():
     seen = []
 
     class B(RecordingBackend):
-        def prefill(self, reqs, pt, starts, counts):
+        def prefill(self, reqs, starts, counts):
             seen.append(list(counts))
-            return super().prefill(reqs, pt, starts, counts)
+            return super().prefill(reqs, starts, counts)
 
-    eng = Engine(table, B(table), chunk=512, prefill_tokens=900)
+    be = B(table)
+    eng = Engine(table, be, chunk=512, prefill_tokens=900)
+    be.engine = eng
     clock = FakeClock(0.001)
     eng.run(tr, clock=clock, sleep=clock.sleep)
     assert all(max(c) <= 512 and sum(c) <= 900 for c in seen)
@@ -132,6 +137,7 @@ def test_admission_waits_for_free_blocks():
     table = BlockTable(62)                 # room for big (61 blocks) but not both at once
     be = RecordingBackend(table)
     eng = Engine(table, be, chunk=4096, prefill_tokens=8192)
+    be.engine = eng
     eng.submit([big, small])
     eng.step(0.0)
     assert [r.rid for r in eng.running] == [0] and len(eng.waiting) == 1
