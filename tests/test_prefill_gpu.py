@@ -91,6 +91,18 @@ def test_persistent_ctas_many_ragged_items(cuda, hq, hkv, causal):
         assert (out[i, :, n:].float() == 0).all()
 
 
+@pytest.mark.parametrize("hq,hkv,L", [(32, 2, 100), (64, 2, 37), (128, 1, 9)])
+def test_large_gqa_groups_few_positions_per_item(cuda, hq, hkv, L):
+    """Groups of 16, 32 and 128 query heads: 8, 4 and 1 positions per 128-row
+    item, chunk lengths that leave the last item partly empty."""
+    starts, totals = [300, 0, 1000], [400, 20, 1009]
+    pt, q, k, v, cos, sin = _case(hq * 3 + L, totals, hq, hkv, L, torch.bfloat16)
+    out = _run(pt, q, k, v, starts, totals, cos, sin, causal=True, kernel="tc")
+    want = ao.prefill_attention(pt, q.float().cpu().numpy(), k.float().cpu().numpy(),
+                                v.float().cpu().numpy(), starts, totals, cos, sin, causal=True)
+    _check(out, want, f"{hq}/{hkv} L={L}")
+
+
 def test_chunked_prefill_reuses_rotated_keys(cuda):
     """One workspace across the chunks of a prefill with krot_valid = tokens
     already rotated. After each chunk the K cache rows of those tokens are
