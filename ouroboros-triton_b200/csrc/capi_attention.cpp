@@ -127,7 +127,7 @@ void plan(ouro::DecodeParams& p, const ouro_decode_args* a, bool* use_tc, size_t
   } else if (a->kernel != 1) {
     fail(OURO_EINVAL, "kernel selector must be 0 (auto), 1 (cuda cores) or 2 (tensor cores)");
   }
-  int split = a->split_blocks > 0 ? a->split_blocks : choose_split(p, tc, 24);
+  int split = a->split_blocks > 0 ? a->split_blocks : choose_split(p, tc, 20);
   split = std::min(split, std::max(p.max_blocks, 1));
   if (tc) split = std::min(split, 512);  // block list lives in shared memory
   p.split_blocks = split;
