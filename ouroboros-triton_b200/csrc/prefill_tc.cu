@@ -39,6 +39,7 @@
 
 #include <algorithm>
 #include <cstring>
+#include <type_traits>
 
 #include "attention.hpp"
 #include "ptx.cuh"
@@ -499,11 +500,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       return max3f(mp[0], mp[1], fmaxf(mp[2], mp[3]));
     };
     // P = exp2(S - base) for 64 keys held in two 32-column blocks, packed to
-    // bf16/fp16 pairs (32 TMEM columns); returns their sum. In tiles without
-    // masked keys kPolyPairs of every 4 pairs use the FMA-pipe polynomial;
-    // otherwise MUFU ex2 throughout, so masked keys (-inf) give exactly 0.
-    auto exp64 = [&](const uint32_t (&a)[32], const uint32_t (&b)[32], float base, bool full,
+    // bf16/fp16 pairs (32 TMEM columns); returns their sum. kPoly (a compile-time
+    // constant, so each tile kind gets its own straight-line code) of every 4
+    // pairs use the FMA-pipe polynomial, the rest MUFU ex2; tiles with masked
+    // keys use MUFU throughout, so masked keys (-inf) give exactly 0.
+    auto exp64 = [&](auto poly, const uint32_t (&a)[32], const uint32_t (&b)[32], float base,
                      uint32_t (&pk)[32]) -> float {
+      constexpr int kPoly = decltype(poly)::value;
       const uint64_t base2 = f2pack(base, base);
       uint64_t lp[4] = {0, 0, 0, 0};
 #pragma unroll
@@ -511,7 +514,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t* v = e2 < 16 ? &a[2 * e2] : &b[2 * e2 - 32];
         const float2 xf =
             f2unpack(f2sub(f2pack(__uint_as_float(v[0]), __uint_as_float(v[1])), base2));
-        const uint64_t pv = (full && (e2 & 3) < kPolyPairs)
+        const uint64_t pv = (e2 & 3) < kPoly
                                 ? exp2_poly2(f2pack(fmaxf(xf.x, -126.f), fmaxf(xf.y, -126.f)))
                                 : f2pack(fast_exp2(xf.x), fast_exp2(xf.y));
         lp[e2 & 3] = f2add(lp[e2 & 3], pv);
@@ -580,18 +583,24 @@ __global__ void __launch_bounds__(kThreads, 1)
         // Pass 2: P for keys 0..63 over S columns 0..31 (their scores are in
         // registers), then keys 64..127 reloaded (columns 64..127, untouched)
         // and stored over columns 32..63.
-        uint32_t pk[32];
-        l += exp64(sa, sb, base, full, pk);
-        tmem_st32(lane_addr + s_col, pk);
-        tmem_ld32(lane_addr + s_col + 64, sa);
-        tmem_ld32(lane_addr + s_col + 96, sb);
-        tmem_wait_ld();
-        if (!full) {
-          mask32(sa, key0 + 64, kmax_row);
-          mask32(sb, key0 + 96, kmax_row);
-        }
-        l += exp64(sa, sb, base, full, pk);
-        tmem_st32(lane_addr + s_col + 32, pk);
+        auto pass2 = [&](auto poly) {  // poly > 0 only in tiles without masked keys
+          uint32_t pk[32];
+          l += exp64(poly, sa, sb, base, pk);
+          tmem_st32(lane_addr + s_col, pk);
+          tmem_ld32(lane_addr + s_col + 64, sa);
+          tmem_ld32(lane_addr + s_col + 96, sb);
+          tmem_wait_ld();
+          if (decltype(poly)::value == 0 && !full) {
+            mask32(sa, key0 + 64, kmax_row);
+            mask32(sb, key0 + 96, kmax_row);
+          }
+          l += exp64(poly, sa, sb, base, pk);
+          tmem_st32(lane_addr + s_col + 32, pk);
+        };
+        if (kPolyPairs > 0 && full)  // warp-uniform
+          pass2(std::integral_constant<int, kPolyPairs>{});
+        else
+          pass2(std::integral_constant<int, 0>{});
         tmem_wait_st();
         tc_fence_before();
         mbar_arrive(&bars->p_ready[par]);
