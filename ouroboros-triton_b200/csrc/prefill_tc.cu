@@ -7,10 +7,11 @@
 // Persistent CTAs (one per SM) walk their items back to back; for each item the
 // CTA walks 128-key tiles (two 64-token blocks resolved through the page table)
 // up to its causal limit. Rings, TMEM buffers and barrier phases run on across
-// item boundaries, and the softmax warps load the next item's query tile while
-// they write the current item's output, so the tensor core starts on the next
-// item without waiting for the epilogue:
-//   warps 8, 10 TMA producers for two separate 2-stage rings (128-byte
+// item boundaries, and the work of an item boundary (merging the softmax
+// halves, writing the output, rotating a query tile) belongs to a warpgroup of
+// its own, so the softmax warps and the tensor core go straight on to the next
+// item. Query tiles are double-buffered: item d uses buffer d % 2.
+//   warps 8, 10 TMA producers for two separate rings, 3 K and 2 V stages (128-byte
 //               swizzle, layout [64-column atom][128 keys][128 B]): K tiles,
 //               already rotated, from the dense scratch written by rope_k.cu
 //               (one box of 128 keys per atom), refilled as soon as S_j is
@@ -18,7 +19,9 @@
 //               block), refilled when PV_j is done
 //   warp 9      TMEM owner and MMA issuer: S_j = Q K_j^T into TMEM buffer
 //               j % 2, then O_{j%2} += P_j V_j with P_j read from TMEM (V as an
-//               MN-major operand), tcgen05.commit to mbarriers
+//               MN-major operand), tcgen05.commit to mbarriers; after an item's
+//               last PV one commit tells the epilogue that O is final
+//   warp 11     idle (completes the third warpgroup)
 //   warps 0-7   softmax. Warp w owns TMEM lanes 32 (w % 4) .. +31 (one query
 //               row per thread) and the tiles of parity w / 4: each parity keeps
 //               its own running max m, row sum l and accumulator O, so the two
@@ -28,11 +31,18 @@
 //               on the shared MUFU. Per tile: max over the 128 scores (two TMEM
 //               passes), lazy rescaling of O (only when m grows by more than
 //               2^8), P = exp2(S - m) as bf16/fp16 pairs stored over the tile's
-//               own S columns. The epilogue merges the parities:
-//               O = (2^(m_0-m) O_0 + 2^(m_1-m) O_1) / (2^(m_0-m) l_0 + 2^(m_1-m) l_1),
-//               m = max(m_0, m_1), each warp writing 64 of the row's 128 output
-//               columns; it also rotates the next item's query tile.
+//               own S columns. After an item's last tile a warp publishes its
+//               (m, l) and starts on the next item.
+//   warps 12-15 epilogue, one TMEM lane quarter each (one row per thread): once
+//               O is final, O = (2^(m_0-m) O_0 + 2^(m_1-m) O_1) /
+//               (2^(m_0-m) l_0 + 2^(m_1-m) l_1), m = max(m_0, m_1), staged in
+//               the item's own (now unused) query buffer and stored coalesced;
+//               then O is released for the next item and the query tile of the
+//               item after next is rotated into the same buffer.
 // TMEM columns: S/P buffers at 0 and 128, O_0 at 256, O_1 at 384 (512 allocated).
+// Registers: the block launches with 128 per thread (512 threads); the softmax
+// warpgroups raise theirs to 168, the producer/MMA warpgroup lowers to 56 and
+// the epilogue to 120.
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -58,10 +68,20 @@ constexpr int kTile = 2 * kAtom;  // 128 rows x 128 columns x 2 bytes
 constexpr int kSoftmaxWarps = 8;                   // 4 lane quarters x 2 key halves
 constexpr int kSoftmaxThreads = kSoftmaxWarps * 32;
 constexpr int kWarpK = 8, kWarpMma = 9, kWarpV = 10;  // K loads, MMA / TMEM, V loads
-constexpr int kThreads = 11 * 32;
+constexpr int kWarpEpi = 12;                          // first epilogue warp
+constexpr int kEpiThreads = 128;
+constexpr int kThreads = 16 * 32;
+// Per-thread register budgets after the split (launch: 65536 / kThreads = 128).
+constexpr int kRegsSoftmax = 168, kRegsIssue = 56, kRegsEpi = 120;
+static_assert(2 * 128 * kRegsSoftmax + 128 * kRegsIssue + 128 * kRegsEpi <= 65536,
+              "register split exceeds the launch allocation");
+static_assert(kThreads * 128 == 65536, "launch allocation of 128 registers per thread");
+// Named barriers (id 0 is __syncthreads).
+constexpr uint32_t kBarSoftmax = 1, kBarEpi = 2;
 constexpr float kRescaleLog2 = 8.0f;
 // Pairs of every 4 key pairs whose exponential goes through exp2_poly2 instead
-// of MUFU ex2 (0..4).
+// of MUFU ex2 (0..4). Measured: every share above 0 is slower (the softmax is
+// bound by its instruction chain, not by the MUFU pipe).
 constexpr int kPolyPairs = 0;
 
 // Ring depths. K tile j + 3 may load once S_j is done (k_empty); three K slots
@@ -75,12 +95,14 @@ static_assert(kStagesV == 2, "V slots are tied to the S/P buffer parity");
 
 // Shared-memory map (offsets from a 1024-byte aligned base). P never touches
 // shared memory: it is written over its own S columns in TMEM and read from
-// there by the PV MMA.
-constexpr int kOffQ = 0;
-constexpr int kOffK = kOffQ + kTile;             // kStagesK K tiles
+// there by the PV MMA. Item d's query tile sits in buffer d % 2; once O is
+// final the same buffer stages its output: epilogue warp q stages rows
+// 32 q .. 32 q + 31, the rows whose query units it also writes.
+constexpr int kOffQ0 = 0;
+constexpr int kOffK = kOffQ0 + kTile;            // kStagesK K tiles
 constexpr int kOffV = kOffK + kStagesK * kTile;  // kStagesV V tiles
-constexpr int kOffStage = kOffV + kStagesV * kTile;  // output staging, 4 KB per softmax warp
-constexpr int kOffMl = kOffStage + kSoftmaxWarps * 32 * 128;  // (m, l) per half and row
+constexpr int kOffQ1 = kOffV + kStagesV * kTile;
+constexpr int kOffMl = kOffQ1 + kTile;           // (m, l) per parity and row
 constexpr int kOffBar = kOffMl + 2 * kBM * 8;
 // The dynamic shared window starts 1024-byte aligned (after the 1 KB the
 // system reserves); the kernel checks this instead of padding for it.
@@ -89,12 +111,22 @@ static_assert(kSmemBytes <= 232448, "shared memory");
 
 // Every ring barrier is per buffer: a parity wait is only valid while the
 // barrier is at most one phase past the awaited one, and per-buffer barriers
-// keep each waiter within that window.
+// keep each waiter within that window. The once-per-item barriers stay within
+// it because each one's next phase needs a step of its waiter first:
+//   ml_ready (softmax -> epilogue, item d's (m, l) written): the softmax writes
+//            item d + 1's only after ml_free(d);
+//   ml_free  (epilogue -> softmax, (m, l) read);
+//   o_full   (MMA commit after item d's last PV): item d + 1's needs its first
+//            PV, which waits for o_free(d);
+//   o_free   (epilogue -> MMA, O read out);
+//   q_ready[b] (query tile of item d in buffer b = d % 2): the epilogue writes
+//            item d + 2's only after o_full(d), i.e. after the MMA took item d.
 struct Bars {
   uint64_t k_full[kStagesK], k_empty[kStagesK], v_full[kStagesV];
   uint64_t s_full[2];
   uint64_t p_ready[2], pv_done[2];       // per S/P buffer = tile parity
-  uint64_t q_ready, merge, o_free;        // once per item
+  uint64_t q_ready[2];                   // per query buffer
+  uint64_t ml_ready, ml_free, o_full, o_free;  // once per item
   uint32_t tmem_base;
   int32_t abort;
 };
@@ -149,8 +181,7 @@ __device__ __forceinline__ float fast_exp2(float x) {
 }
 
 // 2^x for a pair of x in [-126, 2^20] on the FMA pipes, so that part of the
-// softmax exponentials bypass the MUFU unit (which otherwise needs as many
-// cycles per tile as the tensor core). Cody-Waite split x = n + f with
+// softmax exponentials bypass the MUFU unit. Cody-Waite split x = n + f with
 // n = round(x) (the 1.5 * 2^23 shift trick leaves n in the low mantissa bits
 // of t) and f in [-0.5, 0.5]; 2^f from a degree-3 polynomial fitted for
 // minimal maximum relative error on [-0.5, 0.5] (Remez exchange, 7.5e-5 in
@@ -183,14 +214,16 @@ struct Item {
   bool bad;  // negative query position
 };
 
-__device__ __forceinline__ Item item_at(const RowsParams& p, int L, int n_qt, int ppt) {
+// Item L from its sequence's length and query start (no memory access).
+__device__ __forceinline__ Item item_from(const RowsParams& p, int L, int n_qt, int ppt,
+                                          int seq_len, int q_start) {
   Item it;
   const int group = L / n_qt;
   it.qt = n_qt - 1 - (L - group * n_qt);
   it.s = group / p.Hkv;
   it.kvh = group - it.s * p.Hkv;
-  it.seq_len = p.seq_lens[it.s];
-  it.q0 = (p.q_start ? p.q_start[it.s] : 0) + it.qt * ppt;
+  it.seq_len = seq_len;
+  it.q0 = q_start + it.qt * ppt;
   it.bad = it.q0 < 0;
   // rows whose position lies in the chunk and the sequence
   it.rows_valid = max(0, min(min(ppt, p.Lq - it.qt * ppt), it.seq_len - it.q0));
@@ -200,34 +233,69 @@ __device__ __forceinline__ Item item_at(const RowsParams& p, int L, int n_qt, in
   return it;
 }
 
+__device__ __forceinline__ Item item_at(const RowsParams& p, int L, int n_qt, int ppt) {
+  const int s = (L / n_qt) / p.Hkv;
+  return item_from(p, L, n_qt, ppt, p.seq_lens[s], p.q_start ? p.q_start[s] : 0);
+}
+
 // Next item of this CTA at or after L that has work (L >= n_items: none).
+// Only the softmax walk reports negative query positions.
 __device__ __forceinline__ int next_item(const RowsParams& p, int L, int n_items, int n_qt, int ppt,
-                                         Item& it) {
+                                         Item& it, bool report = false) {
   for (; L < n_items; L += gridDim.x) {
     it = item_at(p, L, n_qt, ppt);
     if (it.n_tiles > 0) return L;
-    if (it.bad && p.status) atomicOr(p.status, kStatusBadPosition);
+    if (report && it.bad && p.status) atomicOr(p.status, kStatusBadPosition);
   }
   return n_items;
 }
 
-// The query tile of one item, loaded into registers (16-byte vectors, all
+// The two loads an item needs (its sequence's length and query start), issued
+// one item ahead so that their latency overlaps the current item's tiles;
+// item_resolve builds the item from them, or walks on past items without
+// work (loading as next_item does).
+struct ItemLoads {
+  int L, seq_len, q_start;
+};
+
+__device__ __forceinline__ ItemLoads item_loads(const RowsParams& p, int L, int n_items, int n_qt) {
+  ItemLoads a{L, 0, 0};
+  if (L < n_items) {
+    const int s = (L / n_qt) / p.Hkv;
+    a.seq_len = p.seq_lens[s];
+    a.q_start = p.q_start ? p.q_start[s] : 0;
+  }
+  return a;
+}
+
+__device__ __forceinline__ int item_resolve(const RowsParams& p, const ItemLoads& a, int n_items,
+                                            int n_qt, int ppt, Item& it, bool report = false) {
+  if (a.L >= n_items) return n_items;
+  it = item_from(p, a.L, n_qt, ppt, a.seq_len, a.q_start);
+  if (it.n_tiles > 0) return a.L;
+  if (report && it.bad && p.status) atomicOr(p.status, kStatusBadPosition);
+  return next_item(p, a.L + gridDim.x, n_items, n_qt, ppt, it, report);
+}
+
+// Four query units of an item, loaded into registers (16-byte vectors, all
 // loads issued together) and then rotated and scaled by softmax_scale * log2 e
 // into the swizzled Q buffer. Row R is head kvh*G + R / ppt at position
-// q0 + R % ppt; unit u = (R, c) covers the pairs (d, d + 64), d in [8c, 8c+8).
-// Eight consecutive threads take the 8 units of one row, so a warp-wide load
-// reads 4 contiguous row segments.
+// q0 + R % ppt; unit (R, c) covers the pairs (d, d + 64), d in [8c, 8c+8).
+// The caller passes rows R0, R0 + dR, R0 + 2 dR, R0 + 3 dR and one c; eight
+// consecutive threads take the 8 units of one row, so a warp-wide load reads 4
+// contiguous row segments.
 template <typename T>
 struct QTile {
   uint4 lo[4], hi[4];
   float4 cs[8], sn[8];
 
-  __device__ __forceinline__ void load(const RowsParams& p, const Item& it, int ppt, int tid) {
+  __device__ __forceinline__ void load(const RowsParams& p, const Item& it, int ppt, int R0,
+                                       int dR, int c) {
     const int half = kHD / 2;
     const int lppt = 31 - __clz(ppt);
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
-      const int u = tid + kSoftmaxThreads * k, R = u >> 3, c = u & 7;
+      const int R = R0 + dR * k;
       const int iR = R & (ppt - 1), posR = it.q0 + iR;  // ppt = 128 / G is a power of 2
       lo[k] = hi[k] = make_uint4(0, 0, 0, 0);
       cs[2 * k] = cs[2 * k + 1] = make_float4(1.f, 1.f, 1.f, 1.f);
@@ -249,10 +317,10 @@ struct QTile {
       }
     }
   }
-  __device__ __forceinline__ void store(uint8_t* qs, float scale, int tid) {
+  __device__ __forceinline__ void store(uint8_t* qs, float scale, int R0, int dR, int c) {
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
-      const int u = tid + kSoftmaxThreads * k, R = u >> 3, c = u & 7;
+      const int R = R0 + dR * k;
       rope8<T>(lo[k], hi[k], reinterpret_cast<const float*>(&cs[2 * k]),
                reinterpret_cast<const float*>(&sn[2 * k]), scale);
       *reinterpret_cast<uint4*>(qs + sw_off(R, c)) = lo[k];
@@ -293,10 +361,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&bars->s_full[i], 1);
       mbar_init(&bars->p_ready[i], 128);
       mbar_init(&bars->pv_done[i], 1);
+      mbar_init(&bars->q_ready[i], 1);
     }
-    mbar_init(&bars->q_ready, kSoftmaxThreads);
-    mbar_init(&bars->merge, kSoftmaxThreads);
-    mbar_init(&bars->o_free, kSoftmaxThreads);
+    mbar_init(&bars->ml_ready, kSoftmaxThreads);
+    mbar_init(&bars->ml_free, kEpiThreads);
+    mbar_init(&bars->o_full, 1);
+    mbar_init(&bars->o_free, kEpiThreads);
     fence_barrier_init();
   }
   if (warp == kWarpMma) {
@@ -316,124 +386,248 @@ __global__ void __launch_bounds__(kThreads, 1)
   // Every role walks the same item sequence and counts tiles globally: ring
   // slots and TMEM buffers rotate across item boundaries, and every barrier
   // phase follows from the global tile index g (or the item count done).
-  if (warp == kWarpK || warp == kWarpV) {
-    // ------------------------------- TMA producers -------------------------------
-    if (lane == 0) {
-      const bool is_k = warp == kWarpK;
-      tma_prefetch_desc(is_k ? &tm_k : &tm_v);
-      const uint64_t pol = policy_evict_last();  // tiles are re-read by other CTAs
-      uint64_t* full = is_k ? bars->k_full : bars->v_full;
-      uint64_t* empty = is_k ? bars->k_empty : bars->pv_done;  // V slot g % 2 frees with PV_g
-      uint8_t* ring = smem + (is_k ? kOffK : kOffV);
-      const uint32_t stages = is_k ? kStagesK : kStagesV;
-      uint32_t g = 0;
-      Item it;
-      for (int L = next_item(p, blockIdx.x, n_items, n_qt, ppt, it); L < n_items && !*s_abort;
-           L = next_item(p, L + gridDim.x, n_items, n_qt, ppt, it)) {
-        const int32_t* row = p.page_table + static_cast<int64_t>(it.s) * p.max_blocks;
-        for (int j = 0; j < it.n_tiles; ++j, ++g) {
-          const uint32_t st = g % stages;
-          if (g >= stages && !mbar_wait(&empty[st], ((g / stages) - 1) & 1)) {
-            fail(kStatusWaitTimeout);
-            break;
-          }
-          mbar_arrive_expect_tx(&full[st], kTile);
-          uint8_t* dst = ring + st * kTile;
-          if (is_k) {
-            // rotated keys: rows (s, kvh, 128 j .. 128 j + 127) of the scratch
-            const int ky = (it.s * p.Hkv + it.kvh) * krot_rows_per_head + j * kBN;
-            for (int a = 0; a < 2; ++a) tma_load_2d(dst + a * kAtom, &tm_k, a * 64, ky, &full[st], pol);
-          } else {
-            for (int blk = 0; blk < 2; ++blk) {
-              const int b = 2 * j + blk;
-              const int lb = b < it.nb ? b : 2 * j;  // a block past the keys repeats a valid one
-              int phys = lb < p.max_blocks ? row[lb] : -1;
-              if (phys < 0 || phys >= p.n_phys) {
-                if (p.status) atomicOr(p.status, kStatusBadPageEntry);
-                phys = 0;
+  if (warp >= kWarpK && warp < kWarpEpi) {
+    regs_decrease<kRegsIssue>();
+    if (warp == kWarpK || warp == kWarpV) {
+      // ------------------------------- TMA producers -------------------------------
+      if (lane == 0) {
+        const bool is_k = warp == kWarpK;
+        tma_prefetch_desc(is_k ? &tm_k : &tm_v);
+        const uint64_t pol = policy_evict_last();  // tiles are re-read by other CTAs
+        uint64_t* full = is_k ? bars->k_full : bars->v_full;
+        uint64_t* empty = is_k ? bars->k_empty : bars->pv_done;  // V slot g % 2 frees with PV_g
+        uint8_t* ring = smem + (is_k ? kOffK : kOffV);
+        const uint32_t stages = is_k ? kStagesK : kStagesV;
+        uint32_t g = 0;
+        Item it;
+        for (int L = next_item(p, blockIdx.x, n_items, n_qt, ppt, it); L < n_items && !*s_abort;
+             L = next_item(p, L + gridDim.x, n_items, n_qt, ppt, it)) {
+          const int32_t* row = p.page_table + static_cast<int64_t>(it.s) * p.max_blocks;
+          for (int j = 0; j < it.n_tiles; ++j, ++g) {
+            const uint32_t st = g % stages;
+            if (g >= stages && !mbar_wait(&empty[st], ((g / stages) - 1) & 1)) {
+              fail(kStatusWaitTimeout);
+              break;
+            }
+            mbar_arrive_expect_tx(&full[st], kTile);
+            uint8_t* dst = ring + st * kTile;
+            if (is_k) {
+              // rotated keys: rows (s, kvh, 128 j .. 128 j + 127) of the scratch
+              const int ky = (it.s * p.Hkv + it.kvh) * krot_rows_per_head + j * kBN;
+              for (int a = 0; a < 2; ++a) tma_load_2d(dst + a * kAtom, &tm_k, a * 64, ky, &full[st], pol);
+            } else {
+              for (int blk = 0; blk < 2; ++blk) {
+                const int b = 2 * j + blk;
+                const int lb = b < it.nb ? b : 2 * j;  // a block past the keys repeats a valid one
+                int phys = lb < p.max_blocks ? row[lb] : -1;
+                if (phys < 0 || phys >= p.n_phys) {
+                  if (p.status) atomicOr(p.status, kStatusBadPageEntry);
+                  phys = 0;
+                }
+                const int y = (phys * p.Hkv + it.kvh) * kBlock;
+                for (int a = 0; a < 2; ++a)
+                  tma_load_2d(dst + a * kAtom + blk * (kAtom / 2), &tm_v, a * 64, y, &full[st], pol);
               }
-              const int y = (phys * p.Hkv + it.kvh) * kBlock;
-              for (int a = 0; a < 2; ++a)
-                tma_load_2d(dst + a * kAtom + blk * (kAtom / 2), &tm_v, a * 64, y, &full[st], pol);
             }
           }
         }
       }
-    }
-  } else if (warp == kWarpMma) {
-    // ------------------------------ MMA issuer ------------------------------
-    if (lane == 0) {
-      const uint32_t idesc_s = umma_idesc_f16(Elem<T>::kBf16, kBM, kBN, false, false);
-      const uint32_t idesc_pv = umma_idesc_f16(Elem<T>::kBf16, kBM, kHD, false, true);
-      // Shared-memory descriptors are computed once: a K step adds 32 B (K-major)
-      // or 2048 B (V, MN-major) to the 14-bit start-address field (units of 16 B),
-      // a ring slot adds kTile, an atom kAtom. Every tcgen05 instruction costs the
-      // issuing thread ~70 cycles, so nothing else sits between them.
-      const uint64_t q_desc = umma_desc_sw128(smem_u32(smem + kOffQ), 16, 1024);
-      const uint64_t k_desc = umma_desc_sw128(smem_u32(smem + kOffK), 16, 1024);
-      const uint64_t v_desc = umma_desc_sw128(smem_u32(smem + kOffV), kAtom, 1024);
-      constexpr uint64_t kSlot = kTile >> 4;
-      uint32_t g = 0, done = 0;
-      // O_b += P V for global tile gg, b = gg % 2: the accumulator of the tile
-      // parity. P is the A operand in TMEM: 64 columns of packed pairs over the
-      // first half of the tile's S buffer. The first tile of each parity in an
-      // item overwrites its accumulator; the item's first PV waits until the
-      // previous item's epilogue has read O (o_free). The commit to pv_done also
-      // frees V slot b.
-      auto issue_pv = [&](uint32_t gg, uint32_t j) -> bool {
-        const uint32_t b = gg & 1;
-        if (!mbar_wait(&bars->v_full[b], (gg >> 1) & 1)) return false;
-        if (j == 0 && done > 0 && !mbar_wait(&bars->o_free, (done - 1) & 1)) return false;
-        if (!mbar_wait(&bars->p_ready[b], (gg >> 1) & 1)) return false;
-        tc_fence_after();  // P was stored to TMEM by the softmax threads
-        const uint64_t vd = v_desc + b * kSlot;
-        const uint32_t a_tmem = tmem + b * 128, d_tmem = tmem + 256 + 128 * b;
+    } else if (warp == kWarpMma) {
+      // ------------------------------ MMA issuer ------------------------------
+      if (lane == 0) {
+        const uint32_t idesc_s = umma_idesc_f16(Elem<T>::kBf16, kBM, kBN, false, false);
+        const uint32_t idesc_pv = umma_idesc_f16(Elem<T>::kBf16, kBM, kHD, false, true);
+        // Shared-memory descriptors are computed once: a K step adds 32 B (K-major)
+        // or 2048 B (V, MN-major) to the 14-bit start-address field (units of 16 B),
+        // a ring slot adds kTile, an atom kAtom. Every tcgen05 instruction costs the
+        // issuing thread ~70 cycles, so nothing else sits between them.
+        const uint64_t q_desc0 = umma_desc_sw128(smem_u32(smem + kOffQ0), 16, 1024);
+        const uint64_t q_desc1 = umma_desc_sw128(smem_u32(smem + kOffQ1), 16, 1024);
+        const uint64_t k_desc = umma_desc_sw128(smem_u32(smem + kOffK), 16, 1024);
+        const uint64_t v_desc = umma_desc_sw128(smem_u32(smem + kOffV), kAtom, 1024);
+        constexpr uint64_t kSlot = kTile >> 4;
+        uint32_t g = 0, done = 0;
+        // O_b += P V for global tile gg (tile j of item dd), b = gg % 2: the
+        // accumulator of the tile parity. P is the A operand in TMEM: 64 columns
+        // of packed pairs over the first half of the tile's S buffer. The first
+        // tile of each parity in an item overwrites its accumulator; the item's
+        // first PV waits until the epilogue has read the previous item's O
+        // (o_free). The commit to pv_done also frees V slot b.
+        auto issue_pv = [&](uint32_t gg, uint32_t j, uint32_t dd) -> bool {
+          const uint32_t b = gg & 1;
+          if (!mbar_wait(&bars->v_full[b], (gg >> 1) & 1)) return false;
+          if (j == 0 && dd > 0 && !mbar_wait(&bars->o_free, (dd - 1) & 1)) return false;
+          if (!mbar_wait(&bars->p_ready[b], (gg >> 1) & 1)) return false;
+          tc_fence_after();  // P was stored to TMEM by the softmax threads
+          const uint64_t vd = v_desc + b * kSlot;
+          const uint32_t a_tmem = tmem + b * 128, d_tmem = tmem + 256 + 128 * b;
 #pragma unroll
-        for (int kk = 0; kk < kBN / 16; ++kk)
-          // A = P [128 rows x 16 keys] (8 TMEM columns); B = V [16 keys x 128 d] MN-major
-          umma_f16_ts(d_tmem, a_tmem + 8 * kk, vd + kk * (2048 >> 4), idesc_pv,
-                      (j < 2 && kk == 0) ? 0u : 1u);
-        umma_commit(&bars->pv_done[b]);
-        return true;
-      };
-      // Issue order S_0, S_1, PV_0, S_2, PV_1, ... across items: S_{g+2}
-      // overwrites the TMEM buffer of S_g / P_g only after PV_g was issued
-      // (which waited for P_g, hence for the loads of S_g), and tcgen05.mma
-      // operations of one thread execute in issue order. Q and K reach the MMA
-      // through shared memory only (TMA, or stores fenced to the async proxy
-      // before q_ready), so their barrier waits need no tcgen05 fence.
-      bool ok = true;
-      Item it;
-      for (int L = next_item(p, blockIdx.x, n_items, n_qt, ppt, it); L < n_items && ok && !*s_abort;
-           L = next_item(p, L + gridDim.x, n_items, n_qt, ppt, it)) {
-        if (!mbar_wait(&bars->q_ready, done & 1)) {  // this item's Q tile is in shared memory
-          ok = false;
-          break;
-        }
-        for (int j = 0; j < it.n_tiles && ok; ++j) {
-          const uint32_t gg = g + j, b = gg & 1, st = gg % kStagesK;
-          if (!mbar_wait(&bars->k_full[st], (gg / kStagesK) & 1)) {
+          for (int kk = 0; kk < kBN / 16; ++kk)
+            // A = P [128 rows x 16 keys] (8 TMEM columns); B = V [16 keys x 128 d] MN-major
+            umma_f16_ts(d_tmem, a_tmem + 8 * kk, vd + kk * (2048 >> 4), idesc_pv,
+                        (j < 2 && kk == 0) ? 0u : 1u);
+          umma_commit(&bars->pv_done[b]);
+          return true;
+        };
+        // One issue order over the global tiles of all items: S_g, then PV_{g-1}
+        // (whichever items they belong to), so the next item's first score
+        // tiles run while this item's last softmax does. S_{g+2} overwrites the
+        // TMEM buffer of S_g / P_g only after PV_g was issued (which waited for
+        // P_g, hence for the loads of S_g), and tcgen05.mma operations of one
+        // thread execute in issue order. After an item's last PV one commit to
+        // o_full tells the epilogue that its O_0, O_1 (and every S MMA reading
+        // its query buffer) are done. Q and K reach the MMA through shared
+        // memory only (TMA, or stores fenced to the async proxy before
+        // q_ready), so their barrier waits need no tcgen05 fence.
+        bool ok = true;
+        bool pend = false;  // a tile whose PV is still to issue
+        uint32_t pend_j = 0, pend_d = 0;
+        bool pend_last = false;
+        Item it;
+        int L = next_item(p, blockIdx.x, n_items, n_qt, ppt, it);
+        while (L < n_items && ok && !*s_abort) {
+          const ItemLoads nx = item_loads(p, L + gridDim.x, n_items, n_qt);
+          // this item's Q tile is in shared memory
+          if (!mbar_wait(&bars->q_ready[done & 1], (done >> 1) & 1)) {
             ok = false;
             break;
           }
-          const uint64_t kd = k_desc + st * kSlot;
+          const uint64_t q_desc = (done & 1) ? q_desc1 : q_desc0;
+          for (int j = 0; j < it.n_tiles && ok; ++j) {
+            const uint32_t gg = g + j, b = gg & 1, st = gg % kStagesK;
+            if (!mbar_wait(&bars->k_full[st], (gg / kStagesK) & 1)) {
+              ok = false;
+              break;
+            }
+            const uint64_t kd = k_desc + st * kSlot;
 #pragma unroll
-          for (int kk = 0; kk < kHD / 16; ++kk) {
-            const uint64_t step = (kk >> 2) * (kAtom >> 4) + (kk & 3) * (32 >> 4);
-            umma_f16_ss(tmem + b * 128, q_desc + step, kd + step, idesc_s, kk > 0 ? 1u : 0u);
+            for (int kk = 0; kk < kHD / 16; ++kk) {
+              const uint64_t step = (kk >> 2) * (kAtom >> 4) + (kk & 3) * (32 >> 4);
+              umma_f16_ss(tmem + b * 128, q_desc + step, kd + step, idesc_s, kk > 0 ? 1u : 0u);
+            }
+            umma_commit(&bars->s_full[b]);
+            umma_commit(&bars->k_empty[st]);
+            if (pend) {
+              ok = issue_pv(gg - 1, pend_j, pend_d);
+              if (ok && pend_last) umma_commit(&bars->o_full);
+            }
+            pend = true;
+            pend_j = j;
+            pend_d = done;
+            pend_last = j == it.n_tiles - 1;
           }
-          umma_commit(&bars->s_full[b]);
-          umma_commit(&bars->k_empty[st]);
-          if (j >= 1 && !issue_pv(gg - 1, j - 1)) ok = false;
+          g += it.n_tiles;
+          ++done;
+          L = item_resolve(p, nx, n_items, n_qt, ppt, it);
         }
-        if (ok) ok = issue_pv(g + it.n_tiles - 1, it.n_tiles - 1);
-        g += it.n_tiles;
-        ++done;
+        if (ok && pend && !*s_abort) {
+          ok = issue_pv(g - 1, pend_j, pend_d);
+          if (ok) umma_commit(&bars->o_full);
+        }
+        if (!ok) fail(kStatusWaitTimeout);
       }
-      if (!ok) fail(kStatusWaitTimeout);
     }
+  } else if (warp >= kWarpEpi) {
+    // ------------------------------ epilogue warps 12-15 ------------------------------
+    regs_decrease<kRegsEpi>();
+    const int quarter = warp & 3;
+    const int r = quarter * 32 + lane;  // TMEM lane == query row == staged output row
+    const uint32_t lane_addr = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
+    const float2* ml = reinterpret_cast<const float2*>(smem + kOffMl);
+    uint32_t done = 0;
+    bool ok = true;
+    Item it, iq;
+    int L = next_item(p, blockIdx.x, n_items, n_qt, ppt, it);
+    // Query tiles of items 0 and 1 are written by the softmax warps; this walk
+    // points at item done + 2.
+    int Lq = L < n_items ? next_item(p, L + gridDim.x, n_items, n_qt, ppt, iq) : n_items;
+    if (Lq < n_items) Lq = next_item(p, Lq + gridDim.x, n_items, n_qt, ppt, iq);
+    while (L < n_items) {
+      // Sleeping waits: these warps share schedulers with the softmax warps.
+      if (!__all_sync(0xffffffffu, mbar_wait_sleep(&bars->ml_ready, done & 1, 128)) ||
+          !__all_sync(0xffffffffu, mbar_wait_sleep(&bars->o_full, done & 1, 128))) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const float2 a0 = ml[r], a1 = ml[kBM + r];
+      mbar_arrive(&bars->ml_free);
+      const float m = fmaxf(a0.x, a1.x);
+      // A parity without tiles in this item (one-tile items) keeps m = -inf and
+      // l = 0; its accumulator holds an older item's values and is not read.
+      const bool has0 = a0.x != -INFINITY, has1 = a1.x != -INFINITY;
+      const float w0 = has0 ? fast_exp2(a0.x - m) : 0.f;
+      const float w1 = has1 ? fast_exp2(a1.x - m) : 0.f;
+      const float den = w0 * a0.y + w1 * a1.y;
+      const float inv = den > 0.f ? 1.f / den : 0.f;
+      const float s0 = w0 * inv, s1 = w1 * inv;
+      // Output row r (128 columns, 256 B) staged over query row r of this item's
+      // buffer: columns 0..63 in atom 0, 64..127 in atom 1, 16-byte chunks XOR
+      // swizzled by the row.
+      uint8_t* qbuf = smem + ((done & 1) ? kOffQ1 : kOffQ0);
+#pragma unroll
+      for (int c2 = 0; c2 < 4; ++c2) {
+        uint32_t o0[32], o1[32];
+        tmem_ld32(lane_addr + 256 + 32 * c2, o0);
+        tmem_ld32(lane_addr + 384 + 32 * c2, o1);
+        tmem_wait_ld();
+#pragma unroll
+        for (int e8 = 0; e8 < 4; ++e8) {
+          float o[8];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            const float v0 = has0 ? __uint_as_float(o0[e8 * 8 + e]) * s0 : 0.f;
+            const float v1 = has1 ? __uint_as_float(o1[e8 * 8 + e]) * s1 : 0.f;
+            o[e] = v0 + v1;
+          }
+          uint4 w;
+          w.x = Elem<T>::from2(o[0], o[1]);
+          w.y = Elem<T>::from2(o[2], o[3]);
+          w.z = Elem<T>::from2(o[4], o[5]);
+          w.w = Elem<T>::from2(o[6], o[7]);
+          const int ch = c2 * 4 + e8;  // 16-byte chunk of the row, 0..15
+          *reinterpret_cast<uint4*>(qbuf + (ch >> 3) * kAtom + sw_off(r, ch & 7)) = w;
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&bars->o_free);  // O may take the next item's first PV
+      __syncwarp();
+      // Two rows per warp-wide store (16 lanes x 16 B each).
+#pragma unroll 4
+      for (int itr = 0; itr < 16; ++itr) {
+        const int R = quarter * 32 + 2 * itr + (lane >> 4), ch = lane & 15;
+        const int iR = R & (ppt - 1);
+        if (iR < it.rows_valid) {
+          T* orow = static_cast<T*>(p.out) +
+                    ((static_cast<int64_t>(it.s) * p.Hq + it.kvh * G + (R >> lppt)) * p.Lq +
+                     it.qt * ppt + iR) * kHD;
+          *reinterpret_cast<uint4*>(orow + ch * 8) =
+              *reinterpret_cast<const uint4*>(qbuf + (ch >> 3) * kAtom + sw_off(R, ch & 7));
+        }
+      }
+      __syncwarp();
+      // Item done + 2's query tile into the same buffer: this warp writes rows
+      // 32 quarter .. +31 (the rows it staged), in two rounds of 16 rows.
+      if (Lq < n_items) {
+        QTile<T> qn;
+#pragma unroll 1
+        for (int rnd = 0; rnd < 2; ++rnd) {
+          const int R0 = quarter * 32 + 16 * rnd + (lane >> 3);
+          qn.load(p, iq, ppt, R0, 4, lane & 7);
+          qn.store(qbuf, p.scale_log2, R0, 4, lane & 7);
+        }
+        fence_proxy_async_smem();
+        named_barrier(kBarEpi, kEpiThreads);
+        if (threadIdx.x == kWarpEpi * 32) mbar_arrive(&bars->q_ready[done & 1]);
+        Lq = next_item(p, Lq + gridDim.x, n_items, n_qt, ppt, iq);
+      }
+      ++done;
+      L = next_item(p, L + gridDim.x, n_items, n_qt, ppt, it);
+    }
+    if (!ok) fail(kStatusWaitTimeout);
   } else {
     // ------------------------------ softmax warps 0-7 ------------------------------
+    regs_increase<kRegsSoftmax>();
     const int quarter = warp & 3, par = warp >> 2;  // TMEM lane quarter, tile parity
     const int r = quarter * 32 + lane;              // TMEM lane == query row
     const int tid = threadIdx.x;                    // 0 .. 255
@@ -441,17 +635,26 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t s_col = 128 * par;               // this parity's S / P buffer
     const uint32_t o_col = 256 + 128 * par;         // this parity's accumulator
     float2* ml = reinterpret_cast<float2*>(smem + kOffMl);  // [parity][row]: (m, l)
-    uint8_t* stage = smem + kOffStage + warp * (32 * 128);
     uint32_t g = 0, done = 0;
     bool ok = true;
-    Item it, nx;
-    int L = next_item(p, blockIdx.x, n_items, n_qt, ppt, it);
-    QTile<T> qn;
-    if (L < n_items) {
-      qn.load(p, it, ppt, tid);
-      qn.store(smem + kOffQ, p.scale_log2, tid);
-      fence_proxy_async_smem();
-      mbar_arrive(&bars->q_ready);
+    Item it;
+    int L = next_item(p, blockIdx.x, n_items, n_qt, ppt, it, true);
+    // Query tiles of the first two items (buffers 0 and 1); later ones come
+    // from the epilogue warps.
+    {
+      Item iq = it;
+      int Lq = L;
+#pragma unroll 1
+      for (int b = 0; b < 2 && Lq < n_items; ++b) {
+        QTile<T> qn;
+        const int R0 = tid >> 3;
+        qn.load(p, iq, ppt, R0, 32, tid & 7);
+        qn.store(smem + (b ? kOffQ1 : kOffQ0), p.scale_log2, R0, 32, tid & 7);
+        fence_proxy_async_smem();
+        named_barrier(kBarSoftmax, kSoftmaxThreads);
+        if (tid == 0) mbar_arrive(&bars->q_ready[b]);
+        Lq = next_item(p, Lq + gridDim.x, n_items, n_qt, ppt, iq);
+      }
     }
     // Token scope (optional): the row at position i keeps key j when tags[j] or
     // lo[i] <= j < hi[i]; sc_lo / sc_hi are set per item below.
@@ -525,6 +728,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       return t.x + t.y;
     };
     while (L < n_items) {
+      const ItemLoads nx = item_loads(p, L + gridDim.x, n_items, n_qt);
       const int i = r & (ppt - 1);
       const bool live = i < it.rows_valid;
       const int pos = it.q0 + i;
@@ -606,91 +810,18 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_arrive(&bars->p_ready[par]);
       }
       if (!ok) break;
-      // Next item's query tile: issue its loads now, so they land while this
-      // item's epilogue runs. Without a next item nothing is loaded, and the
-      // store below only fills the free Q buffer with zeros (no MMA reads it).
-      const int Ln = next_item(p, L + gridDim.x, n_items, n_qt, ppt, nx);
-      if (Ln >= n_items) nx.rows_valid = 0;
-      qn.load(p, nx, ppt, tid);
-
-      // ---- epilogue: this parity's accumulator is final once the PV of its
-      // last tile in the item is done (if it had one).
-      const int jl = ((n - 1 - j0) & 1) ? n - 2 : n - 1;  // last tile of this parity
-      if (jl >= 0) {
-        const uint32_t gg = g + jl;
-        if (!__all_sync(0xffffffffu, mbar_wait(&bars->pv_done[par], (gg >> 1) & 1))) ok = false;
-      }
-      // Merge the parities: every softmax thread arrives exactly once per item,
-      // also after a failed wait, so the other warps' bounded waits end.
-      ml[par * kBM + r] = make_float2(m_ref, l);
-      tc_fence_before();
-      mbar_arrive(&bars->merge);
-      if (!ok || !__all_sync(0xffffffffu, mbar_wait(&bars->merge, done & 1))) {
+      // Publish this parity's (m, l) for the epilogue once it has read the
+      // previous item's; the accumulator itself is read after the MMA's o_full
+      // commit. Every softmax thread arrives exactly once per item.
+      if (done > 0 && !__all_sync(0xffffffffu, mbar_wait(&bars->ml_free, (done - 1) & 1))) {
         ok = false;
         break;
       }
-      tc_fence_after();
-      const float2 a0 = ml[r], a1 = ml[kBM + r];
-      const float m = fmaxf(a0.x, a1.x);
-      // A parity without tiles in this item (one-tile items) keeps m = -inf and
-      // l = 0; its accumulator holds an older item's values and is not read.
-      const bool has0 = a0.x != -INFINITY, has1 = a1.x != -INFINITY;
-      const float w0 = has0 ? fast_exp2(a0.x - m) : 0.f;
-      const float w1 = has1 ? fast_exp2(a1.x - m) : 0.f;
-      const float den = w0 * a0.y + w1 * a1.y;
-      const float inv = den > 0.f ? 1.f / den : 0.f;
-      const float s0 = w0 * inv, s1 = w1 * inv;
-      // Output columns [64 par, 64 par + 64) of this warp's 32 rows, staged as
-      // [32 rows][8 x 16 B chunks] with an XOR swizzle, then stored 4 rows per
-      // warp-wide instruction.
-#pragma unroll
-      for (int c4 = 0; c4 < 4; ++c4) {
-        uint32_t o0[16], o1[16];
-        tmem_ld16(lane_addr + 256 + 64 * par + c4 * 16, o0);
-        tmem_ld16(lane_addr + 384 + 64 * par + c4 * 16, o1);
-        tmem_wait_ld();
-#pragma unroll
-        for (int e8 = 0; e8 < 2; ++e8) {
-          float o[8];
-#pragma unroll
-          for (int e = 0; e < 8; ++e) {
-            const float v0 = has0 ? __uint_as_float(o0[e8 * 8 + e]) * s0 : 0.f;
-            const float v1 = has1 ? __uint_as_float(o1[e8 * 8 + e]) * s1 : 0.f;
-            o[e] = v0 + v1;
-          }
-          uint4 w;
-          w.x = Elem<T>::from2(o[0], o[1]);
-          w.y = Elem<T>::from2(o[2], o[3]);
-          w.z = Elem<T>::from2(o[4], o[5]);
-          w.w = Elem<T>::from2(o[6], o[7]);
-          const int chunk = c4 * 2 + e8;
-          *reinterpret_cast<uint4*>(stage + lane * 128 + ((chunk ^ (lane & 7)) << 4)) = w;
-        }
-      }
-      tc_fence_before();
-      mbar_arrive(&bars->o_free);  // O may take the next item's first PV
-      __syncwarp();
-#pragma unroll
-      for (int itr = 0; itr < 8; ++itr) {
-        const int rl = itr * 4 + (lane >> 3), chunk = lane & 7;
-        const int R = quarter * 32 + rl, iR = R & (ppt - 1);
-        if (iR < it.rows_valid) {
-          T* orow = static_cast<T*>(p.out) +
-                    ((static_cast<int64_t>(it.s) * p.Hq + it.kvh * G + (R >> lppt)) * p.Lq +
-                     it.qt * ppt + iR) * kHD;
-          *reinterpret_cast<uint4*>(orow + 64 * par + chunk * 8) =
-              *reinterpret_cast<const uint4*>(stage + rl * 128 + ((chunk ^ (rl & 7)) << 4));
-        }
-      }
-      __syncwarp();
+      ml[par * kBM + r] = make_float2(m_ref, l);
+      mbar_arrive(&bars->ml_ready);
       g += n;
       ++done;
-      L = Ln;
-      it = nx;
-      // Every S MMA of this item is done, so the Q buffer is free.
-      qn.store(smem + kOffQ, p.scale_log2, tid);
-      fence_proxy_async_smem();
-      mbar_arrive(&bars->q_ready);
+      L = item_resolve(p, nx, n_items, n_qt, ppt, it, true);
     }
     if (!ok) fail(kStatusWaitTimeout);
   }

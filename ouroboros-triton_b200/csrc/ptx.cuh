@@ -80,6 +80,20 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
   }
 }
 
+// The same wait for warps that are not on a critical path: sleeps `sleep_ns`
+// between polls so that their issue slots go to the warps sharing the
+// scheduler.
+__device__ __forceinline__ bool mbar_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t sleep_ns,
+                                                uint64_t limit_ns = 2000000000ull) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = global_timer_ns();
+  for (uint32_t i = 1;; ++i) {
+    __nanosleep(sleep_ns);
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 15u) == 0 && global_timer_ns() - t0 > limit_ns) return false;
+  }
+}
+
 // ---------------------------------------------------------------------------
 // TMA (bulk tensor copies global -> shared, completion on an mbarrier)
 // ---------------------------------------------------------------------------
@@ -190,6 +204,21 @@ __device__ __forceinline__ float max3f(float a, float b, float c) {
 // Named barrier over `nthreads` threads (id 0 is __syncthreads).
 __device__ __forceinline__ void named_barrier(uint32_t id, uint32_t nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
+// Per-thread register budget of the executing warpgroup (all four warps run the
+// same instruction). Increases draw on what decreases released: the budgets of
+// all warpgroups, times their threads, must add up to at most the registers the
+// block was launched with, or an increase never completes.
+template <uint32_t kRegs>
+__device__ __forceinline__ void regs_increase() {
+  static_assert(kRegs >= 24 && kRegs <= 256 && kRegs % 8 == 0, "setmaxnreg range");
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegs));
+}
+template <uint32_t kRegs>
+__device__ __forceinline__ void regs_decrease() {
+  static_assert(kRegs >= 24 && kRegs <= 256 && kRegs % 8 == 0, "setmaxnreg range");
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegs));
 }
 
 template <typename T>
