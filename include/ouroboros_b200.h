@@ -201,7 +201,8 @@ typedef struct ouro_attention_args {
   int32_t max_blocks, num_phys_blocks, max_positions;
   int32_t dtype, causal, kernel; /* kernel: 0 auto, 1 CUDA cores, 2 tensor cores */
   float softmax_scale;        /* <= 0: 1/sqrt(D) */
-  void* workspace;            /* tensor-core path: rotated-key scratch, 16-B aligned */
+  void* workspace;            /* tensor-core path: rotated-key scratch + 256-B launch
+                                 counter (zeroed by the library), 16-B aligned */
   size_t workspace_bytes;     /* >= ouro_attention_plan's bytes */
   const int32_t* krot_valid;  /* tensor-core path, optional device [S]: keys
                                  [0, krot_valid[s]) of sequence s are already rotated in
@@ -217,7 +218,7 @@ typedef struct ouro_attention_args {
 } ouro_attention_args;
 
 /* Kernel choice and the workspace the tensor-core path needs
- * (S * Hkv * max_blocks * 64 * D elements of the cache dtype; 0 on CUDA cores). */
+ * (S * Hkv * max_blocks * 64 * D elements of the cache dtype + 256 bytes; 0 on CUDA cores). */
 int ouro_attention_plan(const ouro_attention_args* args, size_t* workspace_bytes,
                         int32_t* uses_tensor_cores);
 int ouro_paged_attention(const ouro_attention_args* args, void* stream);

@@ -13,10 +13,11 @@
 // item. Query tiles are double-buffered: item d uses buffer d % 2.
 //   warps 8, 10 TMA producers for two separate rings, 3 K and 2 V stages (128-byte
 //               swizzle, layout [64-column atom][128 keys][128 B]): K tiles,
-//               already rotated, from the dense scratch written by rope_k.cu
-//               (one box of 128 keys per atom), refilled as soon as S_j is
-//               done; V tiles from the paged cache (boxes of 64 keys, one per
-//               block), refilled when PV_j is done
+//               already rotated, from a dense scratch (one box of 128 keys per
+//               atom), refilled as soon as S_j is done; V tiles from the paged
+//               cache (boxes of 64 keys, one per block), refilled when PV_j is
+//               done. A K tile holding keys that this launch rotates waits for
+//               the grid-wide rotation barrier (below)
 //   warp 9      TMEM owner and MMA issuer: S_j = Q K_j^T into TMEM buffer
 //               j % 2, then O_{j%2} += P_j V_j with P_j read from TMEM (V as an
 //               MN-major operand), tcgen05.commit to mbarriers; after an item's
@@ -33,7 +34,12 @@
 //               2^8), P = exp2(S - m) as bf16/fp16 pairs stored over the tile's
 //               own S columns. After an item's last tile a warp publishes its
 //               (m, l) and starts on the next item.
-//   warps 12-15 epilogue, one TMEM lane quarter each (one row per thread): once
+//   warps 12-15 key rotation first: RoPE for the keys that no earlier call
+//               sharing the workspace rotated (each CTA a share, written to the
+//               scratch), then one arrival per CTA on a grid-wide counter the
+//               launcher zeroes (the launch is cooperative, so every CTA is
+//               resident);
+//               then epilogue, one TMEM lane quarter each (one row per thread): once
 //               O is final, O = (2^(m_0-m) O_0 + 2^(m_1-m) O_1) /
 //               (2^(m_0-m) l_0 + 2^(m_1-m) l_1), m = max(m_0, m_1), staged in
 //               the item's own (now unused) query buffer and stored coalesced;
@@ -41,8 +47,8 @@
 //               item after next is rotated into the same buffer.
 // TMEM columns: S/P buffers at 0 and 128, O_0 at 256, O_1 at 384 (512 allocated).
 // Registers: the block launches with 128 per thread (512 threads); the softmax
-// warpgroups raise theirs to 168, the producer/MMA warpgroup lowers to 56 and
-// the epilogue to 120.
+// warpgroups raise theirs to 160, the producer/MMA warpgroup lowers to 56 and
+// the rotation/epilogue warpgroup raises to 136.
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -72,10 +78,11 @@ constexpr int kWarpEpi = 12;                          // first epilogue warp
 constexpr int kEpiThreads = 128;
 constexpr int kThreads = 16 * 32;
 // Per-thread register budgets after the split (launch: 65536 / kThreads = 128).
-constexpr int kRegsSoftmax = 168, kRegsIssue = 56, kRegsEpi = 120;
-static_assert(2 * 128 * kRegsSoftmax + 128 * kRegsIssue + 128 * kRegsEpi <= 65536,
+constexpr uint32_t kRegsLaunch = 128;
+constexpr uint32_t kRegsSoftmax = 160, kRegsIssue = 56, kRegsEpi = 136;
+static_assert(2 * 128 * kRegsSoftmax + 128 * kRegsIssue + 128 * kRegsEpi <= kThreads * kRegsLaunch,
               "register split exceeds the launch allocation");
-static_assert(kThreads * 128 == 65536, "launch allocation of 128 registers per thread");
+static_assert(kThreads * kRegsLaunch == 65536, "launch allocation of 128 registers per thread");
 // Named barriers (id 0 is __syncthreads).
 constexpr uint32_t kBarSoftmax = 1, kBarEpi = 2;
 constexpr float kRescaleLog2 = 8.0f;
@@ -277,6 +284,102 @@ __device__ __forceinline__ int item_resolve(const RowsParams& p, const ItemLoads
   return next_item(p, a.L + gridDim.x, n_items, n_qt, ppt, it, report);
 }
 
+// RoPE for the keys that no earlier call sharing this workspace rotated (blocks
+// b with (b + 1) * 64 > krot_valid[s] that start inside the sequence), written
+// to the dense scratch [S, Hkv, bps * 64, 128] the K producer streams from.
+// Units (sequence, block, group of 4 KV heads) go round-robin over the CTAs; in
+// a CTA the 128 threads of the epilogue warpgroup take a unit in two passes of
+// 32 rows: thread t owns row t / 4 (+ 32) and the 16 half-split pairs
+// (d, d + 64), d in [16 (t % 4), +16), and reads the row's cos/sin once for the
+// group. Lane k of each warp looks up unit k of a batch of 32, so the lookups'
+// loads overlap, and a pass issues all its loads (cos/sin and the 4 heads)
+// before it rotates: two round trips to memory per unit. Rows past the
+// sequence are rotated too (their scores are masked); rows past the RoPE
+// tables get the identity rotation.
+template <typename T>
+__device__ void rotate_new_keys(const RowsParams& p, T* krot, int bps, int t) {
+  constexpr int kGroup = 4, kHalf = kHD / 2;
+  const int groups = (p.Hkv + kGroup - 1) / kGroup;
+  const int64_t per_seq = static_cast<int64_t>(bps) * groups;
+  const int64_t n_units = static_cast<int64_t>(p.S) * per_seq;
+  const int lane = t & 31;
+  for (int64_t base = blockIdx.x; base < n_units; base += 32 * static_cast<int64_t>(gridDim.x)) {
+    const int64_t uk = base + static_cast<int64_t>(lane) * gridDim.x;
+    int phys = -2;  // -2: nothing to rotate in unit k
+    if (uk < n_units) {
+      const int s = static_cast<int>(uk / per_seq);
+      const int b = static_cast<int>((uk - s * per_seq) / groups);
+      // three independent loads (b < bps = max_blocks, so the entry exists)
+      const int kv = p.krot_valid ? p.krot_valid[s] : 0;
+      const int len = p.seq_lens[s];
+      const int entry = p.page_table[static_cast<int64_t>(s) * p.max_blocks + b];
+      if (b * kBlock < len && (b + 1) * kBlock > kv) phys = entry;
+    }
+#pragma unroll 1
+    for (int k = 0; k < 32; ++k) {
+      const int ph = __shfl_sync(0xffffffffu, phys, k);
+      if (ph == -2) continue;
+      if (ph < 0 || ph >= p.n_phys) {
+        if (t == 0 && p.status) atomicOr(p.status, kStatusBadPageEntry);
+        continue;
+      }
+      const int64_t u = base + static_cast<int64_t>(k) * gridDim.x;
+      const int s = static_cast<int>(u / per_seq);
+      const int rem = static_cast<int>(u - s * per_seq);
+      const int b = rem / groups, h0 = (rem - b * groups) * kGroup;
+      const int qd = (t & 3) * 16;
+#pragma unroll 1
+      for (int pass = 0; pass < 2; ++pass) {
+        const int row = (t >> 2) + 32 * pass, pos = b * kBlock + row;
+        const bool in_table = pos < p.max_pos;
+        const T* src = static_cast<const T*>(p.k) +
+                       (static_cast<int64_t>(ph) * p.Hkv * kBlock + row) * kHD + qd;
+        T* dst = krot + (static_cast<int64_t>(s) * p.Hkv * bps * kBlock + pos) * kHD + qd;
+        // every load of the pass first: the row's cos/sin and the 4 heads' pairs
+        float4 cv[4], sv[4];
+        uint4 lo[kGroup][2], hi[kGroup][2];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          cv[i] = make_float4(1.f, 1.f, 1.f, 1.f);
+          sv[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+        if (in_table) {
+          const float4* cr = reinterpret_cast<const float4*>(p.cos + static_cast<int64_t>(pos) * kHalf + qd);
+          const float4* sr = reinterpret_cast<const float4*>(p.sin + static_cast<int64_t>(pos) * kHalf + qd);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) cv[i] = cr[i], sv[i] = sr[i];
+        }
+#pragma unroll
+        for (int h = 0; h < kGroup; ++h)
+          if (h0 + h < p.Hkv) {
+            const uint4* in = reinterpret_cast<const uint4*>(src + (h0 + h) * kBlock * kHD);
+            lo[h][0] = in[0], lo[h][1] = in[1];
+            hi[h][0] = in[kHalf / 8], hi[h][1] = in[kHalf / 8 + 1];
+          }
+        const float* c = reinterpret_cast<const float*>(cv);
+        const float* sn = reinterpret_cast<const float*>(sv);
+#pragma unroll
+        for (int h = 0; h < kGroup; ++h)
+          if (h0 + h < p.Hkv) {
+            rope8<T>(lo[h][0], hi[h][0], c, sn, 1.f);
+            rope8<T>(lo[h][1], hi[h][1], c + 8, sn + 8, 1.f);
+            uint4* out = reinterpret_cast<uint4*>(dst + static_cast<int64_t>(h0 + h) * bps * kBlock * kHD);
+            out[0] = lo[h][0], out[1] = lo[h][1];
+            out[kHalf / 8] = hi[h][0], out[kHalf / 8 + 1] = hi[h][1];
+          }
+      }
+    }
+  }
+}
+
+// Grid-wide arrival after a CTA's rotations on a word the launcher zeroes
+// before the launch; the K producers wait for it to reach gridDim.x. The launch
+// is cooperative, so every CTA that is waited for is resident.
+__device__ __forceinline__ void rotation_arrive(unsigned long long* word) {
+  __threadfence();
+  atomicAdd(word, 1ull);
+}
+
 // Four query units of an item, loaded into registers (16-byte vectors, all
 // loads issued together) and then rotated and scaled by softmax_scale * log2 e
 // into the swizzled Q buffer. Row R is head kvh*G + R / ppt at position
@@ -333,7 +436,7 @@ template <typename T, bool kScoped>
 __global__ void __launch_bounds__(kThreads, 1)
     prefill_tc_kernel(const __grid_constant__ CUtensorMap tm_k,
                       const __grid_constant__ CUtensorMap tm_v, const RowsParams p,
-                      int32_t krot_rows_per_head) {
+                      int32_t krot_rows_per_head, unsigned long long* rot_sync) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = smem_raw;
   if ((smem_u32(smem) & 1023u) != 0) {  // 128-byte-swizzled TMA / UMMA tiles need 1 KB alignment
@@ -387,7 +490,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   // slots and TMEM buffers rotate across item boundaries, and every barrier
   // phase follows from the global tile index g (or the item count done).
   if (warp >= kWarpK && warp < kWarpEpi) {
-    regs_decrease<kRegsIssue>();
+    regs_set<kRegsLaunch, kRegsIssue>();
     if (warp == kWarpK || warp == kWarpV) {
       // ------------------------------- TMA producers -------------------------------
       if (lane == 0) {
@@ -399,11 +502,30 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint8_t* ring = smem + (is_k ? kOffK : kOffV);
         const uint32_t stages = is_k ? kStagesK : kStagesV;
         uint32_t g = 0;
+        // Key tiles holding keys that this launch rotates wait until every CTA
+        // has done its rotations (once; tiles of keys rotated by earlier calls
+        // load at once).
+        const unsigned long long rot_done = gridDim.x;
+        bool rotated = !is_k;
         Item it;
         for (int L = next_item(p, blockIdx.x, n_items, n_qt, ppt, it); L < n_items && !*s_abort;
              L = next_item(p, L + gridDim.x, n_items, n_qt, ppt, it)) {
           const int32_t* row = p.page_table + static_cast<int64_t>(it.s) * p.max_blocks;
+          const int kv = (!rotated && p.krot_valid) ? p.krot_valid[it.s] : 0;
           for (int j = 0; j < it.n_tiles; ++j, ++g) {
+            if (!rotated && (j + 1) * kBN > kv) {
+              const uint64_t t0 = global_timer_ns();
+              while (ld_acquire_gpu(rot_sync) < rot_done && !*s_abort) {
+                __nanosleep(256);  // one polling thread per CTA, on one word
+                if (global_timer_ns() - t0 > 2000000000ull) {
+                  fail(kStatusWaitTimeout);
+                  break;
+                }
+              }
+              if (*s_abort) break;
+              fence_proxy_async_global();
+              rotated = true;
+            }
             const uint32_t st = g % stages;
             if (g >= stages && !mbar_wait(&empty[st], ((g / stages) - 1) & 1)) {
               fail(kStatusWaitTimeout);
@@ -529,7 +651,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp >= kWarpEpi) {
     // ------------------------------ epilogue warps 12-15 ------------------------------
-    regs_decrease<kRegsEpi>();
+    regs_set<kRegsLaunch, kRegsEpi>();
+    // First this CTA's share of the key rotation (the softmax warps meanwhile
+    // rotate the first query tiles; the first epilogue is an item away).
+    {
+      const int t = threadIdx.x - kWarpEpi * 32;
+      rotate_new_keys<T>(p, static_cast<T*>(p.workspace), krot_rows_per_head / kBlock, t);
+      fence_proxy_async_global();
+      named_barrier(kBarEpi, kEpiThreads);
+      if (t == 0) rotation_arrive(rot_sync);
+    }
     const int quarter = warp & 3;
     const int r = quarter * 32 + lane;  // TMEM lane == query row == staged output row
     const uint32_t lane_addr = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
@@ -627,7 +758,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (!ok) fail(kStatusWaitTimeout);
   } else {
     // ------------------------------ softmax warps 0-7 ------------------------------
-    regs_increase<kRegsSoftmax>();
+    regs_set<kRegsLaunch, kRegsSoftmax>();
     const int quarter = warp & 3, par = warp >> 2;  // TMEM lane quarter, tile parity
     const int r = quarter * 32 + lane;              // TMEM lane == query row
     const int tid = threadIdx.x;                    // 0 .. 255
@@ -883,9 +1014,15 @@ bool prefill_tc_supported(const RowsParams& p, int dtype) {
   return prefill_encode_fn() != nullptr;
 }
 
-int64_t prefill_workspace_bytes(const RowsParams& p) {
+namespace {
+// Rotated-key scratch, then 256 bytes for the launch's rotation barrier word.
+int64_t krot_bytes(const RowsParams& p) {
   return static_cast<int64_t>(p.S) * p.Hkv * p.max_blocks * kBlock * kHD * 2;
 }
+
+}  // namespace
+
+int64_t prefill_workspace_bytes(const RowsParams& p) { return krot_bytes(p) + 256; }
 
 cudaError_t launch_prefill_tc(const RowsParams& p, int dtype, cudaStream_t stream) {
   if (!prefill_tc_supported(p, dtype)) return cudaErrorNotSupported;
@@ -901,19 +1038,19 @@ cudaError_t launch_prefill_tc(const RowsParams& p, int dtype, cudaStream_t strea
   const uint64_t k_rows = static_cast<uint64_t>(p.S) * p.Hkv * rows_per_head;
   if (!kv_map(&mk, p.workspace, dt, k_rows, kBN) || !kv_map(&mv, p.v, dt, v_rows, kBlock))
     return cudaErrorInvalidValue;
-  cudaError_t e = launch_rope_k(p, dtype, p.workspace, p.max_blocks, stream);
-  if (e != cudaSuccess) return e;
   // Persistent CTAs: one per SM (shared memory allows no second), each walking
-  // items c, c + grid, ...
+  // items c, c + grid, ... The launch is cooperative: the K producers wait for
+  // the key rotations of all CTAs, so all of them must be resident.
   const int ppt = kBM / p.G;
   const int64_t n_items = static_cast<int64_t>((p.Lq + ppt - 1) / ppt) * p.Hkv * p.S;
   if (n_items >= (int64_t(1) << 31)) return cudaErrorInvalidValue;
   int dev = 0, sms = 0;
-  e = cudaGetDevice(&dev);
+  cudaError_t e = cudaGetDevice(&dev);
   if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   if (e != cudaSuccess) return e;
   dim3 grid(static_cast<unsigned>(std::min<int64_t>(n_items, sms)));
-  using Kernel = void (*)(const CUtensorMap, const CUtensorMap, const RowsParams, int32_t);
+  using Kernel = void (*)(const CUtensorMap, const CUtensorMap, const RowsParams, int32_t,
+                          unsigned long long*);
   const bool scoped = p.scope_tags != nullptr;
   Kernel kernel = dtype == 2 ? (scoped ? prefill_tc_kernel<__nv_bfloat16, true>
                                        : prefill_tc_kernel<__nv_bfloat16, false>)
@@ -921,8 +1058,21 @@ cudaError_t launch_prefill_tc(const RowsParams& p, int dtype, cudaStream_t strea
                                        : prefill_tc_kernel<__half, false>);
   e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
   if (e != cudaSuccess) return e;
-  kernel<<<grid, kThreads, kSmemBytes, stream>>>(mk, mv, p, rows_per_head);
-  return cudaGetLastError();
+  unsigned long long* rot_sync =
+      reinterpret_cast<unsigned long long*>(static_cast<uint8_t*>(p.workspace) + krot_bytes(p));
+  e = cudaMemsetAsync(rot_sync, 0, sizeof(*rot_sync), stream);
+  if (e != cudaSuccess) return e;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = kSmemBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, mk, mv, p, rows_per_head, rot_sync);
 }
 
 }  // namespace ouro

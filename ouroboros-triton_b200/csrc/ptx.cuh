@@ -80,6 +80,19 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
   }
 }
 
+// 64-bit load with acquire semantics at GPU scope (flags written by other CTAs).
+__device__ __forceinline__ uint64_t ld_acquire_gpu(const unsigned long long* p) {
+  uint64_t v;
+  asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Orders this thread's generic-proxy global accesses with later async-proxy
+// (TMA) accesses to global memory.
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
 // The same wait for warps that are not on a critical path: sleeps `sleep_ns`
 // between polls so that their issue slots go to the warps sharing the
 // scheduler.
@@ -219,6 +232,13 @@ template <uint32_t kRegs>
 __device__ __forceinline__ void regs_decrease() {
   static_assert(kRegs >= 24 && kRegs <= 256 && kRegs % 8 == 0, "setmaxnreg range");
   asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegs));
+}
+// From the launch budget kFrom to kTo: an increase, a decrease (which may only
+// lower the count), or nothing.
+template <uint32_t kFrom, uint32_t kTo>
+__device__ __forceinline__ void regs_set() {
+  if constexpr (kTo > kFrom) regs_increase<kTo>();
+  else if constexpr (kTo < kFrom) regs_decrease<kTo>();
 }
 
 template <typename T>

@@ -43,9 +43,5 @@ bool prefill_tc_supported(const RowsParams& p, int dtype);
 // Scratch for the rotated keys: S * Hkv * max_blocks * 64 * D elements.
 int64_t prefill_workspace_bytes(const RowsParams& p);
 cudaError_t launch_prefill_tc(const RowsParams& p, int dtype, cudaStream_t stream);
-// Writes RoPE-rotated keys of every block below seq_len into `krot`
-// ([S, Hkv, blocks_per_seq * 64, 128], the cache dtype).
-cudaError_t launch_rope_k(const RowsParams& p, int dtype, void* krot, int32_t blocks_per_seq,
-                          cudaStream_t stream);
 
 }  // namespace ouro
