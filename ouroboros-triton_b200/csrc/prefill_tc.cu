@@ -34,12 +34,12 @@
 //               2^8), P = exp2(S - m) as bf16/fp16 pairs stored over the tile's
 //               own S columns. After an item's last tile a warp publishes its
 //               (m, l) and starts on the next item.
-//   warps 12-15 key rotation first: RoPE for the keys that no earlier call
-//               sharing the workspace rotated (each CTA a share, written to the
-//               scratch), then one arrival per CTA on a grid-wide counter the
-//               launcher zeroes (the launch is cooperative, so every CTA is
-//               resident);
-//               then epilogue, one TMEM lane quarter each (one row per thread): once
+//   warps 12-15 first the key rotation: RoPE for the keys that no earlier
+//               call sharing the workspace rotated (each CTA a share, written
+//               to the scratch), then one arrival per CTA on a grid-wide
+//               counter the launcher zeroes (the launch is cooperative, so
+//               every CTA is resident). Then the epilogue, one TMEM lane
+//               quarter per warp (one row per thread): once
 //               O is final, O = (2^(m_0-m) O_0 + 2^(m_1-m) O_1) /
 //               (2^(m_0-m) l_0 + 2^(m_1-m) l_1), m = max(m_0, m_1), staged in
 //               the item's own (now unused) query buffer and stored coalesced;
@@ -71,7 +71,7 @@ constexpr int kBM = 128;          // query rows per CTA
 constexpr int kBN = 128;          // keys per tile
 constexpr int kAtom = 128 * 128;  // one 64-column atom of a 128-row tile (bytes)
 constexpr int kTile = 2 * kAtom;  // 128 rows x 128 columns x 2 bytes
-constexpr int kSoftmaxWarps = 8;                   // 4 lane quarters x 2 key halves
+constexpr int kSoftmaxWarps = 8;                   // 4 lane quarters x 2 tile parities
 constexpr int kSoftmaxThreads = kSoftmaxWarps * 32;
 constexpr int kWarpK = 8, kWarpMma = 9, kWarpV = 10;  // K loads, MMA / TMEM, V loads
 constexpr int kWarpEpi = 12;                          // first epilogue warp
