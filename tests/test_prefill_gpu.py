@@ -137,6 +137,39 @@ def test_chunked_prefill_reuses_rotated_keys(cuda):
                 k[pt[s, b]] = 7.0
 
 
+def test_key_rotation_many_units_per_cta(cuda):
+    """A 32-token chunk at the end of ~9k-token sequences: 16 work items, so 16
+    CTAs rotate 564 units of 64 keys x 4 KV heads (several lookup batches per
+    CTA). A second launch on the same workspace with krot_valid inside a block
+    (100, 4000) re-rotates only from that block on: the cache rows of the
+    blocks wholly below it are overwritten first and must not matter."""
+    hq, hkv, L = 32, 8, 32
+    totals = [9000, 8500]
+    starts = [t - L for t in totals]
+    pt, q, k, v, cos, sin = _case(77, totals, hq, hkv, L, torch.bfloat16)
+    want = ao.prefill_attention(pt, q.float().cpu().numpy(), k.float().cpu().numpy(),
+                                v.float().cpu().numpy(), starts, totals, cos, sin, causal=True)
+    ptd = torch.from_numpy(pt).cuda()
+    cos_d, sin_d = torch.from_numpy(cos).cuda(), torch.from_numpy(sin).cuda()
+    starts_d = torch.tensor(starts, dtype=torch.int32, device="cuda")
+    lens_d = torch.tensor(totals, dtype=torch.int32, device="cuda")
+    ws = None
+    for kv in (None, [100, 4000]):
+        status = torch.zeros(1, dtype=torch.int32, device="cuda")
+        call = ba.PrefillCall(ptd, q, k, v, starts_d, lens_d, cos_d, sin_d, kernel="tc",
+                              status=status, workspace=ws,
+                              krot_valid=None if kv is None else torch.tensor(kv, dtype=torch.int32))
+        ws = call.workspace
+        out = call.launch()
+        torch.cuda.synchronize()
+        assert int(status.item()) == 0
+        _check(out, want, f"krot_valid={kv}")
+        if kv is None:
+            for s_, kv_s in enumerate([100, 4000]):
+                for b in range(kv_s // 64):
+                    k[pt[s_, b]] = 7.0
+
+
 @pytest.mark.parametrize("hq,hkv,dtype,kernel", [
     (32, 8, torch.bfloat16, "tc"), (16, 2, torch.float16, "tc"), (8, 4, torch.float32, "simt")])
 def test_prefill_with_token_scope_vs_oracle(cuda, hq, hkv, dtype, kernel):
