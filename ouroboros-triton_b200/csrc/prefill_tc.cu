@@ -29,11 +29,13 @@
 //               warps of a row never wait on each other inside the key loop,
 //               and since S of tile j + 1 is ready half a period after S of
 //               tile j, one warp's max pass overlaps the other's exponentials
-//               on the shared MUFU. Per tile: max over the 128 scores (two TMEM
-//               passes), lazy rescaling of O (only when m grows by more than
-//               2^8), P = exp2(S - m) as bf16/fp16 pairs stored over the tile's
-//               own S columns. After an item's last tile a warp publishes its
-//               (m, l) and starts on the next item.
+//               on the shared MUFU. Per tile: the 128 scores of the row in
+//               registers (one TMEM round trip), their max, lazy rescaling of O
+//               (only when m grows by more than 2^8), P = exp2(S - m) as
+//               bf16/fp16 pairs stored over the tile's own S columns, the first
+//               64 keys published on their own so the first half of PV starts
+//               while the rest are exponentiated. After an item's last tile a
+//               warp publishes its (m, l) and starts on the next item.
 //   warps 12-15 first the key rotation: RoPE for the keys that no earlier
 //               call sharing the workspace rotated (each CTA a share, written
 //               to the scratch), then one arrival per CTA on a grid-wide
@@ -47,15 +49,14 @@
 //               item after next is rotated into the same buffer.
 // TMEM columns: S/P buffers at 0 and 128, O_0 at 256, O_1 at 384 (512 allocated).
 // Registers: the block launches with 128 per thread (512 threads); the softmax
-// warpgroups raise theirs to 160, the producer/MMA warpgroup lowers to 56 and
-// the rotation/epilogue warpgroup raises to 136.
+// warpgroups raise theirs to 168, the producer/MMA warpgroup lowers to 56 and
+// the rotation/epilogue warpgroup lowers to 120.
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
 #include <algorithm>
 #include <cstring>
-#include <type_traits>
 
 #include "attention.hpp"
 #include "ptx.cuh"
@@ -79,17 +80,13 @@ constexpr int kEpiThreads = 128;
 constexpr int kThreads = 16 * 32;
 // Per-thread register budgets after the split (launch: 65536 / kThreads = 128).
 constexpr uint32_t kRegsLaunch = 128;
-constexpr uint32_t kRegsSoftmax = 160, kRegsIssue = 56, kRegsEpi = 136;
+constexpr uint32_t kRegsSoftmax = 168, kRegsIssue = 56, kRegsEpi = 120;
 static_assert(2 * 128 * kRegsSoftmax + 128 * kRegsIssue + 128 * kRegsEpi <= kThreads * kRegsLaunch,
               "register split exceeds the launch allocation");
 static_assert(kThreads * kRegsLaunch == 65536, "launch allocation of 128 registers per thread");
 // Named barriers (id 0 is __syncthreads).
 constexpr uint32_t kBarSoftmax = 1, kBarEpi = 2;
 constexpr float kRescaleLog2 = 8.0f;
-// Pairs of every 4 key pairs whose exponential goes through exp2_poly2 instead
-// of MUFU ex2 (0..4). Measured: every share above 0 is slower (the softmax is
-// bound by its instruction chain, not by the MUFU pipe).
-constexpr int kPolyPairs = 0;
 
 // Ring depths. K tile j + 3 may load once S_j is done (k_empty); three K slots
 // give the TMA the time of two tiles, which it needs when the MMA thread runs
@@ -131,7 +128,7 @@ static_assert(kSmemBytes <= 232448, "shared memory");
 struct Bars {
   uint64_t k_full[kStagesK], k_empty[kStagesK], v_full[kStagesV];
   uint64_t s_full[2];
-  uint64_t p_ready[2], pv_done[2];       // per S/P buffer = tile parity
+  uint64_t p_ready[2], p_half[2], pv_done[2];  // per S/P buffer = tile parity
   uint64_t q_ready[2];                   // per query buffer
   uint64_t ml_ready, ml_free, o_full, o_free;  // once per item
   uint32_t tmem_base;
@@ -185,26 +182,6 @@ __device__ __forceinline__ float fast_exp2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
-}
-
-// 2^x for a pair of x in [-126, 2^20] on the FMA pipes, so that part of the
-// softmax exponentials bypass the MUFU unit. Cody-Waite split x = n + f with
-// n = round(x) (the 1.5 * 2^23 shift trick leaves n in the low mantissa bits
-// of t) and f in [-0.5, 0.5]; 2^f from a degree-3 polynomial fitted for
-// minimal maximum relative error on [-0.5, 0.5] (Remez exchange, 7.5e-5 in
-// fp32 Horner form, far below the bf16 / fp16 rounding of P); 2^n is added
-// into the exponent field as n << 23 (t's exponent bits shift out).
-__device__ __forceinline__ uint64_t exp2_poly2(uint64_t x) {
-  constexpr float kShift = 12582912.0f;  // 1.5 * 2^23
-  constexpr float c0 = 0.99992806f, c1 = 0.69326097f, c2 = 0.24261113f, c3 = 0.05517167f;
-  const uint64_t t = f2add(x, f2pack(kShift, kShift));
-  const uint64_t f = f2sub(x, f2sub(t, f2pack(kShift, kShift)));
-  uint64_t p = f2fma(f2pack(c3, c3), f, f2pack(c2, c2));
-  p = f2fma(p, f, f2pack(c1, c1));
-  p = f2fma(p, f, f2pack(c0, c0));
-  const float2 pf = f2unpack(p), tf = f2unpack(t);
-  return f2pack(__uint_as_float(__float_as_uint(pf.x) + (__float_as_uint(tf.x) << 23)),
-                __uint_as_float(__float_as_uint(pf.y) + (__float_as_uint(tf.y) << 23)));
 }
 
 __device__ __forceinline__ uint32_t sw_off(int row, int chunk) {
@@ -463,6 +440,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int i = 0; i < 2; ++i) {
       mbar_init(&bars->s_full[i], 1);
       mbar_init(&bars->p_ready[i], 128);
+      mbar_init(&bars->p_half[i], 128);
       mbar_init(&bars->pv_done[i], 1);
       mbar_init(&bars->q_ready[i], 1);
     }
@@ -579,15 +557,21 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t b = gg & 1;
           if (!mbar_wait(&bars->v_full[b], (gg >> 1) & 1)) return false;
           if (j == 0 && dd > 0 && !mbar_wait(&bars->o_free, (dd - 1) & 1)) return false;
-          if (!mbar_wait(&bars->p_ready[b], (gg >> 1) & 1)) return false;
-          tc_fence_after();  // P was stored to TMEM by the softmax threads
           const uint64_t vd = v_desc + b * kSlot;
           const uint32_t a_tmem = tmem + b * 128, d_tmem = tmem + 256 + 128 * b;
+          // P of keys 0..63 (TMEM columns 0..31) is published before the rest
+          if (!mbar_wait(&bars->p_half[b], (gg >> 1) & 1)) return false;
+          tc_fence_after();  // P was stored to TMEM by the softmax threads
 #pragma unroll
-          for (int kk = 0; kk < kBN / 16; ++kk)
+          for (int kk = 0; kk < kBN / 32; ++kk)
             // A = P [128 rows x 16 keys] (8 TMEM columns); B = V [16 keys x 128 d] MN-major
             umma_f16_ts(d_tmem, a_tmem + 8 * kk, vd + kk * (2048 >> 4), idesc_pv,
                         (j < 2 && kk == 0) ? 0u : 1u);
+          if (!mbar_wait(&bars->p_ready[b], (gg >> 1) & 1)) return false;
+          tc_fence_after();
+#pragma unroll
+          for (int kk = kBN / 32; kk < kBN / 16; ++kk)
+            umma_f16_ts(d_tmem, a_tmem + 8 * kk, vd + kk * (2048 >> 4), idesc_pv, 1u);
           umma_commit(&bars->pv_done[b]);
           return true;
         };
@@ -834,13 +818,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       return max3f(mp[0], mp[1], fmaxf(mp[2], mp[3]));
     };
     // P = exp2(S - base) for 64 keys held in two 32-column blocks, packed to
-    // bf16/fp16 pairs (32 TMEM columns); returns their sum. kPoly (a compile-time
-    // constant, so each tile kind gets its own straight-line code) of every 4
-    // pairs use the FMA-pipe polynomial, the rest MUFU ex2; tiles with masked
-    // keys use MUFU throughout, so masked keys (-inf) give exactly 0.
-    auto exp64 = [&](auto poly, const uint32_t (&a)[32], const uint32_t (&b)[32], float base,
+    // bf16/fp16 pairs (32 TMEM columns); returns their sum. Masked keys (-inf)
+    // give exactly 0.
+    auto exp64 = [&](const uint32_t (&a)[32], const uint32_t (&b)[32], float base,
                      uint32_t (&pk)[32]) -> float {
-      constexpr int kPoly = decltype(poly)::value;
       const uint64_t base2 = f2pack(base, base);
       uint64_t lp[4] = {0, 0, 0, 0};
 #pragma unroll
@@ -848,9 +829,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t* v = e2 < 16 ? &a[2 * e2] : &b[2 * e2 - 32];
         const float2 xf =
             f2unpack(f2sub(f2pack(__uint_as_float(v[0]), __uint_as_float(v[1])), base2));
-        const uint64_t pv = (e2 & 3) < kPoly
-                                ? exp2_poly2(f2pack(fmaxf(xf.x, -126.f), fmaxf(xf.y, -126.f)))
-                                : f2pack(fast_exp2(xf.x), fast_exp2(xf.y));
+        const uint64_t pv = f2pack(fast_exp2(xf.x), fast_exp2(xf.y));
         lp[e2 & 3] = f2add(lp[e2 & 3], pv);
         const float2 pf = f2unpack(pv);
         pk[e2] = Elem<T>::from2(pf.x, pf.y);
@@ -885,57 +864,48 @@ __global__ void __launch_bounds__(kThreads, 1)
         // Tiles that lie wholly below every row's key limit skip the per-key masks
         // (never with a token scope).
         const bool full = !kScoped && __all_sync(0xffffffffu, key0 + kBN <= kmax_row);
-        // Pass 1: row max over the 128 scores; keys 0..63 stay in registers.
-        uint32_t sa[32], sb[32];
-        tmem_ld32(lane_addr + s_col + 64, sa);
-        tmem_ld32(lane_addr + s_col + 96, sb);
-        tmem_wait_ld();
-        float mx = fmaxf(mask_max32(sa, key0 + 64, kmax_row, full),
-                         mask_max32(sb, key0 + 96, kmax_row, full));
+        // All 128 scores of the row in registers: one TMEM round trip.
+        uint32_t sa[32], sb[32], sc[32], sd[32];
         tmem_ld32(lane_addr + s_col, sa);
         tmem_ld32(lane_addr + s_col + 32, sb);
+        tmem_ld32(lane_addr + s_col + 64, sc);
+        tmem_ld32(lane_addr + s_col + 96, sd);
         tmem_wait_ld();
-        mx = max3f(mx, mask_max32(sa, key0, kmax_row, full), mask_max32(sb, key0 + 32, kmax_row, full));
+        const float mx = fmaxf(fmaxf(mask_max32(sa, key0, kmax_row, full),
+                                     mask_max32(sb, key0 + 32, kmax_row, full)),
+                               fmaxf(mask_max32(sc, key0 + 64, kmax_row, full),
+                                     mask_max32(sd, key0 + 96, kmax_row, full)));
         const bool grow = mx > m_ref + kRescaleLog2 || (m_ref == -INFINITY && mx != -INFINITY);
         const float m_new = grow ? mx : m_ref;
         const float factor = (grow && m_ref != -INFINITY) ? fast_exp2(m_ref - m_new) : 1.f;
         // Rescale this parity's accumulator in TMEM. Its last PV (tile gg - 2)
         // finished before S of tile gg did, so no wait is needed.
         if (__any_sync(0xffffffffu, factor != 1.f)) {
-#pragma unroll
-          for (int c4 = 0; c4 < 4; ++c4) {
-            uint32_t raw[32];
-            tmem_ld32(lane_addr + o_col + c4 * 32, raw);
+#pragma unroll 1
+          for (int c8 = 0; c8 < 8; ++c8) {
+            uint32_t raw[16];
+            tmem_ld16(lane_addr + o_col + c8 * 16, raw);
             tmem_wait_ld();
 #pragma unroll
-            for (int e = 0; e < 32; ++e) raw[e] = __float_as_uint(__uint_as_float(raw[e]) * factor);
-            tmem_st32(lane_addr + o_col + c4 * 32, raw);
+            for (int e = 0; e < 16; ++e) raw[e] = __float_as_uint(__uint_as_float(raw[e]) * factor);
+            tmem_st16(lane_addr + o_col + c8 * 16, raw);
           }
         }
         l *= factor;
         m_ref = m_new;
         const float base = m_ref == -INFINITY ? 0.f : m_ref;
-        // Pass 2: P for keys 0..63 over S columns 0..31 (their scores are in
-        // registers), then keys 64..127 reloaded (columns 64..127, untouched)
-        // and stored over columns 32..63.
-        auto pass2 = [&](auto poly) {  // poly > 0 only in tiles without masked keys
+        // P of keys 0..63 over S columns 0..31, published on its own so the
+        // first half of PV starts while keys 64..127 are exponentiated.
+        {
           uint32_t pk[32];
-          l += exp64(poly, sa, sb, base, pk);
+          l += exp64(sa, sb, base, pk);
           tmem_st32(lane_addr + s_col, pk);
-          tmem_ld32(lane_addr + s_col + 64, sa);
-          tmem_ld32(lane_addr + s_col + 96, sb);
-          tmem_wait_ld();
-          if (decltype(poly)::value == 0 && !full) {
-            mask32(sa, key0 + 64, kmax_row);
-            mask32(sb, key0 + 96, kmax_row);
-          }
-          l += exp64(poly, sa, sb, base, pk);
+          tmem_wait_st();
+          tc_fence_before();
+          mbar_arrive(&bars->p_half[par]);
+          l += exp64(sc, sd, base, pk);
           tmem_st32(lane_addr + s_col + 32, pk);
-        };
-        if (kPolyPairs > 0 && full)  // warp-uniform
-          pass2(std::integral_constant<int, kPolyPairs>{});
-        else
-          pass2(std::integral_constant<int, 0>{});
+        }
         tmem_wait_st();
         tc_fence_before();
         mbar_arrive(&bars->p_ready[par]);
