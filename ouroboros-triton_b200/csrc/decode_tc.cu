@@ -6,11 +6,15 @@
 //   * Warp 0 builds the chunk's block list from the page table, the block
 //     mask and the token scope (blocks without an allowed key are skipped,
 //     never loaded) and primes a STAGES-deep
-//     ring of 16-token stages: for every KV head the K and V rows of the 16
-//     tokens (each a contiguous 4 KB run of the [n_phys, Hkv, 64, D] cache)
-//     plus the cos/sin rows of their positions, all TMA tiles with 128-byte
-//     swizzle, completion on an mbarrier. K/V use an evict-first L2 policy
-//     (streamed once); the RoPE tables evict-last (shared by every sequence).
+//     ring of 16-token stages: the K and V rows of the 16 tokens for all HPC
+//     KV heads (per head a contiguous 4 KB run of the [n_phys, Hkv, 64, D]
+//     cache) plus the cos/sin rows of their positions, all TMA tiles with
+//     128-byte swizzle, completion on an mbarrier. The cache is addressed as
+//     a 3-D tensor [n_phys * Hkv][64][D], so one box per 64-column half takes
+//     the 16 rows of all HPC heads (16 KB at D = 128, HPC = 8): four K/V
+//     copies per stage instead of 4 * HPC small ones, which measured 14 %
+//     more HBM bandwidth. K/V use an evict-first L2 policy (streamed once);
+//     the RoPE tables evict-last (shared by every sequence).
 //   * Stage i is consumed by the warps (head, i % 2): each owns KV head
 //     kvh0 + head and its G query heads, and keeps its own online-softmax
 //     state; the last of the HPC warps releasing a stage issues the TMA
@@ -94,16 +98,14 @@ __device__ __forceinline__ void issue_stage(const CUtensorMap* tm_k, const CUten
   *use_slot = use;  // consumers of this use wait for this word before the parity wait
   mbar_arrive_expect_tx(full, L::kStage + (p.scope_tags ? 16u : 0u));
   const int pos_row = b * kBlock + u * kTok;
+  // One box per 64-column half covers the 16 tokens of all HPC heads (16 KB at
+  // D = 128): [half][head][16 rows][128 B] in shared memory.
 #pragma unroll
-  for (int h = 0; h < HPC; ++h) {
-    const int y = (phys * p.Hkv + kvh0 + h) * kBlock + u * kTok;
-#pragma unroll
-    for (int bx = 0; bx < L::kKBoxes; ++bx) {
-      tma_load_2d(stg + L::kK + h * L::kHeadTile + bx * (kTok * 128), tm_k, bx * 64, y, full,
-                  pol_stream);
-      tma_load_2d(stg + L::kV + h * L::kHeadTile + bx * (kTok * 128), tm_v, bx * 64, y, full,
-                  pol_stream);
-    }
+  for (int bx = 0; bx < L::kKBoxes; ++bx) {
+    tma_load_3d(stg + L::kK + bx * (HPC * kTok * 128), tm_k, bx * 64, u * kTok,
+                phys * p.Hkv + kvh0, full, pol_stream);
+    tma_load_3d(stg + L::kV + bx * (HPC * kTok * 128), tm_v, bx * 64, u * kTok,
+                phys * p.Hkv + kvh0, full, pol_stream);
   }
 #pragma unroll
   for (int bx = 0; bx < L::kTBoxes; ++bx) {
@@ -301,8 +303,9 @@ __global__ void __launch_bounds__(HPC * kWph * 32, 1)
         break;
       }
       const uint8_t* stg = stages + st * L::kStage;
-      const uint32_t kbase = smem_u32(stg + L::kK + head * L::kHeadTile);
-      const uint32_t vbase = smem_u32(stg + L::kV + head * L::kHeadTile);
+      const uint32_t kbase = smem_u32(stg + L::kK + head * (kTok * 128));
+      const uint32_t vbase = smem_u32(stg + L::kV + head * (kTok * 128));
+      constexpr int kBoxStride = HPC * kTok * 128;  // between the 64-column halves
       const uint8_t* cosb = stg + L::kCos;
       const uint8_t* sinb = stg + L::kSin;
 
@@ -314,9 +317,9 @@ __global__ void __launch_bounds__(HPC * kWph * 32, 1)
         uint32_t ka[4], kb[4];
         {
           const int kc2 = kc + HALF_KC;
-          ldmatrix_x4(kbase + (kc >> 2) * (kTok * 128) + swz128(k_row, (kc & 3) * 2 + k_chunk),
+          ldmatrix_x4(kbase + (kc >> 2) * kBoxStride + swz128(k_row, (kc & 3) * 2 + k_chunk),
                       ka[0], ka[1], ka[2], ka[3]);
-          ldmatrix_x4(kbase + (kc2 >> 2) * (kTok * 128) + swz128(k_row, (kc2 & 3) * 2 + k_chunk),
+          ldmatrix_x4(kbase + (kc2 >> 2) * kBoxStride + swz128(k_row, (kc2 & 3) * 2 + k_chunk),
                       kb[0], kb[1], kb[2], kb[3]);
         }
 #pragma unroll
@@ -380,7 +383,7 @@ __global__ void __launch_bounds__(HPC * kWph * 32, 1)
       for (int mt = 0; mt < KC; ++mt) {
         const int box = mt >> 2, chunk = (mt & 3) * 2 + v_chunk;
         uint32_t vf[4];
-        ldmatrix_x4_trans(vbase + box * (kTok * 128) + swz128(v_row, chunk), vf[0], vf[1], vf[2],
+        ldmatrix_x4_trans(vbase + box * kBoxStride + swz128(v_row, chunk), vf[0], vf[1], vf[2],
                           vf[3]);
         MK::mma(o[mt], vf, pb0, pb1);
       }
@@ -538,6 +541,22 @@ bool make_map(CUtensorMap* m, const void* base, CUtensorMapDataType dt, uint64_t
          CUDA_SUCCESS;
 }
 
+// [n_phys * Hkv, 64, D] cache as a 3-D tensor: boxes of [heads][rows][64 columns], 128-byte swizzle.
+bool make_map_kv3(CUtensorMap* m, const void* base, CUtensorMapDataType dt, uint64_t D,
+                  uint64_t planes, uint32_t box_rows, uint32_t box_planes) {
+  EncodeTiledFn enc = encode_fn();
+  if (enc == nullptr) return false;
+  cuuint64_t dims[3] = {D, static_cast<cuuint64_t>(kBlock), planes};
+  cuuint64_t strides[2] = {D * 2, D * 2 * kBlock};
+  cuuint32_t box[3] = {64, box_rows, box_planes};
+  cuuint32_t estr[3] = {1, 1, 1};
+  std::memset(m, 0, sizeof(*m));
+  return enc(m, dt, 3, const_cast<void*>(base), dims, strides, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) ==
+         CUDA_SUCCESS;
+}
+
 template <int D, int HPC>
 size_t tc_smem_bytes(int split_blocks) {
   using L = TcLayout<D, HPC>;
@@ -548,9 +567,9 @@ size_t tc_smem_bytes(int split_blocks) {
 template <typename T, int D, int HPC>
 cudaError_t launch_tc_typed(const DecodeParams& p, CUtensorMapDataType dt, cudaStream_t stream) {
   CUtensorMap mk, mv, mc, ms;
-  const uint64_t kv_rows = static_cast<uint64_t>(p.n_phys) * p.Hkv * kBlock;
-  if (!make_map(&mk, p.k, dt, D, kv_rows, 2, 64, kTok) ||
-      !make_map(&mv, p.v, dt, D, kv_rows, 2, 64, kTok) ||
+  const uint64_t planes = static_cast<uint64_t>(p.n_phys) * p.Hkv;
+  if (!make_map_kv3(&mk, p.k, dt, D, planes, kTok, HPC) ||
+      !make_map_kv3(&mv, p.v, dt, D, planes, kTok, HPC) ||
       !make_map(&mc, p.cos, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, D / 2, p.max_pos, 4, 32, kTok) ||
       !make_map(&ms, p.sin, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, D / 2, p.max_pos, 4, 32, kTok))
     return cudaErrorInvalidValue;

@@ -125,6 +125,17 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* desc, 
       : "memory");
 }
 
+// 3-D tiled load of the box at (x = inner coordinate, y, z) into `dst`.
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* desc, int32_t x,
+                                            int32_t y, int32_t z, uint64_t* bar, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      ".L2::cache_hint [%0], [%1, {%2, %3, %4}], [%5], %6;" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(desc)), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar)),
+      "l"(policy)
+      : "memory");
+}
+
 // Untiled bulk copy (both addresses 16-byte aligned, size a multiple of 16).
 __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes,
                                           uint64_t* bar) {
