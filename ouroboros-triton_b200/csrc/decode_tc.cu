@@ -107,11 +107,9 @@ __device__ __forceinline__ void issue_stage(const CUtensorMap* tm_k, const CUten
     tma_load_3d(stg + L::kV + bx * (HPC * kTok * 128), tm_v, bx * 64, u * kTok,
                 phys * p.Hkv + kvh0, full, pol_stream);
   }
-#pragma unroll
-  for (int bx = 0; bx < L::kTBoxes; ++bx) {
-    tma_load_2d(stg + L::kCos + bx * (kTok * 128), tm_cos, bx * 32, pos_row, full, pol_keep);
-    tma_load_2d(stg + L::kSin + bx * (kTok * 128), tm_sin, bx * 32, pos_row, full, pol_keep);
-  }
+  // cos / sin rows as [16 rows][kTBoxes][128 B]: one box each
+  tma_load_3d(stg + L::kCos, tm_cos, 0, 0, pos_row, full, pol_keep);
+  tma_load_3d(stg + L::kSin, tm_sin, 0, 0, pos_row, full, pol_keep);
   if (p.scope_tags) bulk_load(tag_dst, p.scope_tags + s * p.scope_stride + pos_row, 16, full);
 }
 
@@ -326,7 +324,7 @@ __global__ void __launch_bounds__(HPC * kWph * 32, 1)
         for (int reg = 0; reg < 4; ++reg) {
           const int row = r + (reg & 1) * 8;
           const int t = kc * 16 + 2 * q4 + (reg & 2) * 4;
-          const uint32_t off = (t >> 5) * (kTok * 128) + swz128(row, (t & 31) >> 2) + (t & 3) * 4;
+          const uint32_t off = swz128(row * L::kTBoxes + (t >> 5), (t & 31) >> 2) + (t & 3) * 4;
           const uint64_t c2 = *reinterpret_cast<const uint64_t*>(cosb + off);
           const uint64_t s2 = *reinterpret_cast<const uint64_t*>(sinb + off);
           const uint64_t lo2 = MK::unpack2(ka[reg]);
@@ -525,22 +523,6 @@ EncodeTiledFn encode_fn() {
   return fn;
 }
 
-// Row-major [rows, inner] tensor, 128-byte-swizzled boxes of [box_rows, box_inner].
-bool make_map(CUtensorMap* m, const void* base, CUtensorMapDataType dt, uint64_t inner,
-              uint64_t rows, uint64_t elem_bytes, uint32_t box_inner, uint32_t box_rows) {
-  EncodeTiledFn enc = encode_fn();
-  if (enc == nullptr) return false;
-  cuuint64_t dims[2] = {inner, rows};
-  cuuint64_t strides[1] = {inner * elem_bytes};
-  cuuint32_t box[2] = {box_inner, box_rows};
-  cuuint32_t estr[2] = {1, 1};
-  std::memset(m, 0, sizeof(*m));
-  return enc(m, dt, 2, const_cast<void*>(base), dims, strides, box, estr,
-             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) ==
-         CUDA_SUCCESS;
-}
-
 // [n_phys * Hkv, 64, D] cache as a 3-D tensor: boxes of [heads][rows][64 columns], 128-byte swizzle.
 bool make_map_kv3(CUtensorMap* m, const void* base, CUtensorMapDataType dt, uint64_t D,
                   uint64_t planes, uint32_t box_rows, uint32_t box_planes) {
@@ -553,6 +535,21 @@ bool make_map_kv3(CUtensorMap* m, const void* base, CUtensorMapDataType dt, uint
   std::memset(m, 0, sizeof(*m));
   return enc(m, dt, 3, const_cast<void*>(base), dims, strides, box, estr,
              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) ==
+         CUDA_SUCCESS;
+}
+
+// [max_pos, halves * 32] fp32 table as a 3-D tensor [max_pos][halves][32]: boxes of 16 rows.
+bool make_map_tbl3(CUtensorMap* m, const void* base, uint64_t halves, uint64_t rows) {
+  EncodeTiledFn enc = encode_fn();
+  if (enc == nullptr) return false;
+  cuuint64_t dims[3] = {32, halves, rows};
+  cuuint64_t strides[2] = {128, 128 * halves};
+  cuuint32_t box[3] = {32, static_cast<cuuint32_t>(halves), static_cast<cuuint32_t>(kTok)};
+  cuuint32_t estr[3] = {1, 1, 1};
+  std::memset(m, 0, sizeof(*m));
+  return enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<void*>(base), dims, strides, box,
+             estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) ==
          CUDA_SUCCESS;
 }
@@ -570,8 +567,7 @@ cudaError_t launch_tc_typed(const DecodeParams& p, CUtensorMapDataType dt, cudaS
   const uint64_t planes = static_cast<uint64_t>(p.n_phys) * p.Hkv;
   if (!make_map_kv3(&mk, p.k, dt, D, planes, kTok, HPC) ||
       !make_map_kv3(&mv, p.v, dt, D, planes, kTok, HPC) ||
-      !make_map(&mc, p.cos, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, D / 2, p.max_pos, 4, 32, kTok) ||
-      !make_map(&ms, p.sin, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, D / 2, p.max_pos, 4, 32, kTok))
+      !make_map_tbl3(&mc, p.cos, D / 64, p.max_pos) || !make_map_tbl3(&ms, p.sin, D / 64, p.max_pos))
     return cudaErrorInvalidValue;
   const size_t smem = tc_smem_bytes<D, HPC>(p.split_blocks);
   auto kernel = decode_tc_kernel<T, D, HPC>;
