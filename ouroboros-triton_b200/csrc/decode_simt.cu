@@ -231,28 +231,65 @@ __global__ void __launch_bounds__(kSimtWarps * 32) decode_simt_kernel(const Deco
   }
 }
 
-// Merges the split-K partials of one (sequence, query head) per CTA.
+// Merges the split-K partials of one (sequence, query head) row per warp, four
+// rows per CTA: lanes hold the splits' (max, sum) 32 at a time, each split's
+// weight 2^(m_i - M) reaches every lane by shuffle, and lane t accumulates
+// columns 4t .. 4t + 3 of each 128-column pass with 16-byte loads (one column
+// per lane and pass of 32 when head_dim is not a multiple of 4).
 template <typename T>
 __global__ void __launch_bounds__(128) decode_combine_kernel(const DecodeParams p) {
-  const int s = blockIdx.x / p.Hq;
-  const int h = blockIdx.x % p.Hq;
-  const SeqGeom g = seq_geom(p, s);
-  if (g.nsplit <= 1) return;  // the decode kernel wrote the final row
-  const int64_t row = static_cast<int64_t>(s) * p.Hq + h;
+  const int lane = threadIdx.x & 31;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * 4 + (threadIdx.x >> 5);
+  if (row >= static_cast<int64_t>(p.S) * p.Hq) return;  // warp-uniform
+  const SeqGeom g = seq_geom(p, static_cast<int>(row / p.Hq));
+  const int n = g.nsplit;
+  if (n <= 1) return;  // the decode kernel wrote the final row
   const float* ml = p.ws_ml + row * p.max_splits * 2;
   float M = -INFINITY;
-  for (int i = 0; i < g.nsplit; ++i) M = fmaxf(M, ml[2 * i]);
+  for (int i = lane; i < n; i += 32) M = fmaxf(M, ml[2 * i]);
+#pragma unroll
+  for (int sh = 16; sh > 0; sh >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, sh));
   float L = 0.f;
   if (M != -INFINITY)
-    for (int i = 0; i < g.nsplit; ++i) L += ml[2 * i + 1] * exp2f(ml[2 * i] - M);
+    for (int i = lane; i < n; i += 32) L += ml[2 * i + 1] * exp2f(ml[2 * i] - M);
+#pragma unroll
+  for (int sh = 16; sh > 0; sh >>= 1) L += __shfl_xor_sync(0xffffffffu, L, sh);
   const float inv = L > 0.f ? 1.f / L : 0.f;
-  T* out = static_cast<T*>(p.out);
-  for (int d = threadIdx.x; d < p.D; d += blockDim.x) {
-    float O = 0.f;
-    if (M != -INFINITY)
-      for (int i = 0; i < g.nsplit; ++i)
-        O += p.ws_o[(row * p.max_splits + i) * p.D + d] * exp2f(ml[2 * i] - M);
-    out[row * p.D + d] = from_f<T>(O * inv);
+  const float* po = p.ws_o + row * p.max_splits * p.D;
+  T* out = static_cast<T*>(p.out) + row * p.D;
+  const bool vec = (p.D & 3) == 0;
+  const int per_pass = vec ? 128 : 32;
+  for (int d0 = 0; d0 < p.D; d0 += per_pass) {
+    const int d = d0 + (vec ? 4 * lane : lane);
+    const bool act = d < p.D;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int i0 = 0; i0 < n; i0 += 32) {
+      const int il = i0 + lane;
+      const float wl = (M != -INFINITY && il < n) ? exp2f(ml[2 * il] - M) : 0.f;
+      const int cnt = min(32, n - i0);
+#pragma unroll 4
+      for (int k = 0; k < cnt; ++k) {
+        const float w = __shfl_sync(0xffffffffu, wl, k);
+        const float* src = po + static_cast<int64_t>(i0 + k) * p.D + d;
+        if (act && vec) {
+          const float4 v = *reinterpret_cast<const float4*>(src);
+          acc.x += w * v.x;
+          acc.y += w * v.y;
+          acc.z += w * v.z;
+          acc.w += w * v.w;
+        } else if (act) {
+          acc.x += w * src[0];
+        }
+      }
+    }
+    if (act) {
+      out[d] = from_f<T>(acc.x * inv);
+      if (vec) {
+        out[d + 1] = from_f<T>(acc.y * inv);
+        out[d + 2] = from_f<T>(acc.z * inv);
+        out[d + 3] = from_f<T>(acc.w * inv);
+      }
+    }
   }
 }
 
@@ -289,7 +326,7 @@ cudaError_t launch_decode_simt_dtype(const DecodeParams& p, int dtype, cudaStrea
 }
 
 cudaError_t launch_decode_combine_dtype(const DecodeParams& p, int dtype, cudaStream_t stream) {
-  dim3 grid(p.S * p.Hq);
+  dim3 grid(static_cast<unsigned>((static_cast<int64_t>(p.S) * p.Hq + 3) / 4));
   switch (dtype) {
     case 0: decode_combine_kernel<float><<<grid, 128, 0, stream>>>(p); break;
     case 1: decode_combine_kernel<__half><<<grid, 128, 0, stream>>>(p); break;

@@ -136,6 +136,21 @@ def test_random_shapes_vs_oracle(cuda, hq, hkv, d, dtype):
                         f"{hq}/{hkv}/{d} {kernel} split={split}")
 
 
+@pytest.mark.parametrize("hq,hkv,d,dtype", [
+    (16, 8, 128, torch.bfloat16),   # combine with 16-byte column loads
+    (4, 2, 34, torch.float16),      # head_dim not a multiple of 4: one column per lane
+])
+def test_more_than_32_splits_vs_oracle(cuda, hq, hkv, d, dtype):
+    """One block per split: 2049 tokens give 33 partials per row, so the combine
+    walks its splits in more than one pass of 32."""
+    lens = [2049, 2200, 70, 1]
+    c = _random_case(hq * 3 + d, lens, hq, hkv, d, dtype)
+    want = _oracle(c)
+    for kernel in ("auto", "simt"):
+        _close_half(_run(c, kernel=kernel, split_blocks=1), want,
+                    f"{hq}/{hkv}/{d} {kernel} split=1")
+
+
 def test_positions_causal_and_block_mask(cuda):
     lens = [900, 300, 1300, 64]
     c = _random_case(5, lens, 16, 2, 128, torch.bfloat16)
