@@ -125,6 +125,8 @@ def test_config2_slice_scope_fp16_matches_reference(cuda, kernel):
     (32, 32, 128, torch.float16),   # MHA
     (16, 16, 64, torch.float16),
     (12, 6, 64, torch.bfloat16),    # KV heads not a multiple of 8
+    (8, 4, 128, torch.float16),     # 4 KV heads per CTA (one TMA box covers 4 heads)
+    (3, 1, 64, torch.bfloat16),     # one KV head, odd GQA group
 ])
 def test_random_shapes_vs_oracle(cuda, hq, hkv, d, dtype):
     lens = [1, 63, 64, 65, 700, 2049, 1500, 129]
