@@ -197,7 +197,7 @@ def run_reference(args):
 # GPU path
 # ---------------------------------------------------------------------------
 
-def _build_shard(torch, device, seed: int, n_seqs: int):
+def _build_shard(torch, device, seed: int, n_seqs: int, len_seed: int | None = None):
     import numpy as np
 
     from oracle import attention_oracle as ao  # RoPE table construction only
@@ -205,7 +205,7 @@ def _build_shard(torch, device, seed: int, n_seqs: int):
 
     W = WORKLOAD
     S, hq, hkv, d = n_seqs, W["q_heads"], W["kv_heads"], W["head_dim"]
-    lens = _lens(seed, S)
+    lens = _lens(seed if len_seed is None else len_seed, S)
     need = sum(-(-n // 64) for n in lens)
     pool = int(math.ceil(need * (1 + W["pool_headroom"])))
     bt = BlockTable(pool)
@@ -258,7 +258,10 @@ def run_ours(args):
 
     W = WORKLOAD
     S = args.seqs if args.seqs > 0 else W["seqs_per_gpu"]
-    sh = _build_shard(torch, device, seed=1234 + rank, n_seqs=S)
+    # Every rank draws the same context lengths (the equal-token shards that the Supervisor's
+    # LPT placement of whole sequences produces, to within one sequence) and its own block
+    # placement and K/V/Q values.
+    sh = _build_shard(torch, device, seed=1234 + rank, n_seqs=S, len_seed=1234)
     status = torch.zeros(1, dtype=torch.int32, device=device)
     call = DecodeCall(sh["pt"], sh["q"], sh["k"], sh["v"], sh["seq_lens"], sh["cos"], sh["sin"],
                       validate=True, split_blocks=args.split_blocks, kernel=args.kernel,
