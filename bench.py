@@ -8,10 +8,15 @@ one token for every sequence (split-K decode + combine).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-Under torchrun (N > 1) every rank holds its own 256-sequence shard (weak
-scaling); `value` is the sum over ranks, timed as the max over ranks.
-`--impl reference` times the CPU path (the numpy restatement of the
-reference's dense_reference, one query row per sequence) on this host's
+The batch is the Supervisor's: 256 sequences at every N (strong scaling).
+Under torchrun (N > 1) the Supervisor (rank 0) places whole sequences on the
+ranks by longest-processing-time on token count, and every step sends each
+rank its queries and metadata and gathers the output rows back over NCCL
+inside the timed region; time = max over ranks. The line also carries the
+weak-scaling figure (256 sequences per GPU, N > 1) and the chunked-prefill
+measurement (8 x 4096-token prompts in 512-token chunks per GPU) as
+sub-objects. `--impl reference` times the CPU path (the numpy restatement of
+the reference's dense_reference, one query row per sequence) on this host's
 cores, rank 0 only.
 """
 
@@ -182,8 +187,11 @@ def run_reference(args):
         "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": 1000.0 * secs / max(args.steps, 1), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": dict(WORKLOAD, parallelism=f"replicas{world}", l2_flush="inputs>L2"),
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": dict({k: x for k, x in WORKLOAD.items() if k != "seqs_per_gpu"},
+                       seqs=WORKLOAD["seqs_per_gpu"],
+                       parallelism="host cores of rank 0 (the reference path has no GPU "
+                                   "sharding)", l2_flush="inputs>L2"),
         "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port",
                          "sample": sample},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
@@ -242,32 +250,116 @@ def _cpu_baseline_leg():
                       "restatement of dense_reference, one thread per sequence"}
 
 
-def run_ours(args):
+def _init_dist(world: int, local: int, timeout_s: int = 120):
+    import datetime
+
     import torch
     import torch.distributed as dist
 
-    from src.kernels.block_attention import DecodeCall, block_attention_decode
-
-    world, rank, local = _dist_env()
     if world > 1:
         torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=120),
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=timeout_s),
                                 device_id=torch.device("cuda", local))
     device = torch.device("cuda", local if world > 1 else 0)
     torch.cuda.set_device(device)
+    return device
 
+
+def _supervisor_batch(n_seqs: int, world: int):
+    """The batch the Supervisor decodes: context lengths (seeded) and their
+    longest-processing-time placement over the ranks by token count."""
+    from src.serving import lpt_placement
+
+    lens = _lens(1234, n_seqs)
+    placement = lpt_placement(lens, [0] * world)
+    shards = [[i for i in range(n_seqs) if placement[i] == r] for r in range(world)]
+    return lens, placement, shards
+
+
+def _pool_blocks(lens) -> int:
+    need = sum(-(-n // 64) for n in lens)
+    return int(math.ceil(need * (1 + WORKLOAD["pool_headroom"])))
+
+
+def _shard_table(lens, seed: int):
+    """One rank's allocator, built by the Supervisor: every block allocated, freed in a
+    seeded shuffled order (scattered chains), then one chain per sequence."""
+    from src.block_table import BlockTable
+
+    pool = _pool_blocks(lens)
+    bt = BlockTable(pool)
+    ids = [bt.allocate_block() for _ in range(pool)]
+    random.Random(seed).shuffle(ids)
+    for i in ids:
+        bt.free_block(i)
+    heads = [bt.allocate_chain(-(-n // 64)) for n in lens]
+    width = max(-(-n // 64) for n in lens)
+    return bt, heads, bt.export_page_table(heads, width), width
+
+
+def _random_pool(torch, device, pool: int, seed: int):
     W = WORKLOAD
-    S = args.seqs if args.seqs > 0 else W["seqs_per_gpu"]
-    # Every rank draws the same context lengths (the equal-token shards that the Supervisor's
-    # LPT placement of whole sequences produces, to within one sequence) and its own block
-    # placement and K/V/Q values.
-    sh = _build_shard(torch, device, seed=1234 + rank, n_seqs=S, len_seed=1234)
+    g = torch.Generator(device=device).manual_seed(seed)
+    k = torch.empty((pool, W["kv_heads"], 64, W["head_dim"]), dtype=torch.bfloat16, device=device)
+    v = torch.empty_like(k)
+    for lo in range(0, pool, 4096):
+        hi = min(pool, lo + 4096)
+        k[lo:hi] = torch.randn((hi - lo,) + tuple(k.shape[1:]), generator=g, device=device) * 0.5
+        v[lo:hi] = torch.randn((hi - lo,) + tuple(k.shape[1:]), generator=g, device=device) * 0.5
+    return k, v
+
+
+def run_ours(args):
+    """The headline line: GQA paged decode of one 256-sequence batch owned by the Supervisor.
+
+    The Supervisor (rank 0) places the batch's whole sequences on the N ranks by
+    longest-processing-time on token count and owns every rank's allocator; rank r
+    holds its pool's K/V. A step is the Supervisor's decode of the batch: permute the
+    queries into shard order, send each rank its queries and metadata (lengths and
+    page-table rows), decode every shard, gather the rows back and restore the batch
+    order (src.dist.DecodeShards), all inside the timed region. N = 1 runs the same
+    step with no collective. Strong scaling: the batch is 256 sequences at every N.
+    """
+    import torch
+    import torch.distributed as dist
+
+    from oracle import attention_oracle as ao  # RoPE table construction only
+    from src.dist import DecodeShards
+    from src.kernels.block_attention import DecodeCall, validate_page_table
+
+    world, rank, local = _dist_env()
+    device = _init_dist(world, local)
+    W = WORKLOAD
+    S, hq, hkv, d = (args.seqs if args.seqs > 0 else W["seqs_per_gpu"]), W["q_heads"], \
+        W["kv_heads"], W["head_dim"]
+    lens, placement, shards = _supervisor_batch(S, world)
+    my_lens = [lens[i] for i in shards[rank]]
+    tables = None
+    if rank == 0:  # the Supervisor's allocators, one per rank's pool
+        tables = [_shard_table([lens[i] for i in shards[r]], 1234 + r) for r in range(world)]
+    sh = DecodeShards(world, rank, device, q_heads=hq, head_dim=d, dtype=torch.bfloat16,
+                      placement=placement if rank == 0 else None,
+                      widths=[t[3] for t in tables] if rank == 0 else None)
+    if sh.n != len(my_lens):
+        raise RuntimeError(f"rank {rank}: shard size {sh.n} != placement {len(my_lens)}")
+    if rank == 0:
+        sh.set_meta([[lens[i] for i in shards[r]] for r in range(world)],
+                    [torch.from_numpy(t[2]) for t in tables])
+    pool = _pool_blocks(my_lens)
+    k, v = _random_pool(torch, device, pool, 1234 + rank)
+    max_b = -(-W["ctx_max"] // 64)
+    cos_np, sin_np = ao.rope_tables(max_b * 64, d, W["rope_base"])
+    cos, sin = torch.from_numpy(cos_np).to(device), torch.from_numpy(sin_np).to(device)
+    q_batch = None
+    if rank == 0:
+        g = torch.Generator(device=device).manual_seed(99)
+        q_batch = (torch.randn((S, hq, d), generator=g, device=device) * 0.5).to(torch.bfloat16)
     status = torch.zeros(1, dtype=torch.int32, device=device)
-    call = DecodeCall(sh["pt"], sh["q"], sh["k"], sh["v"], sh["seq_lens"], sh["cos"], sh["sin"],
-                      validate=True, split_blocks=args.split_blocks, kernel=args.kernel,
-                      status=status)
+    my_blocks = sum(-(-n // 64) for n in my_lens)
+    call = DecodeCall(sh.page_table, sh.q, k, v, sh.seq_lens, cos, sin, out=sh.out,
+                      validate=False, split_blocks=args.split_blocks, kernel=args.kernel,
+                      status=status, total_blocks=my_blocks, max_seq_blocks=sh.width)
     plan = call.plan
-    kv_bytes = sum(sh["lens"]) * W["kv_heads"] * W["head_dim"] * 2 * 2
     stream = torch.cuda.current_stream(device)
 
     def barrier():
@@ -275,141 +367,272 @@ def run_ours(args):
             dist.barrier()
         torch.cuda.synchronize(device)
 
+    sh.step(call.launch, q_batch)  # first step: the metadata has arrived, check it
+    validate_page_table(sh.page_table, sh.seq_lens, pool)
     for _ in range(max(args.warmup, 3)):
-        call.launch()
+        sh.step(call.launch, q_batch)
     barrier()
+    n_ev = args.steps
+    k0 = [torch.cuda.Event(enable_timing=True) for _ in range(n_ev)]
+    k1 = [torch.cuda.Event(enable_timing=True) for _ in range(n_ev)]
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(device.index if world == 1 else local) as clk:
+
+    def launch_timed(i):
+        def run():
+            k0[i].record(stream)
+            call.launch()
+            k1[i].record(stream)
+        return run
+
+    with ClockSampler(device.index) as clk:
         barrier()
         start.record(stream)
-        for _ in range(args.steps):
-            call.launch()
+        for i in range(args.steps):
+            sh.step(launch_timed(i), q_batch)
         stop.record(stream)
         barrier()
     ms = start.elapsed_time(stop)
-    t = torch.tensor([ms], dtype=torch.float64, device=device)
+    kern_ms = sum(a.elapsed_time(b) for a, b in zip(k0, k1)) / args.steps
+    t = torch.tensor([ms, kern_ms], dtype=torch.float64, device=device)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms_max = float(t.item())
+    ms_max, kern_max = float(t[0]), float(t[1])
     step_ms = ms_max / args.steps
-    value = world * S * args.steps / (ms_max / 1000.0)
-    achieved = kv_bytes / (ms / args.steps / 1000.0) / 1e9  # this rank's kernel, GB/s
+    value = S * args.steps / (ms_max / 1000.0)
+    kv_bytes_all = sum(lens) * hkv * d * 2 * 2
+    kv_bytes_mine = sum(my_lens) * hkv * d * 2 * 2
+    # this rank's decode kernels (decode + combine) per launch, timed inside the region
+    achieved_mine = kv_bytes_mine / (kern_ms / 1000.0) / 1e9
 
-    # correctness guard on the measured configuration: a few rows vs the oracle
-    check = _spot_check(torch, sh, call.out) if rank == 0 else None
-    kernel_status = int(status.item())  # nonzero: a bounded wait gave up or a bad entry
-    if check is not None:
-        check["kernel_status"] = kernel_status
-    if kernel_status != 0:
-        print(f"rank {rank}: decode kernels reported status {kernel_status}", file=sys.stderr)
-
-    # e2e through the public API with host buffers: q, page table and lengths copied in
-    # from pinned memory and the output read back, every step. Uploads and read-backs run
-    # on two streams of their own (one per copy direction) with two buffer sets, so step
-    # i + 1's inputs travel while step i decodes and step i's output travels while step
-    # i + 1 decodes; events order each buffer's reuse.
-    q_host = sh["q"].cpu().pin_memory()
-    pt_host = torch.from_numpy(sh["pt_host"]).pin_memory()
-    lens_host = torch.tensor(sh["lens"], dtype=torch.int32).pin_memory()
-    out_host = [torch.empty((S, W["q_heads"], W["head_dim"]), dtype=torch.bfloat16).pin_memory()
-                for _ in range(2)]
-    ins = [tuple(torch.empty_like(x, device=device) for x in (q_host, pt_host, lens_host))
-           for _ in range(2)]
-    outs = [torch.empty_like(out_host[0], device=device) for _ in range(2)]
-    gathered = ([[torch.empty_like(outs[0]) for _ in range(world)] for _ in range(2)]
-                if world > 1 and rank == 0 else [None, None])
-    h2d = sum(x.numel() * x.element_size() for x in (q_host, pt_host, lens_host))
-    d2h = out_host[0].numel() * out_host[0].element_size() * (world if rank == 0 else 1)
-    copy_stream = torch.cuda.Stream(device)  # uploads
-    back_stream = torch.cuda.Stream(device)  # read-backs
-    h2d_done = [torch.cuda.Event() for _ in range(2)]
-    compute_done = [torch.cuda.Event() for _ in range(2)]
-    d2h_done = [torch.cuda.Event() for _ in range(2)]
-    used = [False, False]
-    # the public API for a repeated decode: one prepared call per buffer set, launched each step
-    calls = [DecodeCall(pt_dev, q_dev, sh["k"], sh["v"], lens_dev, sh["cos"], sh["sin"],
-                        out=outs[b], workspace=call.workspace, validate=False,
-                        split_blocks=plan["split_blocks"], kernel=args.kernel)
-             for b, (q_dev, pt_dev, lens_dev) in enumerate(ins)]
-
-    def e2e_step(i):
-        b = i & 1
-        q_dev, pt_dev, lens_dev = ins[b]
-        with torch.cuda.stream(copy_stream):
-            if used[b]:
-                copy_stream.wait_event(compute_done[b])  # step i - 2 is done reading buffer b
-            q_dev.copy_(q_host, non_blocking=True)
-            pt_dev.copy_(pt_host, non_blocking=True)
-            lens_dev.copy_(lens_host, non_blocking=True)
-            h2d_done[b].record(copy_stream)
-        stream.wait_event(h2d_done[b])
-        if used[b]:
-            stream.wait_event(d2h_done[b])  # step i - 2's output has left outs[b]
-        calls[b].launch()
-        if world > 1:  # the Supervisor (rank 0) gathers every shard's rows over NCCL
-            dist.gather(outs[b], gathered[b], dst=0)
-        compute_done[b].record(stream)
-        with torch.cuda.stream(back_stream):
-            back_stream.wait_event(compute_done[b])
-            if world > 1:
-                if rank == 0:
-                    for gbuf in gathered[b]:
-                        out_host[b].copy_(gbuf, non_blocking=True)
-            else:
-                out_host[b].copy_(outs[b], non_blocking=True)
-            d2h_done[b].record(back_stream)
-        used[b] = True
-
-    for i in range(3):
-        e2e_step(i)
-    torch.cuda.synchronize(device)
-    barrier()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e2e_steps = max(5, min(args.steps, 20))
-    e0.record(stream)
-    copy_stream.wait_event(e0)  # the first input copy starts inside the timed region
-    for i in range(e2e_steps):
-        e2e_step(i)
-    stream.wait_stream(back_stream)  # the last read-back is inside the timed region
-    e1.record(stream)
-    barrier()
-    torch.cuda.synchronize(device)
-    te = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=device)
+    # every rank's kernel status and decode rate, to the Supervisor
+    st_all = [torch.zeros(2, dtype=torch.float64, device=device) for _ in range(world)]
+    mine_t = torch.tensor([float(status.item()), achieved_mine], dtype=torch.float64,
+                          device=device)
     if world > 1:
-        dist.all_reduce(te, op=dist.ReduceOp.MAX)
-    e2e_value = world * S * e2e_steps / (float(te.item()) / 1000.0)
+        dist.all_gather(st_all, mine_t)
+    else:
+        st_all = [mine_t]
+    statuses = [int(x[0]) for x in st_all]
+    rates = [float(x[1]) for x in st_all]
+    check = _check_gathered_rows(torch, dist, sh, world, rank, lens, shards, tables, k, v,
+                                 cos_np, sin_np, q_batch)
+    if rank == 0:
+        check["kernel_status"] = statuses
+    if any(statuses):
+        print(f"rank {rank}: decode kernels reported status {statuses}", file=sys.stderr)
 
+    e2e = _e2e_sharded(torch, dist, sh, call, world, rank, device, q_batch, args)
+    weak = _weak_scaling_leg(torch, dist, world, rank, device, args) if world > 1 else None
+    pre = _prefill_leg(args, world, rank, device) if not args.no_prefill else None
     cpu = _cpu_baseline_leg() if (rank == 0 and world == 1 and not args.no_cpu) else None
     peak, peak_kind = _peaks()
     launches = args.steps * (1 + (1 if plan["max_splits"] > 1 else 0))
     if rank == 0:
+        avg_rate = kv_bytes_all / world / (kern_max / 1000.0) / 1e9
         line = {
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_ms,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (seeded; random-init K/V/Q, no dataset)",
-            "config": dict(WORKLOAD, seqs_per_gpu=S,
-                           parallelism=f"dp{world} (whole-sequence shards)",
-                           l2_flush="inputs>L2 (K+V %.1f GB per GPU)" % (kv_bytes / 1e9),
+            "config": dict({k: x for k, x in WORKLOAD.items() if k != "seqs_per_gpu"}, seqs=S,
+                           parallelism=(f"dp{world}: the Supervisor (rank 0) places whole "
+                                        "sequences by LPT on tokens; queries, lengths and "
+                                        "page-table rows go out and outputs come back over "
+                                        "NCCL inside every step" if world > 1 else
+                                        "dp1 (the Supervisor's batch on one GPU)"),
+                           shard_sizes=sh.counts,
+                           shard_tokens=[sum(lens[i] for i in shards[r]) for r in range(world)],
+                           l2_flush="inputs>L2 (K+V %.1f GB per GPU)" % (kv_bytes_all / world / 1e9),
                            split_blocks=plan["split_blocks"], max_splits=plan["max_splits"],
                            kernel="tensor_cores" if plan["tensor_cores"] else "cuda_cores"),
-            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                         "frac": achieved / peak, "traffic": _traffic_from_profile(),
+            "roofline": {"bound": "hbm", "achieved": avg_rate, "peak": peak, "unit": "GB/s",
+                         "frac": avg_rate / peak, "traffic": _traffic_from_profile(world),
                          "peak_source": peak_kind,
-                         "algorithmic_bytes_per_launch": kv_bytes,
-                         "note": "decode + combine per step, K+V bytes once per KV head"},
+                         "algorithmic_bytes_per_launch": kv_bytes_all // world,
+                         "per_rank_GB/s": rates,
+                         "note": "decode + combine launches timed with CUDA events inside the "
+                                 "timed region; K+V bytes once per KV head; achieved = the "
+                                 "batch's bytes / N over the slowest rank's kernel time"},
+            "step_breakdown_ms": {"decode_kernels_max_rank": kern_max,
+                                  "step": step_ms,
+                                  "outside_kernels": step_ms - kern_max},
             "cpu_baseline": cpu,
-            "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": h2d,
-                    "d2h_bytes_per_step": d2h, "steps": e2e_steps},
+            "e2e": e2e,
             "gpu_launches": launches,
             "clocks": clk.summary(),
             "check": check,
         }
+        if weak is not None:
+            line["weak_scaling"] = weak
+        if pre is not None:
+            line["prefill"] = pre
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
     return 0
+
+
+def _check_gathered_rows(torch, dist, sh, world, rank, lens, shards, tables, k, v, cos_np,
+                         sin_np, q_batch):
+    """The Supervisor checks rows it gathered from EVERY rank against the oracle.
+
+    Per rank the two shortest sequences are checked: the rank sends the K/V blocks of
+    their chains (in chain order) to rank 0, which recomputes those rows with the numpy
+    oracle and compares them with the rows of the last gathered step.
+    """
+    import numpy as np
+
+    from oracle import attention_oracle as ao
+
+    picks = [sorted(range(len(shards[r])), key=lambda j: (lens[shards[r][j]], j))[:2]
+             for r in range(world)]
+    blocks = [[-(-lens[shards[r][j]] // 64) for j in picks[r]] for r in range(world)]
+    mine = picks[rank]
+    pt = sh.page_table[mine].cpu().numpy()
+    ids = [int(pt[i, b]) for i in range(len(mine)) for b in range(blocks[rank][i])]
+    sel = torch.tensor(ids, dtype=torch.int64, device=k.device)
+    kb, vb = k.index_select(0, sel).contiguous(), v.index_select(0, sel).contiguous()
+    res = None
+    if rank == 0:
+        errs = []
+        got_all = sh.out_batch.float().cpu().numpy()  # the last timed step's gathered rows
+        for r in range(world):
+            nb = sum(blocks[r])
+            if r == 0:
+                kr, vr = kb, vb
+            else:
+                kr = torch.empty((nb,) + tuple(k.shape[1:]), dtype=k.dtype, device=k.device)
+                vr = torch.empty_like(kr)
+                dist.recv(kr, src=r)
+                dist.recv(vr, src=r)
+            kn, vn = kr.float().cpu().numpy(), vr.float().cpu().numpy()
+            off = 0
+            for j, nbj in zip(picks[r], blocks[r]):
+                b = shards[r][j]
+                ptj = np.full((1, nbj), -1, np.int32)
+                ptj[0, :] = np.arange(off, off + nbj, dtype=np.int32)
+                q = q_batch[b:b + 1].float().cpu().numpy()
+                want = ao.decode_attention(ptj, q, kn, vn, [lens[b]], cos_np, sin_np)
+                e = np.abs(got_all[b:b + 1] - want)
+                errs.append((r, b, float(e.max()), float(e.mean())))
+                off += nbj
+        mx = max(e[2] for e in errs)
+        mean = float(np.mean([e[3] for e in errs]))
+        res = {"rows": len(errs), "per_rank_rows": [list(p) for p in picks],
+               "max_abs": mx, "mean_abs": mean,
+               "per_rank_max_abs": [max(e[2] for e in errs if e[0] == r) for r in range(world)],
+               "tolerance": {"max_abs": 2e-2, "mean_abs": 2e-3},
+               "ok": bool(mx <= 2e-2 and mean <= 2e-3)}
+    else:
+        dist.send(kb, dst=0)
+        dist.send(vb, dst=0)
+    torch.cuda.synchronize(k.device)
+    return res
+
+
+def _e2e_sharded(torch, dist, sh, call, world, rank, device, q_batch, args):
+    """The same step through the public API from host buffers: every step rank 0 uploads the
+    batch's queries and the Supervisor's metadata (every shard's lengths and page-table rows)
+    from pinned memory and reads the batch's output rows back. Two buffer sets and one
+    stream per copy direction, so uploads and read-backs overlap neighbouring steps."""
+    stream = torch.cuda.current_stream(device)
+    steps = max(5, min(args.steps, 20))
+    h2d = d2h = 0
+    if rank == 0:
+        q_host = q_batch.cpu().pin_memory()
+        meta_host = sh.meta_all.cpu().pin_memory()
+        out_host = [torch.empty_like(q_host).pin_memory() for _ in range(2)]
+        ins = [(torch.empty_like(q_batch), torch.empty_like(sh.meta_all)) for _ in range(2)]
+        outs = [torch.empty_like(q_batch) for _ in range(2)]
+        h2d = q_host.numel() * q_host.element_size() + meta_host.numel() * 4
+        d2h = out_host[0].numel() * out_host[0].element_size()
+        up, back = torch.cuda.Stream(device), torch.cuda.Stream(device)
+        h2d_done = [torch.cuda.Event() for _ in range(2)]
+        used_done = [torch.cuda.Event() for _ in range(2)]
+        d2h_done = [torch.cuda.Event() for _ in range(2)]
+        used = [False, False]
+
+    def step(i):
+        if rank != 0:
+            sh.step(call.launch)
+            return
+        b = i & 1
+        qd, md = ins[b]
+        with torch.cuda.stream(up):
+            if used[b]:
+                up.wait_event(used_done[b])  # step i - 2 has consumed buffer set b
+            qd.copy_(q_host, non_blocking=True)
+            md.copy_(meta_host, non_blocking=True)
+            h2d_done[b].record(up)
+        stream.wait_event(h2d_done[b])
+        if used[b]:
+            stream.wait_event(d2h_done[b])  # step i - 2's rows have left outs[b]
+        sh.meta_all.copy_(md, non_blocking=True)
+        sh.step(call.launch, qd, out=outs[b])
+        used_done[b].record(stream)
+        with torch.cuda.stream(back):
+            back.wait_event(used_done[b])
+            out_host[b].copy_(outs[b], non_blocking=True)
+            d2h_done[b].record(back)
+        used[b] = True
+
+    for i in range(3):
+        step(i)
+    torch.cuda.synchronize(device)
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    if rank == 0:
+        up.wait_event(e0)  # the first upload starts inside the timed region
+    for i in range(steps):
+        step(i)
+    if rank == 0:
+        stream.wait_stream(back)  # the last read-back is inside the timed region
+    e1.record(stream)
+    torch.cuda.synchronize(device)
+    if world > 1:
+        dist.barrier()
+    te = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=device)
+    if world > 1:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    return {"value": sum(sh.counts) * steps / (float(te.item()) / 1000.0), "unit": "tokens/s",
+            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "steps": steps}
+
+
+def _weak_scaling_leg(torch, dist, world, rank, device, args):
+    """Secondary figure under torchrun: every rank decodes its own 256-sequence batch
+    (same lengths on every rank, its own placement and values), no collective in the
+    timed loop; value = all ranks' sequences per step / the slowest rank's time."""
+    from src.kernels.block_attention import DecodeCall
+
+    W = WORKLOAD
+    shd = _build_shard(torch, device, seed=1234 + rank, n_seqs=W["seqs_per_gpu"], len_seed=1234)
+    call = DecodeCall(shd["pt"], shd["q"], shd["k"], shd["v"], shd["seq_lens"], shd["cos"],
+                      shd["sin"], validate=True, split_blocks=args.split_blocks,
+                      kernel=args.kernel, total_blocks=sum(-(-n // 64) for n in shd["lens"]),
+                      max_seq_blocks=shd["pt"].shape[1])
+    for _ in range(3):
+        call.launch()
+    torch.cuda.synchronize(device)
+    dist.barrier()
+    s = torch.cuda.current_stream(device)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(s)
+    for _ in range(args.steps):
+        call.launch()
+    e1.record(s)
+    torch.cuda.synchronize(device)
+    t = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    del shd, call
+    torch.cuda.empty_cache()
+    return {"seqs_per_gpu": W["seqs_per_gpu"], "scaling": "weak",
+            "value": world * W["seqs_per_gpu"] * args.steps / (ms / 1000.0), "unit": "tokens/s",
+            "ms_per_step": ms / args.steps,
+            "note": "every rank its own 256-sequence batch; no collective in the timed loop"}
 
 
 def _spot_check(torch, sh, out):
@@ -434,12 +657,15 @@ def _spot_check(torch, sh, out):
     return {"rows": len(idx), "max_abs": float(err.max()), "mean_abs": float(err.mean())}
 
 
-def _traffic_from_profile():
-    """DRAM bytes per launch recorded from the ncu capture of this workload, if any."""
+def _traffic_from_profile(world: int = 1):
+    """DRAM bytes per decode launch on one rank, from the ncu capture of this workload
+    (recorded for the 256-sequence batch on one GPU; a rank's launch reads 1/N of it, as
+    its K+V bytes are 1/N of the batch's)."""
     p = ROOT / "profiles" / "decode_config3_traffic.json"
     if p.exists():
         try:
-            return json.loads(p.read_text()).get("dram_bytes_per_launch")
+            b = json.loads(p.read_text()).get("dram_bytes_per_launch")
+            return None if b is None else int(b / world)
         except (ValueError, OSError):
             return None
     return None
@@ -450,13 +676,13 @@ PREFILL = dict(workload="chunked_prefill_llama3_8b_attention", prompts=8, prompt
                causal=True)
 
 
-def run_prefill(args):
+def _prefill_measure(args, world: int, rank: int, device):
     """Chunked prefill: every 512-token chunk of 8 x 4096-token prompts, causal, GQA 32/8.
 
     A step is one full pass (8 chunk launches, each over all 8 prompts) with the prompts' K/V
     already resident in the paged cache; FLOPs = 4 * D * Hq * sum_p sum_i (i + 1). Under
     torchrun every rank prefills its own 8 prompts on its GPU (whole prompts shard, no
-    collective in the data path): weak scaling, time = max over ranks.
+    collective in the data path): weak scaling, time = max over ranks. Returns the line.
     """
     import torch
     import torch.distributed as dist
@@ -466,13 +692,6 @@ def run_prefill(args):
     from src.kernels.block_attention import PrefillCall
 
     P = PREFILL
-    world, rank, local = _dist_env()
-    if world > 1:
-        torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=120),
-                                device_id=torch.device("cuda", local))
-    device = torch.device("cuda", local if world > 1 else 0)
-    torch.cuda.set_device(device)
     S, T, C = P["prompts"], P["prompt_len"], P["chunk"]
     hq, hkv, d = P["q_heads"], P["kv_heads"], P["head_dim"]
     nbp = T // 64
@@ -505,6 +724,7 @@ def run_prefill(args):
                                  krot_valid=torch.full((S,), c * C, dtype=torch.int32)))
         workspace = calls[-1].workspace
     flops = 4.0 * d * hq * S * (T * (T + 1) / 2.0)
+    steps = args.prefill_steps if args.prefill_steps > 0 else args.steps
     for _ in range(max(args.warmup, 3)):
         for cl in calls:
             cl.launch()
@@ -516,20 +736,19 @@ def run_prefill(args):
             dist.barrier()
         torch.cuda.synchronize()
         e0.record(stream)
-        for _ in range(args.steps):
+        for _ in range(steps):
             for cl in calls:
                 cl.launch()
         e1.record(stream)
         torch.cuda.synchronize()
         if world > 1:
             dist.barrier()
-    ms = e0.elapsed_time(e1) / args.steps
+    ms = e0.elapsed_time(e1) / steps
     if world > 1:  # the job's step time is the slowest rank's
         t = torch.tensor([ms], dtype=torch.float64, device=device)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
-    flops *= world
-    tflops = flops / (ms / 1000.0) / 1e12
+    tflops = flops * world / (ms / 1000.0) / 1e12
     peak = None
     pk = ROOT / "MEASURED_PEAKS.json"
     if pk.exists():
@@ -541,22 +760,45 @@ def run_prefill(args):
     got = calls[-1].out[:2, :1].float().cpu().numpy()
     err = abs(got - want)
     per_gpu = tflops / world
-    line = {
+    kernel_status = int(status.item())
+    del calls, workspace, k, v, q
+    torch.cuda.empty_cache()
+    return {
         "metric": "chunked-prefill attn TFLOP/s (causal, bf16)", "value": tflops,
-        "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "unit": "TFLOP/s", "n_gpus": world, "steps": steps, "warmup": args.warmup,
         "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "dtype": "bf16",
         "data": "synthetic",
-        "config": dict(P, prompts_per_gpu=S, chunk_launches=len(calls),
+        "config": dict(P, prompts_per_gpu=S, chunk_launches=T // C,
                        parallelism=f"dp{world} (whole prompts per GPU)",
                        rotated_keys="one workspace per prefill; each key rotated once (krot_valid)"),
         "tokens_per_s": world * S * T / (ms / 1000.0),
         "roofline": {"bound": "tensor", "achieved": per_gpu, "peak": peak, "unit": "TFLOP/s",
                      "frac": (per_gpu / peak) if peak else None,
-                     "algorithmic_flops_per_step_per_gpu": flops / world},
+                     "peak_source": "measured (bf16_tflops, burst)" if peak else None,
+                     "algorithmic_flops_per_step_per_gpu": flops},
+        "gpu_launches": steps * (T // C),
         "check": {"max_abs": float(err.max()), "mean_abs": float(err.mean()),
-                  "kernel_status": int(status.item())},
+                  "tolerance": {"max_abs": 2e-2, "mean_abs": 2e-3},
+                  "ok": bool(err.max() <= 2e-2 and err.mean() <= 2e-3),
+                  "kernel_status": kernel_status},
         "clocks": clk.summary(),
     }
+
+
+def _prefill_leg(args, world: int, rank: int, device):
+    """The chunked-prefill measurement as a sub-object of the headline line."""
+    line = _prefill_measure(args, world, rank, device)
+    return {k: line[k] for k in ("metric", "value", "unit", "ms_per_step", "steps", "scaling",
+                                 "tokens_per_s", "roofline", "gpu_launches", "check", "clocks",
+                                 "config")}
+
+
+def run_prefill(args):
+    import torch.distributed as dist
+
+    world, rank, local = _dist_env()
+    device = _init_dist(world, local)
+    line = _prefill_measure(args, world, rank, device)
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:
@@ -772,6 +1014,10 @@ def main() -> int:
     ap.add_argument("--split-blocks", type=int, default=0)
     ap.add_argument("--kernel", default="auto", choices=["auto", "tc", "simt"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
+    ap.add_argument("--no-prefill", action="store_true",
+                    help="skip the chunked-prefill sub-object of the decode line")
+    ap.add_argument("--prefill-steps", type=int, default=0,
+                    help="timed prefill passes (default: --steps)")
     ap.add_argument("--workload", choices=["decode", "prefill", "serving", "decode-scoped"],
                     default="decode",
                     help="decode (the headline metric), the chunked-prefill tensor-core pass, "

@@ -140,7 +140,8 @@ typedef struct ouro_decode_args {
   void* out;                  /* [S, Hq, D], dtype */
   void* workspace;            /* split-K partials, >= ouro_decode_plan's bytes, 16-B aligned */
   size_t workspace_bytes;
-  int32_t* status;            /* optional device int32: bit 1 bad page entry,
+  int32_t* status;            /* optional device int32: bit 1 bad page entry or a
+                                 sequence longer than its row (max_blocks, max_seq_blocks),
                                  bit 2 wait timeout, bit 4 position outside the tables */
   int32_t num_seqs, num_q_heads, num_kv_heads, head_dim;
   int32_t max_blocks, num_phys_blocks, max_positions;
@@ -149,6 +150,15 @@ typedef struct ouro_decode_args {
   int32_t causal;             /* 1: keys j <= positions[s] only */
   int32_t kernel;             /* 0 auto, 1 CUDA cores, 2 tensor cores */
   float softmax_scale;        /* <= 0: 1/sqrt(D) */
+  /* Optional host-side sizes of the batch, for the split-K plan (0 = unknown).
+   * total_blocks: sum over sequences of ceil(keys / 64); the planner sizes the
+   *   chunks from it (unknown: num_seqs * the longest row).
+   * max_seq_blocks: no sequence has more than max_seq_blocks * 64 keys; bounds
+   *   the chunks per sequence and so the workspace (unknown: max_blocks).
+   *   Keys beyond it are not read and set status bit 1, as keys beyond the
+   *   page-table row do. */
+  int64_t total_blocks;
+  int32_t max_seq_blocks;
 } ouro_decode_args;
 
 /* Split-K plan for these arguments: blocks per chunk, chunks per sequence

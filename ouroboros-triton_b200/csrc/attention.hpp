@@ -30,6 +30,7 @@ struct DecodeParams {
   int32_t* status;            // optional device status word (kStatus* bits)
   int32_t S, Hq, Hkv, D, G;
   int32_t max_blocks, n_phys, max_pos;
+  int32_t blocks_cap;         // keys read per sequence <= blocks_cap * 64 (<= max_blocks * 64)
   int32_t split_blocks, max_splits;
   int32_t causal;
   float scale_log2;           // softmax_scale * log2(e)
@@ -42,12 +43,23 @@ struct SeqGeom {
   int32_t nsplit;  // split-K chunks
 };
 
+// Keys are clamped to blocks_cap * 64 tokens (the page-table row, or the
+// caller's smaller bound on any sequence's blocks), so a kernel never reads past
+// the row and a sequence never has more than max_splits chunks; a device caller
+// reports a longer sequence as a bad page entry (status bit 1).
 __host__ __device__ inline SeqGeom seq_geom(const DecodeParams& p, int s) {
   SeqGeom g;
   const int32_t len = p.seq_lens[s];
   g.pos = p.positions ? p.positions[s] : len - 1;
   int32_t kv = len;
   if (p.causal && g.pos + 1 < kv) kv = g.pos + 1;
+  const int64_t row_tokens = static_cast<int64_t>(p.blocks_cap) * kBlock;
+  if (kv > row_tokens) {
+    kv = static_cast<int32_t>(row_tokens);
+#ifdef __CUDA_ARCH__
+    if (p.status) atomicOr(p.status, 1);  // kStatusBadPageEntry
+#endif
+  }
   g.kv_len = kv > 0 ? kv : 0;
   g.nb = (g.kv_len + kBlock - 1) / kBlock;
   g.nsplit = (g.nb + p.split_blocks - 1) / p.split_blocks;

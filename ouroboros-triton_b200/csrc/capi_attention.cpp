@@ -42,6 +42,10 @@ int num_sms() {
   return n > 0 ? n : 148;
 }
 
+// Split-K planning: CTAs per SM the planner aims for, and the smallest chunk.
+constexpr int kSplitWaves = 12;
+constexpr int kMinSplitBlocks = 4;
+
 int hpc_of(int hkv) {
   for (int h : {8, 4, 2, 1})
     if (hkv % h == 0) return h;
@@ -95,17 +99,25 @@ ouro::DecodeParams to_params(const ouro_decode_args* a) {
                   !p.out))
     fail(OURO_EINVAL, "null tensor pointer in decode args");
   if (p.scope_tags && p.scope_stride < 1) fail(OURO_EINVAL, "scope_stride must be >= 1");
+  if (a->max_seq_blocks < 0 || a->total_blocks < 0)
+    fail(OURO_EINVAL, "max_seq_blocks and total_blocks must be >= 0 (0 = unknown)");
+  p.blocks_cap = a->max_seq_blocks > 0 ? std::min(a->max_seq_blocks, p.max_blocks) : p.max_blocks;
   return p;
 }
 
-int choose_split(const ouro::DecodeParams& p, bool tc, int waves) {
+// Blocks per split-K chunk: the batch's (block, KV-head group) work spread over
+// `waves` CTAs per SM. The work is the caller's total_blocks when given, else
+// every row counted as long as the longest allowed one.
+int choose_split(const ouro::DecodeParams& p, int64_t total_blocks, bool tc, int waves) {
   const int hpc = tc ? hpc_of(p.Hkv) : 1;
   const int64_t groups = tc ? p.Hkv / hpc : static_cast<int64_t>(p.Hkv) * ((p.G + 7) / 8);
-  const int64_t work = static_cast<int64_t>(p.S) * groups * std::max(p.max_blocks, 1);
+  const int64_t blocks = total_blocks > 0 ? total_blocks
+                                          : static_cast<int64_t>(p.S) * std::max(p.blocks_cap, 1);
+  const int64_t work = blocks * groups;
   const int64_t target = static_cast<int64_t>(num_sms()) * std::max(waves, 1);
   int64_t split = (work + target - 1) / std::max<int64_t>(target, 1);
-  split = std::max<int64_t>(split, 4);
-  split = std::min<int64_t>(split, std::max(p.max_blocks, 1));
+  split = std::max<int64_t>(split, kMinSplitBlocks);
+  split = std::min<int64_t>(split, std::max(p.blocks_cap, 1));
   split = std::min<int64_t>(split, 1024);
   return static_cast<int>(std::max<int64_t>(split, 1));
 }
@@ -127,11 +139,12 @@ void plan(ouro::DecodeParams& p, const ouro_decode_args* a, bool* use_tc, size_t
   } else if (a->kernel != 1) {
     fail(OURO_EINVAL, "kernel selector must be 0 (auto), 1 (cuda cores) or 2 (tensor cores)");
   }
-  int split = a->split_blocks > 0 ? a->split_blocks : choose_split(p, tc, 20);
-  split = std::min(split, std::max(p.max_blocks, 1));
+  int split = a->split_blocks > 0 ? a->split_blocks
+                                  : choose_split(p, a->total_blocks, tc, kSplitWaves);
+  split = std::min(split, std::max(p.blocks_cap, 1));
   if (tc) split = std::min(split, 512);  // block list lives in shared memory
   p.split_blocks = split;
-  p.max_splits = std::max(1, (p.max_blocks + split - 1) / split);
+  p.max_splits = std::max(1, (p.blocks_cap + split - 1) / split);
   *use_tc = tc;
   *ws_bytes = p.max_splits > 1
                   ? static_cast<size_t>(p.S) * p.Hq * p.max_splits * (p.D + 2) * sizeof(float)

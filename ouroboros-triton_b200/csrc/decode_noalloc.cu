@@ -20,7 +20,10 @@
 //     every partial the combine step reads is written earlier in the same call.
 //   * The device address of the array is looked up with cudaGetSymbolAddress
 //     on the first call on each device (with that device current) and cached.
-//     Make that first call before any stream capture begins.
+//     Make that first call before any stream capture begins. The cached
+//     address belongs to the device's current context: after cudaDeviceReset
+//     (or anything else that destroys that context) it is stale, so a process
+//     that resets a device must not call this entry point on it again.
 //   * No cudaMalloc, cudaFree or allocating library routine is called.
 #include <cuda_runtime.h>
 
@@ -79,9 +82,16 @@ extern "C" int ouro_paged_decode_noalloc(const ouro_decode_args* args, void* str
       const size_t per_split =
           static_cast<size_t>(p.S) * p.Hq * (p.D + 2) * sizeof(float);
       const int fit = static_cast<int>(kScratchBytes / per_split);
-      a.split_blocks = fit >= 2 ? (p.max_blocks + fit - 1) / fit : std::max(p.max_blocks, 1);
+      a.split_blocks = fit >= 2 ? (p.blocks_cap + fit - 1) / fit : std::max(p.blocks_cap, 1);
       p = ouro::capi::decode_params(&a);
       ouro::capi::decode_plan(p, &a, &tc, &ws);
+      if (ws > kScratchBytes && tc && args->kernel == 0) {
+        // The tensor-core kernel caps a chunk at 512 blocks, which can leave
+        // more chunks than fit; the CUDA-core kernel takes chunks of any size.
+        a.kernel = 1;
+        p = ouro::capi::decode_params(&a);
+        ouro::capi::decode_plan(p, &a, &tc, &ws);
+      }
       if (ws > kScratchBytes) fail(OURO_EINVAL, "decode does not fit the static scratch");
     }
     if (p.S == 0) return OURO_OK;

@@ -13,6 +13,11 @@ stateless worker. Per step:
 Every rank takes the same collective calls in the same order on every path.
 The compute of step 2 is a function argument, so the routing is testable on
 CPU ranks with gloo.
+
+:func:`sharded_step` is the one-shot form (shapes travel in a header every
+call); :class:`DecodeShards` is the repeated form for a fixed batch: shapes
+and buffers are fixed once, and a step is one permute, one point-to-point
+group out, the decode, one group back and one permute.
 """
 
 from __future__ import annotations
@@ -86,3 +91,157 @@ def sharded_step(compute: Callable, world: int, rank: int, device, *, q_shards=N
     if rank != 0:
         return None
     return [g[:c] for g, c in zip(gathered, counts)]
+
+
+class DecodeShards:
+    """Repeated sharded decode of one batch over one process per GPU.
+
+    Rank 0 hosts the Supervisor. It owns every pool's allocator, holds the
+    batch's queries in batch order, and fixes at set-up which rank holds which
+    sequences (``placement``, e.g. longest-processing-time placement by token
+    count, :func:`src.serving.lpt_placement`). Set-up is collective and runs
+    once per batch composition: one broadcast tells every rank its shard size
+    and page-table width, and every buffer is allocated then. A step is
+    collective too and does no host work beyond enqueueing:
+
+      1. rank 0 permutes the queries into shard order (one gather kernel);
+      2. rank 0 sends each rank r > 0 its query rows and its metadata (the
+         shard's lengths followed by its page-table rows, one int32 buffer),
+         NCCL point-to-point in one group; rank 0's own shard is read in place;
+      3. every rank runs ``run()``, which must decode ``q`` / ``page_table`` /
+         ``seq_lens`` (the receive buffers below) into ``out``;
+      4. rank 0 receives every shard's output rows in one group and permutes
+         them back to batch order.
+
+    Every rank calls the same collectives in the same order; every rank must
+    hold at least one sequence. The metadata is resent every step because the
+    lengths grow by one token per step and a chain gains a block every 64
+    tokens; ``set_meta`` (rank 0) rewrites it.
+    """
+
+    def __init__(self, world: int, rank: int, device, *, q_heads: int, head_dim: int, dtype,
+                 placement=None, widths=None, group=None):
+        import torch
+        import torch.distributed as dist
+
+        self.world, self.rank, self.device, self.group = world, rank, device, group
+        hdr = torch.zeros(2 * world, dtype=torch.int64, device=device)
+        if rank == 0:
+            if placement is None or widths is None or len(widths) != world:
+                raise RuntimeError("rank 0 needs the placement and one page-table width per rank")
+            counts = [0] * world
+            for r in placement:
+                if not 0 <= int(r) < world:
+                    raise RuntimeError(f"placement names rank {r} outside [0, {world})")
+                counts[int(r)] += 1
+            hdr[:world] = torch.tensor(counts, dtype=torch.int64)
+            hdr[world:] = torch.tensor([int(w) for w in widths], dtype=torch.int64)
+        if world > 1:
+            dist.broadcast(hdr, src=0, group=group)
+        vals = [int(x) for x in hdr.tolist()]
+        self.counts, self.widths = vals[:world], vals[world:]
+        if min(self.counts) < 1:
+            raise RuntimeError(f"every rank must hold a sequence, shard sizes {self.counts}")
+        if min(self.widths) < 1:
+            raise RuntimeError(f"page-table widths must be >= 1, got {self.widths}")
+        self.n, self.width = self.counts[rank], self.widths[rank]
+        self.q_off = [sum(self.counts[:r]) for r in range(world)]
+        self.meta_len = [c * (1 + w) for c, w in zip(self.counts, self.widths)]
+        self.meta_off = [sum(self.meta_len[:r]) for r in range(world)]
+        S = sum(self.counts)
+        qshape = (q_heads, head_dim)
+        if rank == 0:
+            order = sorted(range(S), key=lambda i: (int(placement[i]), i))
+            self.batch_index = order  # shard-order position -> batch index
+            self.perm = torch.tensor(order, dtype=torch.int64, device=device)
+            inv = [0] * S
+            for pos, i in enumerate(order):
+                inv[i] = pos
+            self.inv = torch.tensor(inv, dtype=torch.int64, device=device)
+            self.q_perm = torch.empty((S,) + qshape, dtype=dtype, device=device)
+            self.meta_all = torch.zeros(sum(self.meta_len), dtype=torch.int32, device=device)
+            self.out_perm = torch.empty((S,) + qshape, dtype=dtype, device=device)
+            self.out_batch = torch.empty((S,) + qshape, dtype=dtype, device=device)
+            self.q = self.q_perm[:self.n]
+            meta = self.meta_all[:self.meta_len[0]]
+            self.out = self.out_perm[:self.n]
+        else:
+            self.q = torch.empty((self.n,) + qshape, dtype=dtype, device=device)
+            meta = torch.zeros(self.meta_len[rank], dtype=torch.int32, device=device)
+            self.out = torch.empty((self.n,) + qshape, dtype=dtype, device=device)
+        self.meta = meta
+        self.seq_lens = meta[:self.n]
+        self.page_table = meta[self.n:].view(self.n, self.width)
+
+    def shard_of(self, r: int) -> list[int]:
+        """Rank 0: the batch indices rank r holds, in its shard order."""
+        return self.batch_index[self.q_off[r]:self.q_off[r] + self.counts[r]]
+
+    def set_meta(self, lens_per_rank, pt_per_rank) -> None:
+        """Rank 0: writes every shard's lengths [n_r] and page-table rows [n_r, w_r]."""
+        import torch
+
+        if self.rank != 0:
+            raise RuntimeError("set_meta runs on the Supervisor's rank (0)")
+        for r in range(self.world):
+            ln = torch.as_tensor(lens_per_rank[r], dtype=torch.int32).reshape(-1)
+            pt = torch.as_tensor(pt_per_rank[r], dtype=torch.int32)
+            if ln.numel() != self.counts[r] or tuple(pt.shape) != (self.counts[r], self.widths[r]):
+                raise RuntimeError(f"rank {r}: lengths / page table do not match the shard "
+                                   f"({self.counts[r]} sequences, width {self.widths[r]})")
+            seg = self.meta_all[self.meta_off[r]:self.meta_off[r] + self.meta_len[r]]
+            seg[:self.counts[r]].copy_(ln, non_blocking=True)
+            seg[self.counts[r]:].copy_(pt.reshape(-1), non_blocking=True)
+
+    def _exchange(self, ops) -> None:
+        import torch.distributed as dist
+
+        if ops:
+            for w in dist.batch_isend_irecv(ops):
+                w.wait()
+
+    def scatter(self, q_batch=None) -> None:
+        """Step parts 1-2: rank 0 passes the batch's queries [S, Hq, D]."""
+        import torch
+        import torch.distributed as dist
+
+        ops = []
+        if self.rank == 0:
+            torch.index_select(q_batch, 0, self.perm, out=self.q_perm)
+            for r in range(1, self.world):
+                ops.append(dist.P2POp(dist.isend, self.q_perm[self.q_off[r]:self.q_off[r] +
+                                                              self.counts[r]], r, self.group))
+                ops.append(dist.P2POp(dist.isend, self.meta_all[self.meta_off[r]:self.meta_off[r] +
+                                                                self.meta_len[r]], r, self.group))
+        else:
+            ops.append(dist.P2POp(dist.irecv, self.q, 0, self.group))
+            ops.append(dist.P2POp(dist.irecv, self.meta, 0, self.group))
+        if self.world > 1:
+            self._exchange(ops)
+
+    def gather(self, out=None):
+        """Step part 4: rank 0 returns the outputs [S, Hq, D] in batch order (in ``out``
+        when given, else in a buffer of its own that the next step overwrites); others None."""
+        import torch
+        import torch.distributed as dist
+
+        ops = []
+        if self.rank == 0:
+            for r in range(1, self.world):
+                ops.append(dist.P2POp(dist.irecv, self.out_perm[self.q_off[r]:self.q_off[r] +
+                                                                self.counts[r]], r, self.group))
+        else:
+            ops.append(dist.P2POp(dist.isend, self.out, 0, self.group))
+        if self.world > 1:
+            self._exchange(ops)
+        if self.rank != 0:
+            return None
+        dst = self.out_batch if out is None else out
+        torch.index_select(self.out_perm, 0, self.inv, out=dst)
+        return dst
+
+    def step(self, run: Callable, q_batch=None, out=None):
+        """One decode step: scatter, ``run()`` on every rank, gather (rank 0 gets the rows)."""
+        self.scatter(q_batch)
+        run()
+        return self.gather(out)

@@ -26,6 +26,7 @@ class DecodeArgs(ctypes.Structure):
         ("max_blocks", _i32), ("num_phys_blocks", _i32), ("max_positions", _i32),
         ("dtype", _i32), ("split_blocks", _i32), ("causal", _i32), ("kernel", _i32),
         ("softmax_scale", ctypes.c_float),
+        ("total_blocks", _i64), ("max_seq_blocks", _i32),
     ]
 
 

@@ -214,7 +214,8 @@ def _scope_tensors(scope, S: int, device):
 
 
 def _decode_args(page_table, q, k_cache, v_cache, seq_lens, cos, sin, positions, mask, scope,
-                 causal, softmax_scale, split_blocks, kernel, out, workspace, status):
+                 causal, softmax_scale, split_blocks, kernel, out, workspace, status,
+                 total_blocks=0, max_seq_blocks=0):
     S, Hq, D = q.shape
     n_phys, Hkv, blk, Dk = k_cache.shape
     a = _capi.DecodeArgs()
@@ -243,6 +244,8 @@ def _decode_args(page_table, q, k_cache, v_cache, seq_lens, cos, sin, positions,
     a.causal = 1 if causal else 0
     a.kernel = _KERNELS[kernel]
     a.softmax_scale = float(softmax_scale) if softmax_scale is not None else 0.0
+    a.total_blocks = int(total_blocks)
+    a.max_seq_blocks = int(max_seq_blocks)
     return a
 
 
@@ -263,11 +266,19 @@ class DecodeCall:
     Building one does the checks and conversions once; :meth:`launch` then
     only enqueues the kernels on the current stream (no host work besides the
     C call), so a serving loop or a CUDA graph can replay it.
+
+    ``total_blocks`` (sum of ceil(keys / 64) over the batch) and
+    ``max_seq_blocks`` (a bound on any sequence's blocks) are optional host
+    figures for the split-K plan: with them the chunks are sized from the
+    batch's real work and the workspace from its longest sequence instead of
+    from the page-table width. Keys beyond ``max_seq_blocks * 64`` are not
+    read and set status bit 1.
     """
 
     def __init__(self, page_table, q, k_cache, v_cache, seq_lens, cos, sin, *, positions=None,
                  mask=None, scope=None, causal=False, softmax_scale=None, out=None,
-                 validate=True, split_blocks=0, kernel="auto", workspace=None, status=None):
+                 validate=True, split_blocks=0, kernel="auto", workspace=None, status=None,
+                 total_blocks=0, max_seq_blocks=0):
         _require_cuda()
         if kernel not in _KERNELS:
             raise RuntimeError(f"kernel must be one of {sorted(_KERNELS)}, got {kernel!r}")
@@ -331,9 +342,11 @@ class DecodeCall:
         self.out = out
         self.device = device
         self.status = status
+        if total_blocks < 0 or max_seq_blocks < 0:
+            raise RuntimeError("total_blocks and max_seq_blocks must be >= 0 (0 = unknown)")
         args = _decode_args(page_table, q, k_cache, v_cache, seq_lens, cos, sin, positions,
                             mask_arg, scope_arg, causal, softmax_scale, split_blocks, kernel, out,
-                            None, status)
+                            None, status, total_blocks, max_seq_blocks)
         self.plan = decode_plan(args)
         if self.plan["workspace_bytes"]:
             need = self.plan["workspace_bytes"]
@@ -417,6 +430,8 @@ def _rows_args(q, q_paged, k_cache, v_cache, page_table, seq_lens, q_start, cos,
     a.causal = 1 if causal else 0
     a.kernel = _KERNELS[kernel]
     a.softmax_scale = float(softmax_scale) if softmax_scale is not None else 0.0
+    a.total_blocks = int(total_blocks)
+    a.max_seq_blocks = int(max_seq_blocks)
     return a
 
 
@@ -641,3 +656,23 @@ def paged_kv_append(k_new, v_new, page_table, start, counts, k_cache, v_cache, *
         _ptr(k_new), _ptr(v_new), _ptr(pt), _ptr(st), _ptr(ct), _ptr(k_cache), _ptr(v_cache),
         S, Hkv, L, D, k_cache.element_size(), pt.shape[1], k_cache.shape[0], _ptr(status),
         _stream_handle(device)), "kv append")
+
+
+def __getattr__(name: str):
+    """Names of the reference module that this one deliberately does not provide.
+
+    ``dense_reference`` (block_attention.py:538-595 of the reference) is the
+    reference's fp32 torch check of this kernel, an O(T^2) CPU-capable
+    computation; this module holds only the GPU path, so the check stays with
+    the code it checks. Callers keep importing it from the reference checkout
+    (``src.kernels.block_attention.dense_reference``), or use this
+    repository's numpy restatement ``oracle.attention_oracle.dense_attention``
+    (test infrastructure).
+    """
+    if name == "dense_reference":
+        raise AttributeError(
+            "dense_reference is not part of the B200 module: it is the reference's fp32 "
+            "check, not the attention path. Import it from the reference checkout "
+            "(src.kernels.block_attention.dense_reference) or use "
+            "oracle.attention_oracle.dense_attention from this repository's tests")
+    raise AttributeError(f"module {__name__!r} has no attribute {name!r}")

@@ -2,7 +2,10 @@
 
 Run in a container where the reference checkout is mounted:
 
-    python tests/golden/make_golden.py --reference /root/reference
+    python tests/golden/make_golden.py --reference <reference checkout>
+
+(or set OURO_REFERENCE; the script stops with a message when neither names a
+checkout holding src/kernels/block_attention.py).
 
 It imports the reference's own ``src`` package (BlockTable, dense_reference,
 golden_attention_mt, block_sparse_mask) and records, for seeded inputs built
@@ -26,6 +29,7 @@ The GPU box never runs this script; tests read only the recorded files.
 from __future__ import annotations
 
 import argparse
+import os
 import json
 import sys
 from pathlib import Path
@@ -223,8 +227,12 @@ def gen_scope_masks(cases, rsm):
 
 def main() -> int:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("OURO_REFERENCE"),
+                    help="the reference checkout (default: $OURO_REFERENCE)")
     args = ap.parse_args()
+    if not args.reference or not (Path(args.reference) / "src" / "kernels" /
+                                  "block_attention.py").exists():
+        ap.error("pass --reference <reference checkout> or set OURO_REFERENCE")
     import numpy as np
     import torch
 
