@@ -424,6 +424,8 @@ def run_ours(args):
     e2e = _e2e_sharded(torch, dist, sh, call, world, rank, device, q_batch, args)
     weak = _weak_scaling_leg(torch, dist, world, rank, device, args) if world > 1 else None
     pre = _prefill_leg(args, world, rank, device) if not args.no_prefill else None
+    refk = (_reference_kernel_leg(args, device)
+            if (rank == 0 and world == 1 and not args.no_reference_kernel) else None)
     cpu = _cpu_baseline_leg() if (rank == 0 and world == 1 and not args.no_cpu) else None
     peak, peak_kind = _peaks()
     launches = args.steps * (1 + (1 if plan["max_splits"] > 1 else 0))
@@ -466,6 +468,8 @@ def run_ours(args):
             line["weak_scaling"] = weak
         if pre is not None:
             line["prefill"] = pre
+        if refk is not None:
+            line["reference_kernel"] = refk
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
@@ -807,6 +811,103 @@ def run_prefill(args):
     return 0
 
 
+REF_KERNEL_SHAPES = {
+    "cpu_decode_batch_fp32": dict(seqs=4, lens=[64, 130, 200, 511], heads=8, head_dim=64,
+                                  dtype="fp32", pool_blocks=64, rope_base=10000.0, std=1.0),
+    "mha_fp16": dict(seqs=32, ctx_min=512, ctx_max=4096, heads=32, head_dim=128, dtype="fp16",
+                     pool_blocks=4096, rope_base=10000.0, std=0.5),
+}
+
+
+def _reference_kernel_leg(args, device):
+    """The reference's own Triton kernel beside this repository's drop-in block_attention.
+
+    Both through their public entry points on identical inputs: full self-attention
+    (every row of every sequence: the reference's entry computes all rows), paged
+    q/k/v, RoPE, no bias. Shapes: the CPU-runnable decode batch (fp32; here the
+    CUDA-core kernel) and the fp16 MHA shape (32 sequences, lens U[512, 4096], 32
+    heads, head_dim 128; here the tcgen05 kernel). Time per call with CUDA events,
+    host-side checks included on both sides; FLOPs = 4 H D sum_s T_s^2.
+    """
+    import torch
+
+    sys.path.insert(0, str(ROOT / "tests"))
+    try:
+        import reference_kernel
+
+        ref = reference_kernel.load()
+    except Exception as exc:  # noqa: BLE001 - the install may be absent
+        return {"unavailable": f"{type(exc).__name__}: {exc}"}
+    from src.block_table import BlockTable
+    from src.kernels.block_attention import block_attention
+
+    out = {"note": "reference = the reference's Triton kernel via its block_attention; ours = "
+                   "src.kernels.block_attention.block_attention; full self-attention, every "
+                   "row; time per call, host checks included"}
+    for name, c in REF_KERNEL_SHAPES.items():
+        rng = random.Random(2)
+        lens = c.get("lens") or [rng.randint(c["ctx_min"], c["ctx_max"]) for _ in range(c["seqs"])]
+        pool, H, D = c["pool_blocks"], c["heads"], c["head_dim"]
+        dt = torch.float32 if c["dtype"] == "fp32" else torch.float16
+        bt = BlockTable(pool)
+        ids = [bt.allocate_block() for _ in range(pool)]
+        rng.shuffle(ids)
+        for i in ids:
+            bt.free_block(i)
+        heads = [bt.allocate_chain(-(-n // 64)) for n in lens]
+        max_b = max(-(-n // 64) for n in lens)
+        pt = torch.from_numpy(bt.export_page_table(heads, max_b)).to(device)
+        g = torch.Generator(device=device).manual_seed(2)
+        qkv = [(torch.randn(pool, H, 64, D, generator=g, device=device) * c["std"]).to(dt)
+               for _ in range(3)]
+        half = D // 2
+        inv = 1.0 / (c["rope_base"] ** (torch.arange(half, dtype=torch.float64) * 2.0 / D))
+        ang = torch.arange(max_b * 64, dtype=torch.float64)[:, None] * inv[None, :]
+        cos, sin = torch.cos(ang).float().to(device), torch.sin(ang).float().to(device)
+        lens_t = torch.tensor(lens, dtype=torch.int32, device=device)
+        call_args = (pt, *qkv, lens_t, cos, sin)
+        flops = 4.0 * H * D * sum(n * n for n in lens)
+        res = {"shape": dict(c, lens=None if "ctx_min" in c else lens)}
+        outs = {}
+        for side, fn in (("reference_triton", ref.block_attention), ("ours", block_attention)):
+            try:
+                for _ in range(2):
+                    o = fn(*call_args)
+                torch.cuda.synchronize(device)
+                steps = 5
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                for _ in range(steps):
+                    o = fn(*call_args)
+                e1.record()
+                torch.cuda.synchronize(device)
+                ms = e0.elapsed_time(e1) / steps
+                res[side] = {"ms_per_call": ms, "TFLOP/s": flops / (ms / 1000.0) / 1e12}
+                outs[side] = o
+            except Exception as exc:  # noqa: BLE001 - record why a side could not run
+                res[side] = {"error": f"{type(exc).__name__}: {str(exc)[:300]}"}
+        if len(outs) == 2:
+            errs = torch.cat([(outs["ours"][s, :, :n].float() - outs["reference_triton"][s, :, :n]
+                               .float()).abs().reshape(-1) for s, n in enumerate(lens)])
+            res["max_abs_diff"], res["mean_abs_diff"] = float(errs.max()), float(errs.mean())
+            res["speedup_vs_reference"] = (res["reference_triton"]["ms_per_call"] /
+                                           res["ours"]["ms_per_call"])
+        out[name] = res
+        del qkv, outs
+        torch.cuda.empty_cache()
+    return out
+
+
+def run_reference_kernel(args):
+    world, rank, local = _dist_env()
+    device = _init_dist(world, local)
+    if rank == 0:
+        line = {"metric": "full self-attention per call: the reference's Triton kernel vs ours",
+                "n_gpus": 1, "data": "synthetic", **_reference_kernel_leg(args, device)}
+        print(json.dumps(line), flush=True)
+    return 0
+
+
 SCOPED = dict(workload="mha_paged_decode_fp16_scoped", seqs=32, heads=32, head_dim=128,
               dtype="fp16", ctx_min=512, ctx_max=4096, pool_blocks=4096, rope_base=10000.0,
               segment_min=32, segment_max=512, seed=2)
@@ -1012,13 +1113,16 @@ def main() -> int:
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--split-blocks", type=int, default=0)
-    ap.add_argument("--kernel", default="auto", choices=["auto", "tc", "simt"])
+    ap.add_argument("--kernel", default="auto", choices=["auto", "tc", "tc2", "simt"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
     ap.add_argument("--no-prefill", action="store_true",
                     help="skip the chunked-prefill sub-object of the decode line")
+    ap.add_argument("--no-reference-kernel", action="store_true",
+                    help="skip the reference Triton kernel comparison (N = 1 only)")
     ap.add_argument("--prefill-steps", type=int, default=0,
                     help="timed prefill passes (default: --steps)")
-    ap.add_argument("--workload", choices=["decode", "prefill", "serving", "decode-scoped"],
+    ap.add_argument("--workload", choices=["decode", "prefill", "serving", "decode-scoped",
+                                           "reference-kernel"],
                     default="decode",
                     help="decode (the headline metric), the chunked-prefill tensor-core pass, "
                          "the serving trace (continuous batching end to end) or the scoped "
@@ -1035,6 +1139,8 @@ def main() -> int:
         return run_serving(args)
     if args.workload == "decode-scoped":
         return run_decode_scoped(args)
+    if args.workload == "reference-kernel":
+        return run_reference_kernel(args)
     return run_ours(args)
 
 

@@ -33,6 +33,7 @@ struct DecodeParams {
   int32_t blocks_cap;         // keys read per sequence <= blocks_cap * 64 (<= max_blocks * 64)
   int32_t split_blocks, max_splits;
   int32_t causal;
+  int32_t tc_ctas_per_sm;     // tensor-core kernel: 1 (8 KV heads per CTA) or 2 (4 per CTA)
   float scale_log2;           // softmax_scale * log2(e)
 };
 

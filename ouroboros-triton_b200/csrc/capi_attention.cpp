@@ -44,7 +44,7 @@ int num_sms() {
 
 // Split-K planning: CTAs per SM the planner aims for, and the smallest chunk.
 constexpr int kSplitWaves = 12;
-constexpr int kMinSplitBlocks = 4;
+constexpr int kMinSplitBlocks = 16;
 
 int hpc_of(int hkv) {
   for (int h : {8, 4, 2, 1})
@@ -102,6 +102,7 @@ ouro::DecodeParams to_params(const ouro_decode_args* a) {
   if (a->max_seq_blocks < 0 || a->total_blocks < 0)
     fail(OURO_EINVAL, "max_seq_blocks and total_blocks must be >= 0 (0 = unknown)");
   p.blocks_cap = a->max_seq_blocks > 0 ? std::min(a->max_seq_blocks, p.max_blocks) : p.max_blocks;
+  p.tc_ctas_per_sm = 1;
   return p;
 }
 
@@ -109,12 +110,13 @@ ouro::DecodeParams to_params(const ouro_decode_args* a) {
 // `waves` CTAs per SM. The work is the caller's total_blocks when given, else
 // every row counted as long as the longest allowed one.
 int choose_split(const ouro::DecodeParams& p, int64_t total_blocks, bool tc, int waves) {
-  const int hpc = tc ? hpc_of(p.Hkv) : 1;
+  const int hpc = tc ? (p.tc_ctas_per_sm == 2 ? 4 : hpc_of(p.Hkv)) : 1;
   const int64_t groups = tc ? p.Hkv / hpc : static_cast<int64_t>(p.Hkv) * ((p.G + 7) / 8);
   const int64_t blocks = total_blocks > 0 ? total_blocks
                                           : static_cast<int64_t>(p.S) * std::max(p.blocks_cap, 1);
   const int64_t work = blocks * groups;
-  const int64_t target = static_cast<int64_t>(num_sms()) * std::max(waves, 1);
+  const int64_t target =
+      static_cast<int64_t>(num_sms()) * std::max(waves, 1) * (tc ? p.tc_ctas_per_sm : 1);
   int64_t split = (work + target - 1) / std::max<int64_t>(target, 1);
   split = std::max<int64_t>(split, kMinSplitBlocks);
   split = std::min<int64_t>(split, std::max(p.blocks_cap, 1));
@@ -133,11 +135,18 @@ void plan(ouro::DecodeParams& p, const ouro_decode_args* a, bool* use_tc, size_t
       a->dtype);
   bool tc = false;
   if (a->kernel == 0) tc = tc_ok;
-  else if (a->kernel == 2) {
+  else if (a->kernel == 2 || a->kernel == 3) {
     if (!tc_ok) fail(OURO_EUNSUPPORTED, "tensor-core decode not built for this dtype/head_dim/group");
+    if (a->kernel == 3) {
+      if (p.Hkv % 4 != 0)
+        fail(OURO_EUNSUPPORTED, "two CTAs per SM need a multiple of 4 KV heads");
+      p.tc_ctas_per_sm = 2;
+    }
     tc = true;
   } else if (a->kernel != 1) {
-    fail(OURO_EINVAL, "kernel selector must be 0 (auto), 1 (cuda cores) or 2 (tensor cores)");
+    fail(OURO_EINVAL,
+         "kernel selector must be 0 (auto), 1 (cuda cores), 2 (tensor cores) or 3 (tensor "
+         "cores, two CTAs per SM)");
   }
   int split = a->split_blocks > 0 ? a->split_blocks
                                   : choose_split(p, a->total_blocks, tc, kSplitWaves);
@@ -242,8 +251,8 @@ int ouro_paged_attention(const ouro_attention_args* args, void* stream) {
     const bool tc_ok = ouro::prefill_tc_supported(p, args->dtype);
     if (args->kernel == 2 && !tc_ok)
       fail(OURO_EUNSUPPORTED,
-           "tensor-core attention needs dense fp16/bf16 queries, head_dim 128, no bias or block "
-           "mask, and a GQA group dividing 128");
+           "tensor-core attention needs fp16/bf16, head_dim 128, no additive bias, a GQA group "
+           "dividing 128, and as many query heads as KV heads for paged queries");
     auto st = static_cast<cudaStream_t>(stream);
     if (args->kernel == 2 || (args->kernel == 0 && tc_ok)) {
       const int64_t need = ouro::prefill_workspace_bytes(p);

@@ -51,14 +51,17 @@ namespace {
 constexpr int kTok = 16;  // tokens per stage
 constexpr int kWph = 2;   // consumer warps per KV head; they take alternate stages
 
-template <int D, int HPC>
+// MINB CTAs share an SM (1: the ring takes ~216 KB; 2: two CTAs of HPC = 4
+// with a 2-stage ring each, so one CTA's prologue and tail overlap the other's
+// streaming on small batches).
+template <int D, int HPC, int MINB = 1>
 struct TcLayout {
   static constexpr int kKBoxes = D / 64;                 // 64-column (128 B) boxes per K/V row
   static constexpr int kTBoxes = (D / 2) / 32;           // 32-column (128 B) boxes per table row
   static constexpr int kHeadTile = kTok * D * 2;         // bytes of one head's K (or V) tile
   static constexpr int kTblTile = kTok * (D / 2) * 4;    // bytes of one cos (or sin) tile
   static constexpr int kStage = 2 * HPC * kHeadTile + 2 * kTblTile;
-  static constexpr int kStages = std::max(2, std::min(6, 221184 / kStage));
+  static constexpr int kStages = std::max(2, std::min(6, (MINB == 1 ? 221184 : 90112) / kStage));
   static constexpr int kK = 0;                           // offsets within a stage
   static constexpr int kV = HPC * kHeadTile;
   static constexpr int kCos = 2 * HPC * kHeadTile;
@@ -113,13 +116,13 @@ __device__ __forceinline__ void issue_stage(const CUtensorMap* tm_k, const CUten
   if (p.scope_tags) bulk_load(tag_dst, p.scope_tags + s * p.scope_stride + pos_row, 16, full);
 }
 
-template <typename T, int D, int HPC>
-__global__ void __launch_bounds__(HPC * kWph * 32, 1)
+template <typename T, int D, int HPC, int MINB>
+__global__ void __launch_bounds__(HPC * kWph * 32, MINB)
     decode_tc_kernel(const __grid_constant__ CUtensorMap tm_k,
                      const __grid_constant__ CUtensorMap tm_v,
                      const __grid_constant__ CUtensorMap tm_cos,
                      const __grid_constant__ CUtensorMap tm_sin, const DecodeParams p) {
-  using L = TcLayout<D, HPC>;
+  using L = TcLayout<D, HPC, MINB>;
   using MK = MmaKind<T>;
   constexpr int S_ = L::kStages;
   constexpr int KC = D / 16;     // 16-column chunks of head_dim
@@ -554,14 +557,14 @@ bool make_map_tbl3(CUtensorMap* m, const void* base, uint64_t halves, uint64_t r
          CUDA_SUCCESS;
 }
 
-template <int D, int HPC>
+template <int D, int HPC, int MINB>
 size_t tc_smem_bytes(int split_blocks) {
-  using L = TcLayout<D, HPC>;
+  using L = TcLayout<D, HPC, MINB>;
   return 1024 + static_cast<size_t>(L::kStages) * L::kStage + 2 * L::kStages * sizeof(uint64_t) +
          L::kStages * 16 + 2 * sizeof(int32_t) * static_cast<size_t>(split_blocks);
 }
 
-template <typename T, int D, int HPC>
+template <typename T, int D, int HPC, int MINB>
 cudaError_t launch_tc_typed(const DecodeParams& p, CUtensorMapDataType dt, cudaStream_t stream) {
   CUtensorMap mk, mv, mc, ms;
   const uint64_t planes = static_cast<uint64_t>(p.n_phys) * p.Hkv;
@@ -569,8 +572,8 @@ cudaError_t launch_tc_typed(const DecodeParams& p, CUtensorMapDataType dt, cudaS
       !make_map_kv3(&mv, p.v, dt, D, planes, kTok, HPC) ||
       !make_map_tbl3(&mc, p.cos, D / 64, p.max_pos) || !make_map_tbl3(&ms, p.sin, D / 64, p.max_pos))
     return cudaErrorInvalidValue;
-  const size_t smem = tc_smem_bytes<D, HPC>(p.split_blocks);
-  auto kernel = decode_tc_kernel<T, D, HPC>;
+  const size_t smem = tc_smem_bytes<D, HPC, MINB>(p.split_blocks);
+  auto kernel = decode_tc_kernel<T, D, HPC, MINB>;
   cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        static_cast<int>(smem));
   if (e != cudaSuccess) return e;
@@ -588,8 +591,13 @@ int pick_hpc(int hkv) {
 template <typename T>
 cudaError_t dispatch_tc(const DecodeParams& p, CUtensorMapDataType dt, cudaStream_t stream) {
   const int hpc = pick_hpc(p.Hkv);
+  if (p.tc_ctas_per_sm == 2) {
+    if (p.D == 128 && p.Hkv % 4 == 0) return launch_tc_typed<T, 128, 4, 2>(p, dt, stream);
+    if (p.D == 64 && p.Hkv % 4 == 0) return launch_tc_typed<T, 64, 4, 2>(p, dt, stream);
+    return cudaErrorNotSupported;
+  }
 #define OURO_TC_CASE(DD, HH) \
-  if (p.D == DD && hpc == HH) return launch_tc_typed<T, DD, HH>(p, dt, stream);
+  if (p.D == DD && hpc == HH) return launch_tc_typed<T, DD, HH, 1>(p, dt, stream);
   OURO_TC_CASE(128, 8) OURO_TC_CASE(128, 4) OURO_TC_CASE(128, 2) OURO_TC_CASE(128, 1)
   OURO_TC_CASE(64, 8) OURO_TC_CASE(64, 4) OURO_TC_CASE(64, 2) OURO_TC_CASE(64, 1)
 #undef OURO_TC_CASE

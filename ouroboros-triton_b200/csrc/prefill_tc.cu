@@ -364,7 +364,7 @@ __device__ __forceinline__ void rotation_arrive(unsigned long long* word) {
 // The caller passes rows R0, R0 + dR, R0 + 2 dR, R0 + 3 dR and one c; eight
 // consecutive threads take the 8 units of one row, so a warp-wide load reads 4
 // contiguous row segments.
-template <typename T>
+template <typename T, bool kPaged>
 struct QTile {
   uint4 lo[4], hi[4];
   float4 cs[8], sn[8];
@@ -381,11 +381,29 @@ struct QTile {
       cs[2 * k] = cs[2 * k + 1] = make_float4(1.f, 1.f, 1.f, 1.f);
       sn[2 * k] = sn[2 * k + 1] = make_float4(0.f, 0.f, 0.f, 0.f);
       if (iR < it.rows_valid) {
-        const T* qrow = static_cast<const T*>(p.q) +
-                        ((static_cast<int64_t>(it.s) * p.Hq + it.kvh * p.G + (R >> lppt)) * p.Lq +
-                         it.qt * ppt + iR) * kHD;
-        lo[k] = *reinterpret_cast<const uint4*>(qrow + 8 * c);
-        hi[k] = *reinterpret_cast<const uint4*>(qrow + half + 8 * c);
+        const int head = it.kvh * p.G + (R >> lppt);
+        const T* qrow = nullptr;
+        if (kPaged) {
+          // the row sits in the paged query cache at its position: block
+          // page_table[s][pos / 64], slot pos % 64 (q_start is 0 here)
+          const int pb = posR >> 6;
+          const int phys = pb < p.max_blocks
+                               ? p.page_table[static_cast<int64_t>(it.s) * p.max_blocks + pb]
+                               : -1;
+          if (phys >= 0 && phys < p.n_phys)
+            qrow = static_cast<const T*>(p.q) +
+                   ((static_cast<int64_t>(phys) * p.Hq + head) * kBlock + (posR & (kBlock - 1))) *
+                       kHD;
+          else if (p.status)
+            atomicOr(p.status, kStatusBadPageEntry);
+        } else {
+          qrow = static_cast<const T*>(p.q) +
+                 ((static_cast<int64_t>(it.s) * p.Hq + head) * p.Lq + it.qt * ppt + iR) * kHD;
+        }
+        if (qrow != nullptr) {
+          lo[k] = *reinterpret_cast<const uint4*>(qrow + 8 * c);
+          hi[k] = *reinterpret_cast<const uint4*>(qrow + half + 8 * c);
+        }
         if (posR < p.max_pos) {
           const float4* cr = reinterpret_cast<const float4*>(p.cos + static_cast<int64_t>(posR) * half + 8 * c);
           const float4* sr = reinterpret_cast<const float4*>(p.sin + static_cast<int64_t>(posR) * half + 8 * c);
@@ -409,7 +427,10 @@ struct QTile {
   }
 };
 
-template <typename T, bool kScoped>
+// kScoped: token scope; kMasked: block mask; kPaged: queries read through the page
+// table (the full self-attention entry). Each combination in use is its own
+// instantiation, so the plain chunked-prefill kernel carries none of their code.
+template <typename T, bool kScoped, bool kMasked, bool kPaged>
 __global__ void __launch_bounds__(kThreads, 1)
     prefill_tc_kernel(const __grid_constant__ CUtensorMap tm_k,
                       const __grid_constant__ CUtensorMap tm_v, const RowsParams p,
@@ -724,7 +745,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // Item done + 2's query tile into the same buffer: this warp writes rows
       // 32 quarter .. +31 (the rows it staged), in two rounds of 16 rows.
       if (Lq < n_items) {
-        QTile<T> qn;
+        QTile<T, kPaged> qn;
 #pragma unroll 1
         for (int rnd = 0; rnd < 2; ++rnd) {
           const int R0 = quarter * 32 + 16 * rnd + (lane >> 3);
@@ -761,7 +782,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       int Lq = L;
 #pragma unroll 1
       for (int b = 0; b < 2 && Lq < n_items; ++b) {
-        QTile<T> qn;
+        QTile<T, kPaged> qn;
         const int R0 = tid >> 3;
         qn.load(p, iq, ppt, R0, 32, tid & 7);
         qn.store(smem + (b ? kOffQ1 : kOffQ0), p.scale_log2, R0, 32, tid & 7);
@@ -844,6 +865,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int pos = it.q0 + i;
       const int kmax_row = !live ? 0 : (p.causal ? min(it.seq_len, pos + 1) : it.seq_len);
       const int n = it.n_tiles;
+      // Block mask (optional): the row's mask row is (s, query block); paged
+      // queries use the row's block (its position / 64), dense chunks row 0, as
+      // the CUDA-core kernel does. Key blocks are looked up per tile.
+      const int8_t* mrow = nullptr;
+      if (kMasked)
+        mrow = p.mask + static_cast<int64_t>(it.s) * p.mask_s +
+               static_cast<int64_t>(kPaged ? (it.qt * ppt + i) >> 6 : 0) * p.mask_q;
+      const int nb_row = kMasked ? (kmax_row + kBlock - 1) / kBlock : 0;
       if (kScoped) {
         sc_tags = p.scope_tags + static_cast<int64_t>(it.s) * p.scope_stride;
         sc_lo = live ? p.scope_lo[static_cast<int64_t>(it.s) * p.scope_stride + pos] : 0;
@@ -861,9 +890,21 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         tc_fence_after();
         const int key0 = j * kBN;
+        // Block mask of the tile's two key blocks: a masked block's keys get -inf
+        // (the row's limit takes care of blocks past its keys).
+        uint32_t kb_keep = 3u;
+        if (kMasked) {
+          const int kb = 2 * j;
+          kb_keep = (kb < nb_row && mrow[static_cast<int64_t>(kb) * p.mask_k] != 0 ? 1u : 0u) |
+                    (kb + 1 < nb_row && mrow[static_cast<int64_t>(kb + 1) * p.mask_k] != 0 ? 2u
+                                                                                          : 0u);
+        }
         // Tiles that lie wholly below every row's key limit skip the per-key masks
-        // (never with a token scope).
-        const bool full = !kScoped && __all_sync(0xffffffffu, key0 + kBN <= kmax_row);
+        // (never with a token scope or a masked block).
+        const bool full =
+            !kScoped && __all_sync(0xffffffffu, key0 + kBN <= kmax_row && kb_keep == 3u);
+        const int kmax_a = (!kMasked || (kb_keep & 1u)) ? kmax_row : min(kmax_row, key0);
+        const int kmax_b = (!kMasked || (kb_keep & 2u)) ? kmax_row : min(kmax_row, key0 + 64);
         // All 128 scores of the row in registers: one TMEM round trip.
         uint32_t sa[32], sb[32], sc[32], sd[32];
         tmem_ld32(lane_addr + s_col, sa);
@@ -871,10 +912,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_ld32(lane_addr + s_col + 64, sc);
         tmem_ld32(lane_addr + s_col + 96, sd);
         tmem_wait_ld();
-        const float mx = fmaxf(fmaxf(mask_max32(sa, key0, kmax_row, full),
-                                     mask_max32(sb, key0 + 32, kmax_row, full)),
-                               fmaxf(mask_max32(sc, key0 + 64, kmax_row, full),
-                                     mask_max32(sd, key0 + 96, kmax_row, full)));
+        const float mx = fmaxf(fmaxf(mask_max32(sa, key0, kmax_a, full),
+                                     mask_max32(sb, key0 + 32, kmax_a, full)),
+                               fmaxf(mask_max32(sc, key0 + 64, kmax_b, full),
+                                     mask_max32(sd, key0 + 96, kmax_b, full)));
         const bool grow = mx > m_ref + kRescaleLog2 || (m_ref == -INFINITY && mx != -INFINITY);
         const float m_new = grow ? mx : m_ref;
         const float factor = (grow && m_ref != -INFINITY) ? fast_exp2(m_ref - m_new) : 1.f;
@@ -973,8 +1014,12 @@ bool kv_map(CUtensorMap* m, const void* base, CUtensorMapDataType dt, uint64_t r
 
 bool prefill_tc_supported(const RowsParams& p, int dtype) {
   if (dtype != 1 && dtype != 2) return false;
-  if (p.D != kHD || p.q_paged || p.bias || p.mask) return false;
+  if (p.D != kHD || p.bias) return false;
+  // built: dense queries with or without a token scope; paged queries with or
+  // without a block mask
+  if (p.q_paged ? p.scope_tags != nullptr : p.mask != nullptr) return false;
   if (p.G < 1 || kBM % p.G != 0) return false;
+  if (p.q_paged && p.G != 1) return false;
   auto aligned = [](const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; };
   if (!aligned(p.q) || !aligned(p.k) || !aligned(p.v) || !aligned(p.out) || !aligned(p.cos) ||
       !aligned(p.sin))
@@ -1021,11 +1066,23 @@ cudaError_t launch_prefill_tc(const RowsParams& p, int dtype, cudaStream_t strea
   dim3 grid(static_cast<unsigned>(std::min<int64_t>(n_items, sms)));
   using Kernel = void (*)(const CUtensorMap, const CUtensorMap, const RowsParams, int32_t,
                           unsigned long long*);
-  const bool scoped = p.scope_tags != nullptr;
-  Kernel kernel = dtype == 2 ? (scoped ? prefill_tc_kernel<__nv_bfloat16, true>
-                                       : prefill_tc_kernel<__nv_bfloat16, false>)
-                             : (scoped ? prefill_tc_kernel<__half, true>
-                                       : prefill_tc_kernel<__half, false>);
+  // Instantiations: dense chunks, plain or with a token scope; paged queries,
+  // plain or with a block mask (prefill_tc_supported admits nothing else).
+  const bool scoped = p.scope_tags != nullptr, masked = p.mask != nullptr;
+  const bool paged = p.q_paged != 0;
+  Kernel kernel = nullptr;
+  if (dtype == 2) {
+    kernel = paged ? (masked ? prefill_tc_kernel<__nv_bfloat16, false, true, true>
+                             : prefill_tc_kernel<__nv_bfloat16, false, false, true>)
+                   : (scoped ? prefill_tc_kernel<__nv_bfloat16, true, false, false>
+                             : prefill_tc_kernel<__nv_bfloat16, false, false, false>);
+  } else {
+    kernel = paged ? (masked ? prefill_tc_kernel<__half, false, true, true>
+                             : prefill_tc_kernel<__half, false, false, true>)
+                   : (scoped ? prefill_tc_kernel<__half, true, false, false>
+                             : prefill_tc_kernel<__half, false, false, false>);
+  }
+  if ((paged && scoped) || (!paged && masked)) return cudaErrorNotSupported;
   e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
   if (e != cudaSuccess) return e;
   unsigned long long* rot_sync =

@@ -38,7 +38,9 @@ struct RowsParams {
 };
 
 cudaError_t launch_attend_rows_simt(const RowsParams& p, int dtype, cudaStream_t stream);
-// tcgen05 chunked prefill: dense fp16/bf16 queries, head_dim 128, no bias / block mask.
+// tcgen05 attention: fp16/bf16, head_dim 128, dense queries (chunked prefill) or paged
+// queries with as many query heads as KV heads (full self-attention); block mask
+// supported, additive bias not (the CUDA-core kernel takes it).
 bool prefill_tc_supported(const RowsParams& p, int dtype);
 // Scratch for the rotated keys: S * Hkv * max_blocks * 64 * D elements.
 int64_t prefill_workspace_bytes(const RowsParams& p);

@@ -54,7 +54,7 @@ __all__ = [
     "validate_page_table",
 ]
 
-_KERNELS = {"auto": 0, "simt": 1, "cuda_cores": 1, "tensor_cores": 2, "tc": 2}
+_KERNELS = {"auto": 0, "simt": 1, "cuda_cores": 1, "tensor_cores": 2, "tc": 2, "tc2": 3}
 
 
 # ---------------------------------------------------------------------------
@@ -368,7 +368,8 @@ class DecodeCall:
 def block_attention_decode(page_table, q, k_cache, v_cache, seq_lens, cos, sin, *,
                            positions=None, mask=None, scope=None, causal=False,
                            softmax_scale=None, out=None, validate=True, split_blocks=0,
-                           kernel="auto", workspace=None, status=None):
+                           kernel="auto", workspace=None, status=None, total_blocks=0,
+                           max_seq_blocks=0):
     """Paged decode attention: one query token per sequence.
 
     Args:
@@ -390,7 +391,8 @@ def block_attention_decode(page_table, q, k_cache, v_cache, seq_lens, cos, sin, 
         softmax_scale: default 1/sqrt(D).
         validate: check the page table on the device first (one 8-byte read
             back; raises RuntimeError with the reference's messages).
-        split_blocks / kernel / workspace / status: launch controls; see
+        split_blocks / kernel / workspace / status / total_blocks /
+            max_seq_blocks: launch controls and planning figures; see
             :class:`DecodeCall`.
 
     Returns:
@@ -399,7 +401,8 @@ def block_attention_decode(page_table, q, k_cache, v_cache, seq_lens, cos, sin, 
     call = DecodeCall(page_table, q, k_cache, v_cache, seq_lens, cos, sin, positions=positions,
                       mask=mask, scope=scope, causal=causal, softmax_scale=softmax_scale,
                       out=out, validate=validate, split_blocks=split_blocks, kernel=kernel,
-                      workspace=workspace, status=status)
+                      workspace=workspace, status=status, total_blocks=total_blocks,
+                      max_seq_blocks=max_seq_blocks)
     return call.launch()
 
 
@@ -430,8 +433,6 @@ def _rows_args(q, q_paged, k_cache, v_cache, page_table, seq_lens, q_start, cos,
     a.causal = 1 if causal else 0
     a.kernel = _KERNELS[kernel]
     a.softmax_scale = float(softmax_scale) if softmax_scale is not None else 0.0
-    a.total_blocks = int(total_blocks)
-    a.max_seq_blocks = int(max_seq_blocks)
     return a
 
 
@@ -447,7 +448,7 @@ def _as_int32(t, name: str):
 
 
 def block_attention(page_table, q_cache, k_cache, v_cache, seq_lens, cos, sin, bias=None,
-                    mask=None, softmax_scale: float | None = None):
+                    mask=None, softmax_scale: float | None = None, *, kernel: str = "auto"):
     """Full paged self-attention: the reference's ``block_attention``, on B200.
 
     Same arguments, checks, error texts and result as the reference
@@ -462,6 +463,10 @@ def block_attention(page_table, q_cache, k_cache, v_cache, seq_lens, cos, sin, b
     * ``bias`` broadcastable to [S, H, Q, K], added to the scaled scores;
     * ``mask`` block mask broadcastable to [S, QB, KB], zero = KV block dropped;
     * ``softmax_scale`` defaults to 1/sqrt(D).
+    * ``kernel`` (keyword, not in the reference): "auto" runs fp16/bf16 caches with
+      head_dim 128 and no bias on the tcgen05 tensor-core kernel (keys rotated once
+      into a scratch the call allocates: S x H x max_blocks x 64 x D elements) and
+      everything else on the CUDA cores; "tc" / "simt" force one.
 
     Returns [S, H, max_len, D] in the cache dtype; rows past seq_lens[s] are 0.
     """
@@ -506,8 +511,17 @@ def block_attention(page_table, q_cache, k_cache, v_cache, seq_lens, cos, sin, b
         mask_arg = (mask, _broadcast_strides(tuple(mask.shape), (S, qb_max, qb_max)))
     q_c = q_cache.to(k_cache.dtype).contiguous()
     out = torch.zeros((S, H, max_len, D), dtype=k_cache.dtype, device=device)
+    if kernel not in _KERNELS or _KERNELS[kernel] > 2:
+        raise RuntimeError(f"kernel must be 'auto', 'tc' or 'simt', got {kernel!r}")
     args = _rows_args(q_c, True, k_cache, v_cache, pt, lens, None, cos, sin, bias_arg, mask_arg,
-                      out, None, H, max_len, False, softmax_scale, "auto")
+                      out, None, H, max_len, False, softmax_scale, kernel)
+    need, tc = ctypes.c_size_t(), ctypes.c_int32()
+    _native.check(_native.lib().ouro_attention_plan(ctypes.byref(args), ctypes.byref(need),
+                                                    ctypes.byref(tc)), "attention plan")
+    workspace = None
+    if tc.value and need.value:
+        workspace = torch.empty(need.value, dtype=torch.uint8, device=device)
+        args.workspace, args.workspace_bytes = _ptr(workspace), need.value
     _launch_rows(args, device)
     return out
 

@@ -93,3 +93,61 @@ def test_chunked_prefill_vs_oracle(cuda, hq, hkv, dtype):
     err = np.abs(out.float().cpu().numpy() - want)
     tol = 2e-2 if dtype != torch.float32 else 1e-4
     assert err.max() < tol and err.mean() < 2e-3, (err.max(), err.mean())
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("with_mask", [False, True])
+def test_block_attention_on_tensor_cores_vs_oracle(cuda, dtype, with_mask):
+    """The drop-in full self-attention on the tcgen05 kernel (paged queries, D 128):
+    ragged lengths (one block, a partial last block, several 128-row query tiles),
+    optionally a block mask with the diagonal kept; every valid row vs the oracle and
+    vs the CUDA-core kernel."""
+    lens = [700, 1100, 64, 200, 129]
+    H, D = 8, 128
+    bt, heads, rows = cases.scattered_chains(BlockTable, 64, lens, 33)
+    q, k, v = cases.paged_caches(torch, 33, 64, H, D, 0.5, dtype)
+    cos, sin = cases.rope_tables_torch(torch, len(rows[0]) * 64, D, 10000.0)
+    pt = torch.tensor(rows, dtype=torch.int32)
+    kw = {}
+    if with_mask:
+        qb = -(-max(lens) // 64)
+        gen = torch.Generator().manual_seed(9)
+        m = (torch.rand(len(lens), qb, qb, generator=gen) < 0.6).to(torch.int8)
+        m |= torch.eye(qb, dtype=torch.int8)
+        kw = dict(mask=m)
+    args = (pt.cuda(), q.cuda(), k.cuda(), v.cuda(), torch.tensor(lens).cuda(), cos.cuda(),
+            sin.cuda())
+    got = ba.block_attention(*args, kernel="tc", **{k2: x.cuda() for k2, x in kw.items()})
+    simt = ba.block_attention(*args, kernel="simt", **{k2: x.cuda() for k2, x in kw.items()})
+    want = ao.dense_attention(pt.numpy(), q.float().numpy(), k.float().numpy(),
+                              v.float().numpy(), lens, cos.numpy(), sin.numpy(),
+                              mask=kw["mask"].numpy() if with_mask else None)
+    for out in (got, simt):
+        errs = np.concatenate([np.abs(out[s, :, :n].float().cpu().numpy() - want[s, :, :n])
+                               .reshape(-1) for s, n in enumerate(lens)])
+        assert errs.max() <= 2e-2 and errs.mean() <= 2e-3, (errs.max(), errs.mean())
+    # rows past each sequence stay zero
+    for s, n in enumerate(lens):
+        assert got[s, :, n:].abs().max().item() == 0 if n < max(lens) else True
+
+
+def test_block_attention_auto_picks_tensor_cores_without_bias(cuda):
+    """kernel='auto' takes the tensor-core kernel for fp16/bf16, D 128, no bias, and the
+    CUDA-core kernel with an additive bias; both agree with the oracle."""
+    lens = [300, 513]
+    H, D = 4, 128
+    bt, heads, rows = cases.scattered_chains(BlockTable, 32, lens, 7)
+    q, k, v = cases.paged_caches(torch, 7, 32, H, D, 0.5, torch.bfloat16)
+    cos, sin = cases.rope_tables_torch(torch, len(rows[0]) * 64, D, 10000.0)
+    pt = torch.tensor(rows, dtype=torch.int32)
+    bias = torch.randn(1, H, max(lens), max(lens), generator=torch.Generator().manual_seed(1))
+    for kw in ({}, dict(bias=bias * 0.25)):
+        out = ba.block_attention(pt.cuda(), q.cuda(), k.cuda(), v.cuda(),
+                                 torch.tensor(lens).cuda(), cos.cuda(), sin.cuda(),
+                                 **{k2: x.cuda() for k2, x in kw.items()})
+        want = ao.dense_attention(pt.numpy(), q.float().numpy(), k.float().numpy(),
+                                  v.float().numpy(), lens, cos.numpy(), sin.numpy(),
+                                  bias=kw["bias"].numpy() if kw else None)
+        for s, n in enumerate(lens):
+            e = np.abs(out[s, :, :n].float().cpu().numpy() - want[s, :, :n])
+            assert e.max() <= 2e-2 and e.mean() <= 2e-3, (kw.keys(), e.max(), e.mean())

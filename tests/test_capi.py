@@ -75,3 +75,88 @@ def test_attention_plan_checks_arguments_on_the_host():
     rc, _, _ = _plan(_attention_args(scope_tags=1 << 33, scope_stride=1024, scope_lo=1 << 34,
                                      scope_hi=1 << 35))
     assert rc == _native.OURO_OK
+
+
+def _cpu_decode_inputs(S=4, hq=64, hkv=8, d=128, max_b=512, n_phys=4096):
+    import torch
+
+    return dict(page_table=torch.zeros((S, max_b), dtype=torch.int32),
+                q=torch.zeros((S, hq, d), dtype=torch.bfloat16),
+                k_cache=torch.zeros((8, hkv, 64, d), dtype=torch.bfloat16),
+                v_cache=torch.zeros((8, hkv, 64, d), dtype=torch.bfloat16),
+                seq_lens=torch.zeros(S, dtype=torch.int32),
+                cos=torch.zeros((max_b * 64, d // 2)), sin=torch.zeros((max_b * 64, d // 2)),
+                n_phys=n_phys)
+
+
+def _decode_plan_of(S, total_blocks=0, max_seq_blocks=0, split=0, kernel="auto"):
+    """The Python argument builder, then the library's planner (no device access)."""
+    from src.kernels import block_attention as ba
+
+    x = _cpu_decode_inputs(S=S)
+    a = ba._decode_args(x["page_table"], x["q"], x["k_cache"], x["v_cache"], x["seq_lens"],
+                        x["cos"], x["sin"], None, None, None, False, None, split, kernel,
+                        torch_empty_like(x["q"]), None, None, total_blocks, max_seq_blocks)
+    a.num_phys_blocks = x["n_phys"]
+    return ba.decode_plan(a)
+
+
+def torch_empty_like(t):
+    import torch
+
+    return torch.empty_like(t)
+
+
+def test_decode_planner_sizes_chunks_from_the_real_work():
+    """The split-K planner on the workload shape (GQA 64/8, D 128, 512-block rows):
+    with total_blocks it plans from the batch's blocks, and max_seq_blocks bounds the
+    chunks per sequence (so the workspace) instead of the page-table width."""
+    wide = _decode_plan_of(256)
+    real = _decode_plan_of(256, total_blocks=256 * 320, max_seq_blocks=512)
+    small = _decode_plan_of(32, total_blocks=32 * 320, max_seq_blocks=512)
+    assert real["split_blocks"] < wide["split_blocks"]
+    assert small["split_blocks"] < real["split_blocks"]
+    bounded = _decode_plan_of(32, total_blocks=32 * 320, max_seq_blocks=200)
+    assert bounded["max_splits"] == -(-200 // bounded["split_blocks"])
+    assert bounded["workspace_bytes"] < small["workspace_bytes"]
+
+
+def test_decode_plan_rejects_negative_hints():
+    from src import _native as nat
+
+    try:
+        _decode_plan_of(4, total_blocks=-1)
+    except RuntimeError as exc:
+        assert "total_blocks" in str(exc)
+    else:
+        raise AssertionError("negative total_blocks accepted")
+    assert nat.last_error()
+
+
+def test_rows_argument_builder_marshals_every_field():
+    """The Python builder of ouro_attention_args runs end to end (paged queries with a
+    bias and a block mask, and a dense chunk), and the library plans both."""
+    import torch
+
+    from src.kernels import block_attention as ba
+
+    S, H, D, max_b = 2, 2, 128, 3
+    q = torch.zeros((16, H, 64, D), dtype=torch.float16)
+    pt = torch.zeros((S, max_b), dtype=torch.int32)
+    lens = torch.tensor([192, 150], dtype=torch.int32)
+    cos = torch.zeros((max_b * 64, D // 2))
+    bias = torch.zeros((1, H, 192, 192))
+    mask = torch.ones((S, 3, 3), dtype=torch.int8)
+    out = torch.zeros((S, H, 192, D), dtype=torch.float16)
+    a = ba._rows_args(q, True, q, q, pt, lens, None, cos, cos, (bias, (0, 192 * 192, 192, 1)),
+                      (mask, (9, 3, 1)), out, None, H, 192, False, None, "auto")
+    lib = _native.lib()
+    need, tc = ctypes.c_size_t(), ctypes.c_int32()
+    assert lib.ouro_attention_plan(ctypes.byref(a), ctypes.byref(need), ctypes.byref(tc)) == 0
+    assert tc.value == 0   # an additive bias runs on the CUDA cores
+    dense = ba._rows_args(torch.zeros((S, H, 128, D), dtype=torch.bfloat16), False,
+                          q.bfloat16(), q.bfloat16(), pt, lens, torch.zeros(S, dtype=torch.int32),
+                          cos, cos, None, None, torch.zeros((S, H, 128, D), dtype=torch.bfloat16),
+                          None, H, 128, True, None, "auto")
+    assert lib.ouro_attention_plan(ctypes.byref(dense), ctypes.byref(need),
+                                   ctypes.byref(tc)) == 0

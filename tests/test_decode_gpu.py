@@ -319,3 +319,46 @@ def test_scope_skips_disallowed_blocks_vs_oracle(cuda, split_blocks):
                                scope_span=span)
     err = np.abs(out.float().cpu().numpy() - want)
     assert err.max() <= 2e-2 and err.mean() <= 2e-3, (err.max(), err.mean())
+
+
+@pytest.mark.parametrize("kernel", ["tc", "simt"])
+def test_sequence_longer_than_its_row_is_clamped_and_reported(cuda, kernel):
+    """A length above 64 * max_blocks (unchecked call) reads no entry past the row:
+    the kernels take the row's keys only and set status bit 1; a max_seq_blocks bound
+    below a sequence's blocks does the same at that bound."""
+    c = _random_case(31, [1000, 300, 640], 16, 2, 128, torch.bfloat16)
+    max_b = c["pt"].shape[1]                       # 16 blocks: sequence 0's full row
+    long = c["lens"].copy()
+    long[0] = 64 * max_b + 1                       # one key past the row
+    pos = np.asarray([999, 299, 639], np.int32)
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    out = _run(dict(c, lens=long), validate=False, status=status, kernel=kernel,
+               positions=torch.from_numpy(pos).cuda(), split_blocks=3)
+    torch.cuda.synchronize()
+    assert int(status.item()) & 1
+    clamped = long.copy()
+    clamped[0] = 64 * max_b
+    _close_half(out, _oracle(dict(c, lens=clamped), positions=pos), f"row clamp {kernel}")
+    # the host bound: no sequence past 10 blocks (sequence 0 has 16)
+    status.zero_()
+    out = _run(c, validate=False, status=status, kernel=kernel, max_seq_blocks=10,
+               total_blocks=10 + 5 + 10)
+    torch.cuda.synchronize()
+    assert int(status.item()) & 1
+    capped = np.minimum(c["lens"], 640)
+    _close_half(out, _oracle(dict(c, lens=capped), positions=c["lens"] - 1), f"cap {kernel}")
+
+
+def test_total_blocks_hint_plans_from_the_real_work(cuda):
+    """A wide table holding short chains: with total_blocks the planner sizes the
+    chunks from the batch's blocks, not from the width; the rows still match."""
+    rng = random.Random(41)
+    lens = [rng.randint(64, 900) for _ in range(200)] + [30000]
+    c = _random_case(41, lens, 64, 8, 128, torch.bfloat16)
+    args = [torch.from_numpy(c[x]).cuda() if isinstance(c[x], np.ndarray) else c[x].cuda()
+            for x in ("pt", "q", "k", "v", "lens", "cos", "sin")]
+    blind = ba.DecodeCall(*args)
+    total = int(sum(-(-n // 64) for n in lens))
+    aware = ba.DecodeCall(*args, total_blocks=total, max_seq_blocks=c["pt"].shape[1])
+    assert aware.plan["split_blocks"] < blind.plan["split_blocks"]
+    _close_half(aware.launch(), _oracle(c), "planned from total_blocks")

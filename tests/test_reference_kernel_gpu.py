@@ -82,3 +82,21 @@ def test_matches_reference_triton_with_a_token_scope_bias(cuda, ref):
     c = dict(lens=lens, rows=rows, q_cache=q, k_cache=k, v_cache=v, cos=cos, sin=sin)
     mx, mean = _run_both(ref, c, bias=bias.cuda())
     assert mx <= MAX_ABS and mean <= MEAN_ABS, (mx, mean)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("with_mask", [False, True])
+def test_matches_reference_triton_on_the_tensor_core_path(cuda, ref, dtype, with_mask):
+    """Head_dim 128, no bias: this repository's call runs on the tcgen05 kernel."""
+    lens = [700, 1100, 64, 257]
+    bt, heads, rows = cases.scattered_chains(BlockTable, 64, lens, 5)
+    q, k, v = cases.paged_caches(torch, 5, 64, 8, 128, 0.5, dtype)
+    cos, sin = cases.rope_tables_torch(torch, len(rows[0]) * 64, 128, 10000.0)
+    c = dict(lens=lens, rows=rows, q_cache=q, k_cache=k, v_cache=v, cos=cos, sin=sin)
+    kw = {}
+    if with_mask:
+        qb = -(-max(lens) // 64)
+        m = (torch.rand(len(lens), qb, qb, generator=torch.Generator().manual_seed(2)) < 0.6)
+        kw = dict(mask=(m.to(torch.int8) | torch.eye(qb, dtype=torch.int8)).cuda())
+    mx, mean = _run_both(ref, c, **kw)
+    assert mx <= MAX_ABS and mean <= MEAN_ABS, (mx, mean)
