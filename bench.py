@@ -1113,7 +1113,7 @@ def main() -> int:
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--split-blocks", type=int, default=0)
-    ap.add_argument("--kernel", default="auto", choices=["auto", "tc", "tc2", "simt"])
+    ap.add_argument("--kernel", default="auto", choices=["auto", "tc", "tc2", "streamk", "simt"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
     ap.add_argument("--no-prefill", action="store_true",
                     help="skip the chunked-prefill sub-object of the decode line")

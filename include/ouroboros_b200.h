@@ -148,8 +148,13 @@ typedef struct ouro_decode_args {
   int32_t dtype;              /* OURO_F32 / OURO_F16 / OURO_BF16 */
   int32_t split_blocks;       /* blocks per split-K chunk; 0 = chosen from the SM count */
   int32_t causal;             /* 1: keys j <= positions[s] only */
-  int32_t kernel;             /* 0 auto, 1 CUDA cores, 2 tensor cores, 3 tensor cores with
-                                 two CTAs per SM (4 KV heads each; num_kv_heads % 4 == 0) */
+  int32_t kernel;             /* 0 auto (4 when built and split_blocks is 0, else 2 when
+                                 built, else 1), 1 CUDA cores, 2 tensor cores (split-K), 3 tensor
+                                 cores with two CTAs per SM (4 KV heads each; num_kv_heads
+                                 % 4 == 0), 4 tensor cores, stream-K: one persistent CTA per
+                                 SM streams an equal share of the batch's blocks (split_blocks
+                                 > 0 sets the CTAs per KV-head group instead of the SM count;
+                                 the plan reports that count as max_splits) */
   float softmax_scale;        /* <= 0: 1/sqrt(D) */
   /* Optional host-side sizes of the batch, for the split-K plan (0 = unknown).
    * total_blocks: sum over sequences of ceil(keys / 64); the planner sizes the

@@ -34,6 +34,8 @@ struct DecodeParams {
   int32_t split_blocks, max_splits;
   int32_t causal;
   int32_t tc_ctas_per_sm;     // tensor-core kernel: 1 (8 KV heads per CTA) or 2 (4 per CTA)
+  int32_t sk_workers;         // > 0: stream-K tensor-core decode with this many CTAs per
+                              // KV-head group (split_blocks / max_splits unused)
   float scale_log2;           // softmax_scale * log2(e)
 };
 
@@ -72,8 +74,14 @@ __host__ __device__ inline SeqGeom seq_geom(const DecodeParams& p, int s) {
 cudaError_t launch_decode_simt_dtype(const DecodeParams& p, int dtype, cudaStream_t stream);
 cudaError_t launch_decode_combine_dtype(const DecodeParams& p, int dtype, cudaStream_t stream);
 // Returns cudaErrorNotSupported when the shape/dtype has no tensor-core build.
+// With p.sk_workers > 0 it launches the stream-K form (prep, decode, merge).
 cudaError_t launch_decode_tc(const DecodeParams& p, int dtype, cudaStream_t stream);
 bool decode_tc_supported(const DecodeParams& p, int dtype);
+// KV heads one tensor-core CTA takes (8, 4, 2 or 1: the largest dividing Hkv).
+int decode_tc_heads_per_cta(int hkv);
+// Stream-K workspace: partials for (S + P) pieces x 2 warps per KV head, then the
+// block prefix sums [S + 1] and the CTAs' first sequences [P] (int32).
+size_t sk_workspace_bytes(int64_t S, int64_t Hq, int64_t D, int64_t P);
 // first_bad: one device u64, set to ~0 before the launch by the caller.
 cudaError_t launch_validate_page_table(const int32_t* pt, const int32_t* lens, int32_t S,
                                        int32_t max_blocks, int32_t n_phys,

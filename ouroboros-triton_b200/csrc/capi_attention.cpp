@@ -103,6 +103,7 @@ ouro::DecodeParams to_params(const ouro_decode_args* a) {
     fail(OURO_EINVAL, "max_seq_blocks and total_blocks must be >= 0 (0 = unknown)");
   p.blocks_cap = a->max_seq_blocks > 0 ? std::min(a->max_seq_blocks, p.max_blocks) : p.max_blocks;
   p.tc_ctas_per_sm = 1;
+  p.sk_workers = 0;
   return p;
 }
 
@@ -133,20 +134,39 @@ void plan(ouro::DecodeParams& p, const ouro_decode_args* a, bool* use_tc, size_t
         return t;
       }(),
       a->dtype);
-  bool tc = false;
-  if (a->kernel == 0) tc = tc_ok;
-  else if (a->kernel == 2 || a->kernel == 3) {
+  bool tc = false, sk = false;
+  if (a->kernel == 0) {
+    // auto: the stream-K form of the tensor-core kernel whenever it is built (it
+    // beat split-K on every batch measured, 32 to 256 sequences), unless the
+    // caller fixed a split-K chunk size; else CUDA cores
+    tc = tc_ok;
+    sk = tc_ok && a->split_blocks == 0;
+  }
+  else if (a->kernel >= 2 && a->kernel <= 4) {
     if (!tc_ok) fail(OURO_EUNSUPPORTED, "tensor-core decode not built for this dtype/head_dim/group");
     if (a->kernel == 3) {
       if (p.Hkv % 4 != 0)
         fail(OURO_EUNSUPPORTED, "two CTAs per SM need a multiple of 4 KV heads");
       p.tc_ctas_per_sm = 2;
     }
+    sk = a->kernel == 4;
     tc = true;
   } else if (a->kernel != 1) {
     fail(OURO_EINVAL,
-         "kernel selector must be 0 (auto), 1 (cuda cores), 2 (tensor cores) or 3 (tensor "
-         "cores, two CTAs per SM)");
+         "kernel selector must be 0 (auto), 1 (cuda cores), 2 (tensor cores), 3 (tensor "
+         "cores, two CTAs per SM) or 4 (tensor cores, stream-K)");
+  }
+  if (sk) {
+    // One persistent CTA per SM: P CTAs per KV-head group, equal shares of the
+    // blocks (split_blocks > 0 sets P instead).
+    const int groups = p.Hkv / ouro::decode_tc_heads_per_cta(p.Hkv);
+    p.sk_workers = a->split_blocks > 0 ? std::min(a->split_blocks, 65535)
+                                       : std::max(1, num_sms() / std::max(groups, 1));
+    p.split_blocks = 1;  // not used by the stream-K kernel
+    p.max_splits = p.sk_workers;
+    *use_tc = true;
+    *ws_bytes = ouro::sk_workspace_bytes(p.S, p.Hq, p.D, p.sk_workers);
+    return;
   }
   int split = a->split_blocks > 0 ? a->split_blocks
                                   : choose_split(p, a->total_blocks, tc, kSplitWaves);
@@ -158,6 +178,26 @@ void plan(ouro::DecodeParams& p, const ouro_decode_args* a, bool* use_tc, size_t
   *ws_bytes = p.max_splits > 1
                   ? static_cast<size_t>(p.S) * p.Hq * p.max_splits * (p.D + 2) * sizeof(float)
                   : 0;
+}
+
+// Launches a planned decode with its workspace (split-K partials, or the
+// stream-K pieces and prefix sums): decode, then the merge when there is one.
+void launch_planned(ouro::DecodeParams& p, int dtype, bool tc, float* workspace,
+                    cudaStream_t st) {
+  if (p.sk_workers > 0) {
+    p.ws_o = workspace;
+    p.ws_ml = workspace + static_cast<size_t>(p.S + p.sk_workers) * 2 * p.Hq * p.D;
+    check_cuda(ouro::launch_decode_tc(p, dtype, st), "decode (tensor cores, stream-K)");
+    return;
+  }
+  if (p.max_splits > 1) {
+    p.ws_o = workspace;
+    p.ws_ml = workspace + static_cast<size_t>(p.S) * p.Hq * p.max_splits * p.D;
+  }
+  if (tc) check_cuda(ouro::launch_decode_tc(p, dtype, st), "decode (tensor cores)");
+  else check_cuda(ouro::launch_decode_simt_dtype(p, dtype, st), "decode (cuda cores)");
+  if (p.max_splits > 1)
+    check_cuda(ouro::launch_decode_combine_dtype(p, dtype, st), "decode combine");
 }
 
 ouro::RowsParams to_rows(const ouro_attention_args* a) {
@@ -292,14 +332,9 @@ int ouro_paged_decode(const ouro_decode_args* args, void* stream) {
         fail(OURO_EINVAL, "decode workspace too small: need " + std::to_string(ws) + " bytes");
       if ((reinterpret_cast<uintptr_t>(args->workspace) & 15u) != 0)
         fail(OURO_EINVAL, "decode workspace must be 16-byte aligned");
-      p.ws_o = static_cast<float*>(args->workspace);
-      p.ws_ml = p.ws_o + static_cast<size_t>(p.S) * p.Hq * p.max_splits * p.D;
     }
-    auto st = static_cast<cudaStream_t>(stream);
-    if (tc) check_cuda(ouro::launch_decode_tc(p, args->dtype, st), "decode (tensor cores)");
-    else check_cuda(ouro::launch_decode_simt_dtype(p, args->dtype, st), "decode (cuda cores)");
-    if (p.max_splits > 1)
-      check_cuda(ouro::launch_decode_combine_dtype(p, args->dtype, st), "decode combine");
+    launch_planned(p, args->dtype, tc, static_cast<float*>(args->workspace),
+                   static_cast<cudaStream_t>(stream));
   })
 }
 
@@ -333,5 +368,9 @@ void decode_plan(DecodeParams& p, const ouro_decode_args* a, bool* use_tc, size_
 }
 
 void cuda_check(cudaError_t e, const char* what) { check_cuda(e, what); }
+
+void decode_launch(DecodeParams& p, int dtype, bool tc, float* workspace, cudaStream_t st) {
+  launch_planned(p, dtype, tc, workspace, st);
+}
 
 }  // namespace ouro::capi

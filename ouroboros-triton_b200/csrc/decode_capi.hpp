@@ -16,5 +16,7 @@ DecodeParams decode_params(const ouro_decode_args* a);
 void decode_plan(DecodeParams& p, const ouro_decode_args* a, bool* use_tc, size_t* ws_bytes);
 // Throws CapiError(OURO_ECUDA) carrying the CUDA error text.
 void cuda_check(cudaError_t e, const char* what);
+// Launches a planned decode (and its merge) with `workspace` of the planned size.
+void decode_launch(DecodeParams& p, int dtype, bool tc, float* workspace, cudaStream_t st);
 
 }  // namespace ouro::capi

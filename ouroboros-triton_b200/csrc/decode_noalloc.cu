@@ -73,6 +73,12 @@ extern "C" int ouro_paged_decode_noalloc(const ouro_decode_args* args, void* str
     bool tc = false;
     size_t ws = 0;
     ouro::capi::decode_plan(p, &a, &tc, &ws);
+    if (ws > kScratchBytes && p.sk_workers > 0) {
+      // the stream-K pieces do not fit: plan the split-K tensor-core kernel instead
+      a.kernel = 2;
+      p = ouro::capi::decode_params(&a);
+      ouro::capi::decode_plan(p, &a, &tc, &ws);
+    }
     if (ws > kScratchBytes) {
       if (args->split_blocks > 0)
         fail(OURO_EINVAL, "split-K partials need " + std::to_string(ws) +
@@ -95,15 +101,7 @@ extern "C" int ouro_paged_decode_noalloc(const ouro_decode_args* args, void* str
       if (ws > kScratchBytes) fail(OURO_EINVAL, "decode does not fit the static scratch");
     }
     if (p.S == 0) return OURO_OK;
-    if (ws > 0) {
-      float* base = scratch_on_current_device();
-      p.ws_o = base;
-      p.ws_ml = base + static_cast<size_t>(p.S) * p.Hq * p.max_splits * p.D;
-    }
-    auto st = static_cast<cudaStream_t>(stream);
-    if (tc) ouro::capi::cuda_check(ouro::launch_decode_tc(p, a.dtype, st), "decode (tensor cores)");
-    else ouro::capi::cuda_check(ouro::launch_decode_simt_dtype(p, a.dtype, st), "decode (cuda cores)");
-    if (p.max_splits > 1)
-      ouro::capi::cuda_check(ouro::launch_decode_combine_dtype(p, a.dtype, st), "decode combine");
+    float* base = ws > 0 ? scratch_on_current_device() : nullptr;
+    ouro::capi::decode_launch(p, a.dtype, tc, base, static_cast<cudaStream_t>(stream));
   })
 }

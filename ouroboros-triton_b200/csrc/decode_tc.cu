@@ -116,6 +116,155 @@ __device__ __forceinline__ void issue_stage(const CUtensorMap* tm_k, const CUten
   if (p.scope_tags) bulk_load(tag_dst, p.scope_tags + s * p.scope_stride + pos_row, 16, full);
 }
 
+// Q^T as the mma B operand for the G query heads of KV head kvh of sequence s:
+// rotated at position pos, scaled by softmax_scale * log2(e). Lane (r, q4) holds
+// head r's column pairs; heads r >= G are zero.
+template <typename T, int D>
+__device__ __forceinline__ void load_q_frag(const DecodeParams& p, int s, int pos, int kvh,
+                                            int lane, uint32_t (&qf)[D / 16][2]) {
+  using MK = MmaKind<T>;
+  constexpr int HALF_KC = D / 32;
+  const int r = lane >> 2, q4 = lane & 3;
+  const T* qrow = static_cast<const T*>(p.q) + (static_cast<int64_t>(s) * p.Hq + kvh * p.G + r) * D;
+  const bool live = r < p.G;
+  const bool pos_ok = pos >= 0 && pos < p.max_pos;
+#pragma unroll
+  for (int kc = 0; kc < HALF_KC; ++kc) {
+#pragma unroll
+    for (int hh = 0; hh < 2; ++hh) {
+      const int t = kc * 16 + 2 * q4 + hh * 8;
+      float2 x0 = make_float2(0.f, 0.f), x1 = make_float2(0.f, 0.f);
+      float2 c = make_float2(1.f, 1.f), sn = make_float2(0.f, 0.f);
+      if (live) {
+        x0 = MK::unpack(*reinterpret_cast<const uint32_t*>(qrow + t));
+        x1 = MK::unpack(*reinterpret_cast<const uint32_t*>(qrow + t + D / 2));
+      }
+      if (pos_ok) {
+        c = *reinterpret_cast<const float2*>(p.cos + static_cast<int64_t>(pos) * (D / 2) + t);
+        sn = *reinterpret_cast<const float2*>(p.sin + static_cast<int64_t>(pos) * (D / 2) + t);
+      }
+      const float sc = p.scale_log2;
+      qf[kc][hh] = MK::pack((x0.x * c.x - x1.x * sn.x) * sc, (x0.y * c.y - x1.y * sn.y) * sc);
+      qf[kc + HALF_KC][hh] =
+          MK::pack((x0.x * sn.x + x1.x * c.x) * sc, (x0.y * sn.y + x1.y * c.y) * sc);
+    }
+  }
+}
+
+// One warp's online-softmax state for its KV head: O^T fragments and, per lane,
+// the running max / partial row sum of its two query heads (columns 2 q4, 2 q4 + 1).
+template <int D>
+struct WarpState {
+  float o[D / 16][4];
+  float m0, m1, l0, l1;
+  __device__ __forceinline__ void reset() {
+#pragma unroll
+    for (int i = 0; i < D / 16; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+    m0 = m1 = -INFINITY;
+    l0 = l1 = 0.f;
+  }
+};
+
+// One 16-token stage for one warp: S^T = K . Q^T with RoPE on the K fragments,
+// masks (keys >= kv_len, token scope), online softmax in base 2, O^T += V^T . P^T.
+// key0 is the stage's first key position; tags (16 bytes) the stage's GLOBAL tags.
+template <typename T, int D, int HPC>
+__device__ __forceinline__ void stage_math(const DecodeParams& p, const uint8_t* stg, int head,
+                                           int lane, const uint32_t (&qf)[D / 16][2],
+                                           WarpState<D>& w, int key0, int kv_len,
+                                           const uint8_t* tags, int lo, int hi) {
+  using L = TcLayout<D, HPC>;
+  using MK = MmaKind<T>;
+  constexpr int KC = D / 16;
+  constexpr int HALF_KC = KC / 2;
+  const int r = lane >> 2, q4 = lane & 3;
+  const int k_row = (lane & 7) + ((lane >> 3) & 1) * 8, k_chunk = lane >> 4;
+  const int v_row = (lane & 7) + (lane >> 4) * 8, v_chunk = (lane >> 3) & 1;
+  const uint32_t kbase = smem_u32(stg + L::kK + head * (kTok * 128));
+  const uint32_t vbase = smem_u32(stg + L::kV + head * (kTok * 128));
+  constexpr int kBoxStride = HPC * kTok * 128;  // between the 64-column halves
+  const uint8_t* cosb = stg + L::kCos;
+  const uint8_t* sinb = stg + L::kSin;
+
+  // S^T = K . Q^T over chunk pairs (kc, kc + D/32): the pair holds the
+  // half-split RoPE partners, rotated in registers right after ldmatrix.
+  float sa[4] = {0.f, 0.f, 0.f, 0.f}, sb[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+  for (int kc = 0; kc < HALF_KC; ++kc) {
+    uint32_t ka[4], kb[4];
+    {
+      const int kc2 = kc + HALF_KC;
+      ldmatrix_x4(kbase + (kc >> 2) * kBoxStride + swz128(k_row, (kc & 3) * 2 + k_chunk),
+                  ka[0], ka[1], ka[2], ka[3]);
+      ldmatrix_x4(kbase + (kc2 >> 2) * kBoxStride + swz128(k_row, (kc2 & 3) * 2 + k_chunk),
+                  kb[0], kb[1], kb[2], kb[3]);
+    }
+#pragma unroll
+    for (int reg = 0; reg < 4; ++reg) {
+      const int row = r + (reg & 1) * 8;
+      const int t = kc * 16 + 2 * q4 + (reg & 2) * 4;
+      const uint32_t off = swz128(row * L::kTBoxes + (t >> 5), (t & 31) >> 2) + (t & 3) * 4;
+      const uint64_t c2 = *reinterpret_cast<const uint64_t*>(cosb + off);
+      const uint64_t s2 = *reinterpret_cast<const uint64_t*>(sinb + off);
+      const uint64_t lo2 = MK::unpack2(ka[reg]);
+      const uint64_t hi2 = MK::unpack2(kb[reg]);
+      // (lo, hi) -> (lo c - hi s, lo s + hi c), two lanes of fp32 per instruction
+      ka[reg] = MK::pack2(f2sub(f2mul(lo2, c2), f2mul(hi2, s2)));
+      kb[reg] = MK::pack2(f2fma(lo2, s2, f2mul(hi2, c2)));
+    }
+    MK::mma(sa, ka, qf[kc][0], qf[kc][1]);
+    MK::mma(sb, kb, qf[kc + HALF_KC][0], qf[kc + HALF_KC][1]);
+  }
+  float sacc[4] = {sa[0] + sb[0], sa[1] + sb[1], sa[2] + sb[2], sa[3] + sb[3]};
+
+  const int j0 = key0 + r;
+  const int j1 = j0 + 8;
+  const bool ok0 = j0 < kv_len && scope_ok(p, tags, r, j0, lo, hi);
+  const bool ok1 = j1 < kv_len && scope_ok(p, tags, r + 8, j1, lo, hi);
+  if (!ok0) sacc[0] = sacc[1] = -INFINITY;
+  if (!ok1) sacc[2] = sacc[3] = -INFINITY;
+
+  float mx0 = fmaxf(sacc[0], sacc[2]), mx1 = fmaxf(sacc[1], sacc[3]);
+#pragma unroll
+  for (int sh = 4; sh < 32; sh <<= 1) {
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, sh));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, sh));
+  }
+  const float mn0 = fmaxf(w.m0, mx0), mn1 = fmaxf(w.m1, mx1);
+  const float base0 = mn0 == -INFINITY ? 0.f : mn0;
+  const float base1 = mn1 == -INFINITY ? 0.f : mn1;
+  const float p00 = exp2f(sacc[0] - base0), p01 = exp2f(sacc[1] - base1);
+  const float p10 = exp2f(sacc[2] - base0), p11 = exp2f(sacc[3] - base1);
+  // Rescale the running sums only when some head's max moved (rare after a few stages).
+  if (__any_sync(0xffffffffu, mn0 != w.m0 || mn1 != w.m1)) {
+    const float a0 = exp2f(w.m0 - base0), a1 = exp2f(w.m1 - base1);
+    w.l0 *= a0;
+    w.l1 *= a1;
+#pragma unroll
+    for (int mt = 0; mt < KC; ++mt) {
+      w.o[mt][0] *= a0;
+      w.o[mt][1] *= a1;
+      w.o[mt][2] *= a0;
+      w.o[mt][3] *= a1;
+    }
+    w.m0 = mn0;
+    w.m1 = mn1;
+  }
+  w.l0 += p00 + p10;
+  w.l1 += p01 + p11;
+  const uint32_t pb0 = movmatrix_trans(MK::pack(p00, p01));
+  const uint32_t pb1 = movmatrix_trans(MK::pack(p10, p11));
+
+  // O^T += V^T . P^T
+#pragma unroll
+  for (int mt = 0; mt < KC; ++mt) {
+    const int box = mt >> 2, chunk = (mt & 3) * 2 + v_chunk;
+    uint32_t vf[4];
+    ldmatrix_x4_trans(vbase + box * kBoxStride + swz128(v_row, chunk), vf[0], vf[1], vf[2], vf[3]);
+    MK::mma(w.o[mt], vf, pb0, pb1);
+  }
+}
+
 template <typename T, int D, int HPC, int MINB>
 __global__ void __launch_bounds__(HPC * kWph * 32, MINB)
     decode_tc_kernel(const __grid_constant__ CUtensorMap tm_k,
@@ -505,6 +654,480 @@ __global__ void __launch_bounds__(HPC * kWph * 32, MINB)
 }
 
 // ---------------------------------------------------------------------------
+// Stream-K decode: persistent CTAs over equal shares of the batch's blocks
+// ---------------------------------------------------------------------------
+// The batch's blocks, sequence after sequence, form one flat range of T blocks
+// (cum[s] = blocks of the sequences before s). CTA c of a KV-head group takes
+// blocks [c T / P, (c + 1) T / P): every CTA streams the same number of blocks
+// whatever the lengths, one CTA per SM, and its stage ring runs on across the
+// sequences its share touches (no wave quantisation, no per-chunk prologue).
+// The piece of sequence s inside CTA c has the id s + c (each CTA boundary and
+// each sequence boundary adds one piece, so ids are unique and below S + P).
+// Each consumer warp writes its online-softmax state for each piece of its CTA
+// to slot (piece, sub); decode_sk_combine_kernel merges the slots of every
+// sequence's pieces into the output row.
+//
+// Warp 0 lists a window of the share at a time: up to kSkMaxSeg pieces and
+// kSkMaxList blocks (block id, physical id and piece index per entry, blocks
+// without an allowed key dropped as in decode_tc_kernel). A sequence cut by a
+// window boundary keeps its warps' state in registers into the next window.
+constexpr int kSkMaxList = 768;
+constexpr int kSkMaxSeg = 48;
+
+struct SkWork {
+  const int32_t* cum;        // [S + 1]: blocks before sequence s (cum[S] = T)
+  const int32_t* first_seq;  // [P]: the sequence holding CTA c's first block
+  float* ws_o;               // [(S + P) * 2][Hq][D] unnormalised partial outputs
+  float* ws_ml;              // [(S + P) * 2][Hq][2] (running max in log2 units, sum)
+  int32_t P;                 // CTAs per KV-head group
+};
+
+struct SkSeg {
+  int32_t s, e_lo, e_hi;     // sequence; list entries [e_lo, e_hi) of the window
+  int32_t kv_len, pos, piece;
+  int32_t cont_in, cont_out; // continues this CTA's state from the previous window / into the next
+};
+static_assert(sizeof(SkSeg) == 32, "segment record");
+
+// Lists one window of CTA c's share, starting at sequence *walk_s, flat block
+// *walk_flat, into segs / list_b (piece index << 24 | block) / list_p; called by
+// all 32 lanes of warp 0. Returns the number of pieces; *n_items the entries.
+__device__ __forceinline__ int sk_build_window(const DecodeParams& p, const SkWork& w, int c,
+                                               int64_t flat_hi, bool carry_in, SkSeg* segs,
+                                               int32_t* list_b, int32_t* list_p, int* walk_s,
+                                               int64_t* walk_flat, int* n_items, bool* carry_out) {
+  const int lane = threadIdx.x & 31;
+  int s = *walk_s;
+  int64_t flat = *walk_flat;
+  int nseg = 0, n = 0;
+  bool cut = false, done = false;
+  while (!done) {
+    // lanes look up the block ranges of the next 32 sequences at once
+    const int si = s + lane;
+    const int64_t lo_i = si < p.S ? w.cum[si] : INT64_MAX;
+    const int64_t hi_i = si < p.S ? w.cum[si + 1] : INT64_MAX;
+    int j = 0;
+    for (; j < 32; ++j) {
+      if (s + j >= p.S) {
+        done = true;
+        break;
+      }
+      const int64_t base = __shfl_sync(0xffffffffu, lo_i, j);
+      const int64_t a = max(base, flat);
+      const int64_t bnd = min(__shfl_sync(0xffffffffu, hi_i, j), flat_hi);
+      if (a >= flat_hi) {  // past this CTA's share
+        done = true;
+        break;
+      }
+      if (a >= bnd) continue;  // a sequence without blocks
+      if (nseg == kSkMaxSeg || n == kSkMaxList) {  // window full at a sequence boundary
+        done = true;
+        break;
+      }
+      const int sj = s + j;
+      const SeqGeom g = seq_geom(p, sj);
+      const int b0 = static_cast<int>(a - base), b1 = static_cast<int>(bnd - base);
+      const int qb = g.pos >= 0 ? g.pos / kBlock : 0;
+      int sc_lo = 0, sc_hi = 0;
+      const uint8_t* sc_row = nullptr;
+      if (p.scope_tags != nullptr) {
+        sc_row = p.scope_tags + static_cast<int64_t>(sj) * p.scope_stride;
+        if (p.scope_span) {
+          sc_lo = p.scope_span[2 * sj];
+          sc_hi = p.scope_span[2 * sj + 1];
+        }
+      }
+      const int e_lo = n;
+      int b = b0;
+      while (b < b1 && n < kSkMaxList) {
+        const int cnt = min(32, min(b1 - b, kSkMaxList - n));  // all kept still fits
+        const int blk = b + lane;
+        bool keep = lane < cnt;
+        int phys = 0;
+        if (keep && p.block_mask != nullptr)
+          keep = p.block_mask[sj * p.mask_s + qb * p.mask_q + blk * p.mask_k] != 0;
+        if (keep && sc_row != nullptr &&
+            !(blk * kBlock < sc_hi && (blk + 1) * kBlock > sc_lo)) {
+          uint32_t any = 0;
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const int64_t off = static_cast<int64_t>(blk) * kBlock + 16 * q;
+            if (off < p.scope_stride) {
+              const uint4 t = *reinterpret_cast<const uint4*>(sc_row + off);
+              any |= t.x | t.y | t.z | t.w;
+            }
+          }
+          keep = any != 0;
+        }
+        if (keep) {
+          phys = p.page_table[static_cast<int64_t>(sj) * p.max_blocks + blk];
+          if (phys < 0 || phys >= p.n_phys) {
+            if (p.status) atomicOr(p.status, kStatusBadPageEntry);
+            keep = false;
+          }
+        }
+        const unsigned bal = __ballot_sync(0xffffffffu, keep);
+        const int rank = __popc(bal & ((1u << lane) - 1u));
+        if (keep) {
+          list_b[n + rank] = (nseg << 24) | blk;
+          list_p[n + rank] = phys;
+        }
+        n += __popc(bal);
+        b += cnt;
+      }
+      if (lane == 0) {
+        SkSeg sg;
+        sg.s = sj;
+        sg.e_lo = e_lo;
+        sg.e_hi = n;
+        sg.kv_len = g.kv_len;
+        sg.pos = g.pos;
+        sg.piece = sj + c;
+        sg.cont_in = (nseg == 0 && carry_in) ? 1 : 0;
+        sg.cont_out = b < b1 ? 1 : 0;
+        segs[nseg] = sg;
+      }
+      ++nseg;
+      flat = base + b;
+      if (b < b1) {  // the list filled inside this sequence: the next window resumes here
+        cut = true;
+        done = true;
+        break;
+      }
+      if (flat >= flat_hi) {  // the share ends with this sequence
+        ++j;
+        done = true;
+        break;
+      }
+    }
+    s += j;
+  }
+  __syncwarp();
+  *walk_s = s;
+  *walk_flat = flat;
+  *n_items = n;
+  *carry_out = cut;
+  return nseg;
+}
+
+template <typename T, int D, int HPC>
+__global__ void __launch_bounds__(HPC * kWph * 32, 1)
+    decode_sk_kernel(const __grid_constant__ CUtensorMap tm_k,
+                     const __grid_constant__ CUtensorMap tm_v,
+                     const __grid_constant__ CUtensorMap tm_cos,
+                     const __grid_constant__ CUtensorMap tm_sin, const DecodeParams p,
+                     const SkWork w) {
+  using L = TcLayout<D, HPC>;
+  constexpr int S_ = L::kStages;
+  constexpr int KC = D / 16;
+  constexpr int kConsumers = HPC * kWph;
+
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint8_t* stages = smem;
+  uint64_t* full = reinterpret_cast<uint64_t*>(stages + S_ * L::kStage);
+  uint32_t* released = reinterpret_cast<uint32_t*>(full + S_);
+  uint8_t* tags = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(released + S_) + 15) & ~static_cast<uintptr_t>(15));
+  int32_t* list_b = reinterpret_cast<int32_t*>(tags + S_ * 16);
+  int32_t* list_p = list_b + kSkMaxList;
+  SkSeg* segs = reinterpret_cast<SkSeg*>(list_p + kSkMaxList);
+  __shared__ int32_t s_nitems, s_nseg, s_abort_flag, s_issued, s_walk_s, s_carry;
+  __shared__ long long s_walk_flat;
+  __shared__ int32_t s_use[8];
+  volatile int32_t* s_abort = &s_abort_flag;
+  static_assert(L::kStages <= 8, "s_use holds at most 8 stages");
+
+  const int c = blockIdx.x;
+  const int kvh0 = blockIdx.y * HPC;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t T_all = w.cum[p.S];
+  const int64_t flat_lo = static_cast<int64_t>(c) * T_all / w.P;
+  const int64_t flat_hi = static_cast<int64_t>(c + 1) * T_all / w.P;
+  if (flat_lo >= flat_hi) return;  // no blocks for this CTA (CTA-uniform)
+
+  if (threadIdx.x == 0) {
+    s_walk_s = w.first_seq[c];
+    s_walk_flat = flat_lo;
+    s_carry = 0;
+    s_issued = 0;
+    *s_abort = 0;
+    for (int i = 0; i < S_; ++i) {
+      mbar_init(&full[i], 1);
+      released[i] = 0;
+      s_use[i] = -1;
+    }
+    fence_barrier_init();
+  }
+  __syncthreads();
+
+  const int head = warp % HPC;
+  const int sub = warp / HPC;
+  const int kvh = kvh0 + head;
+  const int r = lane >> 2, q4 = lane & 3;
+  const int G = p.G;
+  const uint64_t pol_stream = policy_evict_first(), pol_keep = policy_evict_last();
+
+  WarpState<D> st;
+  st.reset();
+  uint32_t qf[KC][2];
+  int cur_s = -1;  // the sequence whose state st holds across a window boundary
+  int lo = 0, hi = 0;
+  int it_base = 0;  // stage iterations of the earlier windows
+  bool ok = true;
+
+  while (true) {
+    if (warp == 0) {
+      int ws = s_walk_s;
+      int64_t wf = s_walk_flat;
+      int nitems = 0;
+      bool carry = false;
+      const int nseg = sk_build_window(p, w, c, flat_hi, s_carry != 0, segs, list_b, list_p, &ws,
+                                       &wf, &nitems, &carry);
+      if (lane == 0) {
+        s_nseg = nseg;
+        s_nitems = nitems;
+        s_walk_s = ws;
+        s_walk_flat = wf;
+        s_carry = carry ? 1 : 0;
+        const int total = nitems * 4;
+        for (int i = 0; i < S_ && i < total; ++i) {
+          const int git = it_base + i;
+          const int e = i >> 2;
+          issue_stage<D, HPC>(&tm_k, &tm_v, &tm_cos, &tm_sin, p, stages + (git % S_) * L::kStage,
+                              &full[git % S_], tags + (git % S_) * 16, &s_use[git % S_], git / S_,
+                              segs[list_b[e] >> 24].s, kvh0, list_b[e] & 0xffffff, list_p[e],
+                              i & 3, pol_stream, pol_keep);
+          s_issued = git + 1;
+        }
+      }
+    }
+    __syncthreads();
+    const int nseg = s_nseg;
+    const int total = s_nitems * 4;
+    if (nseg == 0) break;
+
+    for (int k = 0; k < nseg && ok; ++k) {
+      const SkSeg sg = segs[k];
+      if (!(sg.cont_in && cur_s == sg.s)) {
+        load_q_frag<T, D>(p, sg.s, sg.pos, kvh, lane, qf);
+        st.reset();
+        lo = hi = 0;
+        if (p.scope_span) {
+          lo = p.scope_span[2 * sg.s];
+          hi = p.scope_span[2 * sg.s + 1];
+        }
+      }
+      cur_s = sg.s;
+      int i = 4 * sg.e_lo;
+      if (((it_base + i) & 1) != sub) ++i;
+      for (; i < 4 * sg.e_hi; i += kWph) {
+        const int git = it_base + i;
+        const int sti = git % S_;
+        if (!wait_use(&s_use[sti], git / S_) || !mbar_wait(&full[sti], (git / S_) & 1)) {
+          if (lane == 0 && p.status) atomicOr(p.status, kStatusWaitTimeout);
+          ok = false;
+          break;
+        }
+        const int blk = list_b[i >> 2] & 0xffffff;
+        stage_math<T, D, HPC>(p, stages + sti * L::kStage, head, lane, qf, st,
+                              blk * kBlock + (i & 3) * kTok, sg.kv_len, tags + sti * 16, lo, hi);
+        // Release the stage; the last of the HPC warps reading it refills it.
+        __syncwarp();
+        if (lane == 0) {
+          __threadfence_block();
+          const uint32_t done = atomicAdd(&released[sti], 1u) + 1u;
+          const int nx = i + S_;
+          if (done == static_cast<uint32_t>(HPC) * (git / S_ + 1) && nx < total && !*s_abort) {
+            __threadfence_block();
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            const int e = nx >> 2;
+            issue_stage<D, HPC>(&tm_k, &tm_v, &tm_cos, &tm_sin, p, stages + sti * L::kStage,
+                                &full[sti], tags + sti * 16, &s_use[sti], (it_base + nx) / S_,
+                                segs[list_b[e] >> 24].s, kvh0, list_b[e] & 0xffffff, list_p[e],
+                                nx & 3, pol_stream, pol_keep);
+            atomicMax(&s_issued, it_base + nx + 1);
+          }
+        }
+      }
+      if (!ok) break;
+      if (!sg.cont_out) {
+        // This warp's state for the piece: row sums finished over the 8 token rows.
+        float l0 = st.l0, l1 = st.l1;
+#pragma unroll
+        for (int sh = 4; sh < 32; sh <<= 1) {
+          l0 += __shfl_xor_sync(0xffffffffu, l0, sh);
+          l1 += __shfl_xor_sync(0xffffffffu, l1, sh);
+        }
+        const int ha = 2 * q4, hb = 2 * q4 + 1;
+        const int64_t slot = static_cast<int64_t>(sg.piece) * kWph + sub;
+        const int64_t row_a = slot * p.Hq + kvh * G + ha, row_b = row_a + 1;
+#pragma unroll
+        for (int mt = 0; mt < KC; ++mt) {
+          const int d0 = mt * 16 + r, d1 = d0 + 8;
+          if (ha < G) {
+            w.ws_o[row_a * D + d0] = st.o[mt][0];
+            w.ws_o[row_a * D + d1] = st.o[mt][2];
+          }
+          if (hb < G) {
+            w.ws_o[row_b * D + d0] = st.o[mt][1];
+            w.ws_o[row_b * D + d1] = st.o[mt][3];
+          }
+        }
+        if (r == 0) {
+          if (ha < G) {
+            w.ws_ml[row_a * 2] = st.m0;
+            w.ws_ml[row_a * 2 + 1] = l0;
+          }
+          if (hb < G) {
+            w.ws_ml[row_b * 2] = st.m1;
+            w.ws_ml[row_b * 2 + 1] = l1;
+          }
+        }
+        cur_s = -1;
+      }
+    }
+    if (!ok) *s_abort = 1;
+    it_base += total;
+    __syncthreads();  // every stage of the window consumed: its lists may be rebuilt
+    if (*s_abort) break;
+    if (s_walk_flat >= flat_hi) break;
+  }
+
+  // A wait that gave up leaves copies in flight: wait (bounded) for them before exit.
+  if (*s_abort && threadIdx.x == 0) {
+    const int issued = s_issued;
+    for (int i = max(0, issued - S_); i < issued; ++i)
+      if (!mbar_wait(&full[i % S_], (i / S_) & 1)) break;
+  }
+  (void)kConsumers;
+}
+
+// Blocks per sequence (seq_geom, keys clamped to the row) and their prefix sums
+// into cum[0..S]; then, for each of the P CTAs of a KV-head group, the sequence
+// that holds its first block. One CTA of 1024 threads.
+__global__ void __launch_bounds__(1024) decode_sk_prep_kernel(const DecodeParams p,
+                                                              int32_t* cum, int32_t* first_seq,
+                                                              int32_t P) {
+  __shared__ int32_t warp_sum[32];
+  __shared__ int32_t carry;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  if (tid == 0) {
+    carry = 0;
+    cum[0] = 0;
+  }
+  __syncthreads();
+  for (int base = 0; base < p.S; base += 1024) {
+    const int s = base + tid;
+    int v = s < p.S ? seq_geom(p, s).nb : 0;
+#pragma unroll
+    for (int sh = 1; sh < 32; sh <<= 1) {
+      const int t = __shfl_up_sync(0xffffffffu, v, sh);
+      if (lane >= sh) v += t;
+    }
+    if (lane == 31) warp_sum[warp] = v;
+    __syncthreads();
+    if (warp == 0) {
+      int x = warp_sum[lane];
+#pragma unroll
+      for (int sh = 1; sh < 32; sh <<= 1) {
+        const int t = __shfl_up_sync(0xffffffffu, x, sh);
+        if (lane >= sh) x += t;
+      }
+      warp_sum[lane] = x;
+    }
+    __syncthreads();
+    const int incl = v + (warp > 0 ? warp_sum[warp - 1] : 0) + carry;
+    if (s < p.S) cum[s + 1] = incl;
+    __syncthreads();
+    if (tid == 1023) carry = incl;
+    __syncthreads();
+  }
+  const int64_t T_all = carry;
+  for (int c = tid; c < P; c += 1024) {
+    const int64_t x = static_cast<int64_t>(c) * T_all / P;
+    int lo_s = 0, hi_s = p.S > 0 ? p.S - 1 : 0;
+    while (lo_s < hi_s) {  // largest s with cum[s] <= x
+      const int mid = (lo_s + hi_s + 1) >> 1;
+      if (cum[mid] <= x) lo_s = mid;
+      else hi_s = mid - 1;
+    }
+    first_seq[c] = lo_s;
+  }
+}
+
+// Merges the slots of every piece of a sequence into its output row: one warp
+// per (sequence, query head), four rows per CTA; a sequence without keys gets
+// zeros. Slots of one row are Hq rows apart (piece-major layout).
+template <typename T>
+__global__ void __launch_bounds__(128) decode_sk_combine_kernel(const DecodeParams p,
+                                                                const SkWork w) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * 4 + (threadIdx.x >> 5);
+  if (row >= static_cast<int64_t>(p.S) * p.Hq) return;  // warp-uniform
+  const int s = static_cast<int>(row / p.Hq), h = static_cast<int>(row % p.Hq);
+  T* out = static_cast<T*>(p.out) + row * p.D;
+  const int64_t T_all = w.cum[p.S];
+  const int64_t a = w.cum[s], b = w.cum[s + 1];
+  int n = 0;
+  int64_t first = 0;
+  if (b > a && T_all > 0) {
+    const int64_t c_first = std::min<int64_t>(((a + 1) * w.P - 1) / T_all, w.P - 1);
+    const int64_t c_last = std::min<int64_t>((b * w.P - 1) / T_all, w.P - 1);
+    n = static_cast<int>(kWph * (c_last - c_first + 1));
+    first = (static_cast<int64_t>(s) + c_first) * kWph;  // slot of (piece s + c_first, sub 0)
+  }
+  const int64_t stride = p.Hq;  // between consecutive slots of one row
+  const float* ml = w.ws_ml + (first * p.Hq + h) * 2;
+  float M = -INFINITY;
+  for (int i = lane; i < n; i += 32) M = fmaxf(M, ml[2 * stride * i]);
+#pragma unroll
+  for (int sh = 16; sh > 0; sh >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, sh));
+  float L = 0.f;
+  if (M != -INFINITY)
+    for (int i = lane; i < n; i += 32) L += ml[2 * stride * i + 1] * exp2f(ml[2 * stride * i] - M);
+#pragma unroll
+  for (int sh = 16; sh > 0; sh >>= 1) L += __shfl_xor_sync(0xffffffffu, L, sh);
+  const float inv = L > 0.f ? 1.f / L : 0.f;
+  const float* po = w.ws_o + (first * p.Hq + h) * p.D;
+  const bool vec = (p.D & 3) == 0;
+  const int per_pass = vec ? 128 : 32;
+  for (int d0 = 0; d0 < p.D; d0 += per_pass) {
+    const int d = d0 + (vec ? 4 * lane : lane);
+    const bool act = d < p.D;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int i0 = 0; i0 < n; i0 += 32) {
+      const int il = i0 + lane;
+      const float wl = (M != -INFINITY && il < n) ? exp2f(ml[2 * stride * il] - M) : 0.f;
+      const int cnt = min(32, n - i0);
+      for (int k = 0; k < cnt; ++k) {
+        const float wk = __shfl_sync(0xffffffffu, wl, k);
+        if (wk == 0.f) continue;  // warp-uniform; an empty slot's values are never read
+        const float* src = po + static_cast<int64_t>(i0 + k) * stride * p.D + d;
+        if (act && vec) {
+          const float4 v = *reinterpret_cast<const float4*>(src);
+          acc.x += wk * v.x;
+          acc.y += wk * v.y;
+          acc.z += wk * v.z;
+          acc.w += wk * v.w;
+        } else if (act) {
+          acc.x += wk * src[0];
+        }
+      }
+    }
+    if (act) {
+      out[d] = static_cast<T>(acc.x * inv);
+      if (vec) {
+        out[d + 1] = static_cast<T>(acc.y * inv);
+        out[d + 2] = static_cast<T>(acc.z * inv);
+        out[d + 3] = static_cast<T>(acc.w * inv);
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
 // Host side
 // ---------------------------------------------------------------------------
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
@@ -588,6 +1211,60 @@ int pick_hpc(int hkv) {
   return 1;
 }
 
+template <int D, int HPC>
+size_t sk_smem_bytes() {
+  using L = TcLayout<D, HPC>;
+  return 1024 + static_cast<size_t>(L::kStages) * L::kStage + L::kStages * sizeof(uint64_t) +
+         L::kStages * sizeof(uint32_t) + 16 + L::kStages * 16 + 2 * sizeof(int32_t) * kSkMaxList +
+         sizeof(SkSeg) * kSkMaxSeg;
+}
+
+// Stream-K launch: the block prefix sums and each CTA's first sequence, the
+// persistent decode (P CTAs per KV-head group), the merge of the pieces. The
+// workspace is laid out as sk_workspace_bytes describes.
+template <typename T, int D, int HPC>
+cudaError_t launch_sk_typed(const DecodeParams& p, CUtensorMapDataType dt, cudaStream_t stream) {
+  CUtensorMap mk, mv, mc, ms;
+  const uint64_t planes = static_cast<uint64_t>(p.n_phys) * p.Hkv;
+  if (!make_map_kv3(&mk, p.k, dt, D, planes, kTok, HPC) ||
+      !make_map_kv3(&mv, p.v, dt, D, planes, kTok, HPC) ||
+      !make_map_tbl3(&mc, p.cos, D / 64, p.max_pos) || !make_map_tbl3(&ms, p.sin, D / 64, p.max_pos))
+    return cudaErrorInvalidValue;
+  SkWork w;
+  w.P = p.sk_workers;
+  w.ws_o = p.ws_o;
+  w.ws_ml = p.ws_ml;
+  int32_t* ints = reinterpret_cast<int32_t*>(
+      p.ws_ml + static_cast<size_t>(p.S + w.P) * kWph * p.Hq * 2);
+  w.cum = ints;
+  w.first_seq = ints + p.S + 1;
+  decode_sk_prep_kernel<<<1, 1024, 0, stream>>>(p, ints, ints + p.S + 1, w.P);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  const size_t smem = sk_smem_bytes<D, HPC>();
+  auto kernel = decode_sk_kernel<T, D, HPC>;
+  e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           static_cast<int>(smem));
+  if (e != cudaSuccess) return e;
+  kernel<<<dim3(w.P, p.Hkv / HPC), HPC * kWph * 32, smem, stream>>>(mk, mv, mc, ms, p, w);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  const dim3 cgrid(static_cast<unsigned>((static_cast<int64_t>(p.S) * p.Hq + 3) / 4));
+  decode_sk_combine_kernel<T><<<cgrid, 128, 0, stream>>>(p, w);
+  return cudaGetLastError();
+}
+
+template <typename T>
+cudaError_t dispatch_sk(const DecodeParams& p, CUtensorMapDataType dt, cudaStream_t stream) {
+  const int hpc = pick_hpc(p.Hkv);
+#define OURO_SK_CASE(DD, HH) \
+  if (p.D == DD && hpc == HH) return launch_sk_typed<T, DD, HH>(p, dt, stream);
+  OURO_SK_CASE(128, 8) OURO_SK_CASE(128, 4) OURO_SK_CASE(128, 2) OURO_SK_CASE(128, 1)
+  OURO_SK_CASE(64, 8) OURO_SK_CASE(64, 4) OURO_SK_CASE(64, 2) OURO_SK_CASE(64, 1)
+#undef OURO_SK_CASE
+  return cudaErrorNotSupported;
+}
+
 template <typename T>
 cudaError_t dispatch_tc(const DecodeParams& p, CUtensorMapDataType dt, cudaStream_t stream) {
   const int hpc = pick_hpc(p.Hkv);
@@ -621,8 +1298,20 @@ bool decode_tc_supported(const DecodeParams& p, int dtype) {
 
 cudaError_t launch_decode_tc(const DecodeParams& p, int dtype, cudaStream_t stream) {
   if (!decode_tc_supported(p, dtype)) return cudaErrorNotSupported;
+  if (p.sk_workers > 0) {
+    if (dtype == 2) return dispatch_sk<__nv_bfloat16>(p, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, stream);
+    return dispatch_sk<__half>(p, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, stream);
+  }
   if (dtype == 2) return dispatch_tc<__nv_bfloat16>(p, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, stream);
   return dispatch_tc<__half>(p, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, stream);
+}
+
+int decode_tc_heads_per_cta(int hkv) { return pick_hpc(hkv); }
+
+size_t sk_workspace_bytes(int64_t S, int64_t Hq, int64_t D, int64_t P) {
+  const size_t floats = static_cast<size_t>(S + P) * kWph * Hq * (D + 2);
+  const size_t ints = static_cast<size_t>(S + 1 + P);
+  return (floats + ints) * 4 + 16;
 }
 
 }  // namespace ouro

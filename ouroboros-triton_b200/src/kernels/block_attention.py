@@ -54,7 +54,8 @@ __all__ = [
     "validate_page_table",
 ]
 
-_KERNELS = {"auto": 0, "simt": 1, "cuda_cores": 1, "tensor_cores": 2, "tc": 2, "tc2": 3}
+_KERNELS = {"auto": 0, "simt": 1, "cuda_cores": 1, "tensor_cores": 2, "tc": 2, "tc2": 3,
+            "streamk": 4}
 
 
 # ---------------------------------------------------------------------------

@@ -96,19 +96,19 @@ def test_noalloc_refuses_an_explicit_split_that_does_not_fit(cuda):
 
 
 def test_noalloc_replans_when_the_default_plan_does_not_fit(cuda):
-    """256 sequences of 47 blocks: the default plan's partials (about 85 MB) exceed the
-    32 MiB array, so the entry point re-plans with fewer, larger chunks; the rows still
-    match the allocating entry point."""
-    lens = [3000] * 256
+    """256 sequences of 94 blocks on the split-K kernel: its default plan's partials
+    (about 51 MB) exceed the 32 MiB array, so the entry point re-plans with fewer,
+    larger chunks; the rows still match the allocating entry point."""
+    lens = [6000] * 256
     pt, q, k, v, lens_t, cos, sin = _case(lens, 64, 8, 128, seed=6)
-    call = ba.DecodeCall(pt, q, k, v, lens_t, cos, sin, total_blocks=256 * 47,
-                         max_seq_blocks=47)
+    call = ba.DecodeCall(pt, q, k, v, lens_t, cos, sin, total_blocks=256 * 94,
+                         max_seq_blocks=94, kernel="tc")
     assert call.plan["workspace_bytes"] > 32 << 20   # the default plan does not fit
     want = call.launch().clone()
     for _ in range(2):
         out = torch.full_like(want, float("nan"))
         args = ba._decode_args(*call._keep[:8], call._keep[8], call._keep[9], False, None, 0,
-                               "auto", out, None, None, 256 * 47, 47)
+                               "tc", out, None, None, 256 * 94, 94)
         _native.check(_native.lib().ouro_paged_decode_noalloc(ctypes.byref(args), _stream()),
                       "noalloc decode")
         torch.cuda.synchronize()
