@@ -339,7 +339,8 @@ def run_ours(args):
         tables = [_shard_table([lens[i] for i in shards[r]], 1234 + r) for r in range(world)]
     sh = DecodeShards(world, rank, device, q_heads=hq, head_dim=d, dtype=torch.bfloat16,
                       placement=placement if rank == 0 else None,
-                      widths=[t[3] for t in tables] if rank == 0 else None)
+                      widths=[t[3] for t in tables] if rank == 0 else None,
+                      exchange=args.exchange)
     if sh.n != len(my_lens):
         raise RuntimeError(f"rank {rank}: shard size {sh.n} != placement {len(my_lens)}")
     if rank == 0:
@@ -356,7 +357,7 @@ def run_ours(args):
         q_batch = (torch.randn((S, hq, d), generator=g, device=device) * 0.5).to(torch.bfloat16)
     status = torch.zeros(1, dtype=torch.int32, device=device)
     my_blocks = sum(-(-n // 64) for n in my_lens)
-    call = DecodeCall(sh.page_table, sh.q, k, v, sh.seq_lens, cos, sin, out=sh.out,
+    call = DecodeCall(sh.page_table, sh.q, k, v, sh.seq_lens, cos, sin, out_ptr=sh.out_ptr,
                       validate=False, split_blocks=args.split_blocks, kernel=args.kernel,
                       status=status, total_blocks=my_blocks, max_seq_blocks=sh.width)
     plan = call.plan
@@ -414,21 +415,30 @@ def run_ours(args):
         st_all = [mine_t]
     statuses = [int(x[0]) for x in st_all]
     rates = [float(x[1]) for x in st_all]
+    xst = torch.tensor([float(sh.exchange_status.item())], dtype=torch.float64, device=device)
+    if world > 1:
+        dist.all_reduce(xst, op=dist.ReduceOp.MAX)
     check = _check_gathered_rows(torch, dist, sh, world, rank, lens, shards, tables, k, v,
                                  cos_np, sin_np, q_batch)
     if rank == 0:
         check["kernel_status"] = statuses
+        check["exchange_status"] = int(xst.item())
     if any(statuses):
         print(f"rank {rank}: decode kernels reported status {statuses}", file=sys.stderr)
 
     e2e = _e2e_sharded(torch, dist, sh, call, world, rank, device, q_batch, args)
     weak = _weak_scaling_leg(torch, dist, world, rank, device, args) if world > 1 else None
     pre = _prefill_leg(args, world, rank, device) if not args.no_prefill else None
+    serv = None
+    if not args.no_serving:
+        if args.serving_rate <= 0:
+            args.serving_rate = 4096.0
+        serv = _serving_leg(args, world, rank, device)
     refk = (_reference_kernel_leg(args, device)
             if (rank == 0 and world == 1 and not args.no_reference_kernel) else None)
     cpu = _cpu_baseline_leg() if (rank == 0 and world == 1 and not args.no_cpu) else None
     peak, peak_kind = _peaks()
-    launches = args.steps * (1 + (1 if plan["max_splits"] > 1 else 0))
+    launches = args.steps * plan["launches"]
     if rank == 0:
         avg_rate = kv_bytes_all / world / (kern_max / 1000.0) / 1e9
         line = {
@@ -439,14 +449,21 @@ def run_ours(args):
             "config": dict({k: x for k, x in WORKLOAD.items() if k != "seqs_per_gpu"}, seqs=S,
                            parallelism=(f"dp{world}: the Supervisor (rank 0) places whole "
                                         "sequences by LPT on tokens; queries, lengths and "
-                                        "page-table rows go out and outputs come back over "
-                                        "NCCL inside every step" if world > 1 else
+                                        "page-table rows go out and outputs come back inside "
+                                        "every step" if world > 1 else
                                         "dp1 (the Supervisor's batch on one GPU)"),
+                           exchange=(("peer memory over NVLink (CUDA IPC; fetch / signal / "
+                                      "collect kernels, bounded flag waits)"
+                                      if sh.exchange == "peer" else "NCCL point-to-point")
+                                     if world > 1 else None),
                            shard_sizes=sh.counts,
                            shard_tokens=[sum(lens[i] for i in shards[r]) for r in range(world)],
                            l2_flush="inputs>L2 (K+V %.1f GB per GPU)" % (kv_bytes_all / world / 1e9),
-                           split_blocks=plan["split_blocks"], max_splits=plan["max_splits"],
-                           kernel="tensor_cores" if plan["tensor_cores"] else "cuda_cores"),
+                           split_blocks=None if plan["stream_k"] else plan["split_blocks"],
+                           max_splits=None if plan["stream_k"] else plan["max_splits"],
+                           stream_k_ctas=plan["max_splits"] if plan["stream_k"] else None,
+                           kernel=("tensor_cores_stream_k" if plan["stream_k"] else
+                                   "tensor_cores" if plan["tensor_cores"] else "cuda_cores")),
             "roofline": {"bound": "hbm", "achieved": avg_rate, "peak": peak, "unit": "GB/s",
                          "frac": avg_rate / peak, "traffic": _traffic_from_profile(world),
                          "peak_source": peak_kind,
@@ -468,9 +485,12 @@ def run_ours(args):
             line["weak_scaling"] = weak
         if pre is not None:
             line["prefill"] = pre
+        if serv is not None:
+            line["serving"] = serv
         if refk is not None:
             line["reference_kernel"] = refk
         print(json.dumps(line), flush=True)
+    sh.close()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -1014,14 +1034,17 @@ SERVING = dict(workload="serving_trace_llama3_8b_attention", requests=512, rate_
                pool_fraction=0.25, seed=17)
 
 
-def run_serving(args):
-    """The serving trace: Poisson arrivals, lognormal prompts, 256 output tokens each,
-    continuous batching through the native allocator, token scopes from random segments.
+def _serving_measure(args, world: int, rank: int, device, rate: float):
+    """The serving trace: Poisson arrivals at ``rate`` per second, lognormal prompts, 256
+    output tokens each, continuous batching through the native allocator, token scopes
+    from random segments.
 
-    Every rank builds the same seeded trace and serves its LPT shard of whole requests on
-    its own GPU (sequence-sharded KV; no collective on the data path). value = all ranks'
-    output tokens / the slowest rank's wall time (arrivals run on the wall clock, so the
-    trace's own 8 s of arrivals bound it from below).
+    Every rank builds the same seeded trace; the Supervisor's placement (LPT on total
+    tokens, ``src.engine.shard_requests``) gives each rank whole requests, served by that
+    GPU's engine (sequence-sharded KV; no collective on the data path). value = all ranks'
+    output tokens / the slowest rank's wall time. At the stated 64 requests/s the trace's
+    own ~8 s of arrivals bound it; a compressed rate (all 512 requests within a fraction
+    of a second) measures the engine.
     """
     import torch
     import torch.distributed as dist
@@ -1030,14 +1053,7 @@ def run_serving(args):
     from src.serving import KVPool
 
     P = SERVING
-    world, rank, local = _dist_env()
-    if world > 1:
-        torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=300),
-                                device_id=torch.device("cuda", local))
-    device = torch.device("cuda", local if world > 1 else 0)
-    torch.cuda.set_device(device)
-    trace = make_trace(P["requests"], P["rate_per_s"], P["prompt_median"], P["prompt_sigma"],
+    trace = make_trace(P["requests"], rate, P["prompt_median"], P["prompt_sigma"],
                        P["prompt_min"], P["prompt_max"], P["output_tokens"], P["seed"])
     mine = shard_requests(trace, world)[rank]
     max_total = P["prompt_max"] + P["output_tokens"]
@@ -1078,26 +1094,50 @@ def run_serving(args):
     if pk.exists():
         peak = float(json.loads(pk.read_text())["hbm_gbs"])
     dec_gbs = be.kv_bytes / (dec_ms / 1000.0) / 1e9 if dec_ms > 0 else None
-    line = {
-        "metric": "serving trace output tokens/s (512 requests, Poisson 64/s, 256 output tokens)",
+    arrivals_s = max(r.arrival for r in trace)
+    kv_rank0 = be.kv_bytes
+    del eng, be, pool
+    torch.cuda.empty_cache()
+    return {
+        "metric": "serving trace output tokens/s (512 requests, Poisson arrivals, 256 output "
+                  "tokens)",
         "value": gen / wall, "unit": "tokens/s", "n_gpus": world, "higher_is_better": True,
         "scaling": "strong", "dtype": "bf16",
         "data": "synthetic (seeded trace; random-init stand-in projections, no dataset)",
-        "config": dict(P, parallelism=f"dp{world} (whole requests per GPU, LPT)",
-                       pool_blocks_rank0=pool_blocks),
+        "config": dict(P, rate_per_s=rate, parallelism=f"dp{world} (whole requests per GPU, "
+                                                       "LPT)", pool_blocks_rank0=pool_blocks,
+                       last_arrival_s=arrivals_s),
         "wall_s": wall, "generated_tokens": gen,
+        "arrival_bound": bool(arrivals_s > 0.5 * wall),
         "rank0": {"requests": st["requests"], "steps": st["steps"], "ttft_s": st["ttft_s"],
                   "tpot_s": st["tpot_s"], "peak_running": st["peak_running"],
                   "peak_blocks": st["peak_blocks"], "prompt_tokens": st["prompt_tokens"],
                   "prefill_attention_ms": pre_ms},
-        "decode_attention": {"timing": "CUDA events around each decode call (decode + combine "
-                                       "kernels and the host gap between their launches)",
-                             "bytes_rank0": be.kv_bytes, "ms_rank0": dec_ms,
+        "decode_attention": {"timing": "CUDA events around each decode call (decode kernels "
+                                       "and the host gap between their launches)",
+                             "bytes_rank0": kv_rank0, "ms_rank0": dec_ms,
                              "GB/s_rank0": dec_gbs, "peak_GB/s": peak,
                              "frac": (dec_gbs / peak) if (dec_gbs and peak) else None,
                              "bytes_all_ranks": kv_total},
         "clocks": clk.summary(),
     }
+
+
+def _serving_leg(args, world: int, rank: int, device):
+    """The serving trace at a compressed arrival rate, as a sub-object of the headline line."""
+    line = _serving_measure(args, world, rank, device, args.serving_rate)
+    return {k: line[k] for k in ("metric", "value", "unit", "scaling", "wall_s",
+                                 "generated_tokens", "arrival_bound", "rank0",
+                                 "decode_attention", "config")}
+
+
+def run_serving(args):
+    import torch.distributed as dist
+
+    world, rank, local = _dist_env()
+    device = _init_dist(world, local, timeout_s=300)
+    line = _serving_measure(args, world, rank, device,
+                            args.serving_rate if args.serving_rate > 0 else SERVING["rate_per_s"])
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:
@@ -1117,6 +1157,15 @@ def main() -> int:
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
     ap.add_argument("--no-prefill", action="store_true",
                     help="skip the chunked-prefill sub-object of the decode line")
+    ap.add_argument("--exchange", choices=["peer", "nccl"], default="peer",
+                    help="how the Supervisor's step moves queries and rows between GPUs "
+                         "(N > 1): peer memory over NVLink, or NCCL point-to-point")
+    ap.add_argument("--serving-rate", type=float, default=0.0,
+                    help="arrivals per second of the serving trace (--workload serving: the "
+                         "stated 64; the headline line's serving leg: 4096, all 512 requests "
+                         "within ~0.13 s, so the engine, not the arrivals, sets the time)")
+    ap.add_argument("--no-serving", action="store_true",
+                    help="skip the serving-trace sub-object of the decode line")
     ap.add_argument("--no-reference-kernel", action="store_true",
                     help="skip the reference Triton kernel comparison (N = 1 only)")
     ap.add_argument("--prefill-steps", type=int, default=0,

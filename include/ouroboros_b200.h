@@ -272,6 +272,50 @@ int ouro_kv_append(const void* k_new, const void* v_new, const int32_t* page_tab
  * ---------------------------------------------------------------------- */
 int ouro_paged_decode_noalloc(const ouro_decode_args* args, void* stream);
 
+/* ------------------------------------------------------------------------
+ * Peer-memory exchange for the sharded decode step (no reference counterpart:
+ * the reference has no multi-GPU code; its Supervisor, src/serving.py:120-329,
+ * owns the KV state these steps serve). One process per GPU. The Supervisor's
+ * rank 0 and every worker rank r > 0 share buffers through CUDA IPC handles
+ * (allocated here; the caller passes the 64-byte handles between processes).
+ * A step: rank 0 publishes the query rows in shard order and raises every
+ * worker's ready flag; worker r fetches its rows and metadata from rank 0 over
+ * NVLink, decodes with its output pointed into rank 0's buffer, and raises its
+ * done flag there; rank 0 collects (restores the batch order). Flags are
+ * uint64 step numbers (monotonic, start from 1 in zeroed buffers), written
+ * with system-scope release and read with acquire. Each wait gives up after
+ * timeout_ns, sets status bit 2 and skips its copy, so a missing rank shows as
+ * an error instead of a hang.
+ * ---------------------------------------------------------------------- */
+#define OURO_IPC_HANDLE_BYTES 64
+
+/* cudaMalloc'd, zeroed device buffer that can be shared by ouro_ipc_handle. */
+int ouro_ipc_alloc(size_t bytes, void** out);
+int ouro_ipc_free(void* ptr);
+/* The buffer's IPC handle (OURO_IPC_HANDLE_BYTES bytes) for another process. */
+int ouro_ipc_handle(void* ptr, void* handle_out);
+/* Maps another process's buffer into this one (peer access enabled lazily). */
+int ouro_ipc_open(const void* handle, void** out);
+int ouro_ipc_close(void* ptr);
+/* Rank 0: q_perm[i] = q[perm[i]] (rows of row_bytes, a multiple of 16), then
+ * *peer_ready[j] = step for j < n_peers (peer_ready: a device array of the
+ * workers' ready-flag addresses as mapped in this process). */
+int ouro_shard_publish(const void* q, const int64_t* perm, void* q_perm, int64_t rows,
+                       int64_t row_bytes, uint64_t* const* peer_ready, int32_t n_peers,
+                       uint64_t step, void* stream);
+/* Worker: wait until *ready >= step, then copy bytes0 from src0 to dst0 and
+ * bytes1 from src1 to dst1 (sources in rank 0's buffer; sizes multiples of 16). */
+int ouro_shard_fetch(const uint64_t* ready, uint64_t step, uint64_t timeout_ns, const void* src0,
+                     void* dst0, int64_t bytes0, const void* src1, void* dst1, int64_t bytes1,
+                     int32_t* status, void* stream);
+/* Worker: *flag = step (a flag in rank 0's buffer), after this stream's earlier work. */
+int ouro_shard_signal(uint64_t* flag, uint64_t step, void* stream);
+/* Rank 0: wait until done[i * flag_stride] >= step for i < n_flags, then
+ * out[i] = src[inv[i]] for the rows. */
+int ouro_shard_collect(const uint64_t* done, int32_t n_flags, int32_t flag_stride, uint64_t step,
+                       uint64_t timeout_ns, const void* src, const int64_t* inv, void* out,
+                       int64_t rows, int64_t row_bytes, int32_t* status, void* stream);
+
 #ifdef __cplusplus
 }  /* extern "C" */
 #endif

@@ -93,6 +93,32 @@ def sharded_step(compute: Callable, world: int, rank: int, device, *, q_shards=N
     return [g[:c] for g, c in zip(gathered, counts)]
 
 
+class _DevBytes:
+    """A device address range as a CUDA-array-interface object (zero-copy torch view)."""
+
+    def __init__(self, ptr: int, nbytes: int):
+        self.__cuda_array_interface__ = {"shape": (nbytes,), "typestr": "|u1",
+                                         "data": (ptr, False), "version": 3}
+
+
+def _view(torch, ptr: int, shape, dtype, device):
+    """A torch tensor over device memory at ``ptr`` (not owned by torch)."""
+    n = 1
+    for x in shape:
+        n *= int(x)
+    nbytes = n * torch.tensor([], dtype=dtype).element_size()
+    if nbytes == 0:
+        return torch.empty(shape, dtype=dtype, device=device)
+    raw = torch.as_tensor(_DevBytes(ptr, nbytes), device=device)
+    if raw.data_ptr() != ptr:
+        raise RuntimeError("could not view the shared buffer without a copy")
+    return raw.view(dtype).view(shape)
+
+
+def _align(x: int, a: int = 256) -> int:
+    return -(-x // a) * a
+
+
 class DecodeShards:
     """Repeated sharded decode of one batch over one process per GPU.
 
@@ -104,27 +130,45 @@ class DecodeShards:
     and page-table width, and every buffer is allocated then. A step is
     collective too and does no host work beyond enqueueing:
 
-      1. rank 0 permutes the queries into shard order (one gather kernel);
-      2. rank 0 sends each rank r > 0 its query rows and its metadata (the
-         shard's lengths followed by its page-table rows, one int32 buffer),
-         NCCL point-to-point in one group; rank 0's own shard is read in place;
+      1. rank 0 permutes the queries into shard order;
+      2. each rank r > 0 gets its query rows and its metadata (the shard's
+         lengths followed by its page-table rows, one int32 buffer); rank 0's
+         own shard is read in place;
       3. every rank runs ``run()``, which must decode ``q`` / ``page_table`` /
-         ``seq_lens`` (the receive buffers below) into ``out``;
-      4. rank 0 receives every shard's output rows in one group and permutes
-         them back to batch order.
+         ``seq_lens`` into the rows at ``out_ptr`` (``out`` is their tensor, None
+         on a worker of the peer exchange, whose rows live in rank 0's buffer);
+      4. rank 0 gets every shard's output rows and restores the batch order.
+
+    Two exchanges. ``exchange="nccl"`` moves steps 2 and 4 as NCCL
+    point-to-point groups (any backend: gloo on CPU ranks). ``exchange="peer"``
+    (CUDA, one GPU per rank) shares buffers through CUDA IPC and moves them with
+    the library's kernels: rank 0's permute writes the rows into its shared
+    buffer and raises every worker's ready flag; a worker's fetch kernel waits
+    for its flag and copies its rows and metadata over NVLink; the worker's
+    decode writes its output rows straight into rank 0's shared buffer, its
+    signal kernel raises its done flag there, and rank 0's collect kernel waits
+    for every flag and restores the batch order. Every wait is bounded
+    (``timeout_s``; status bit 2 in ``exchange_status`` when it runs out).
 
     Every rank calls the same collectives in the same order; every rank must
     hold at least one sequence. The metadata is resent every step because the
     lengths grow by one token per step and a chain gains a block every 64
-    tokens; ``set_meta`` (rank 0) rewrites it.
+    tokens; ``set_meta`` (rank 0) rewrites it. ``close()`` (collective) releases
+    the shared buffers.
     """
 
     def __init__(self, world: int, rank: int, device, *, q_heads: int, head_dim: int, dtype,
-                 placement=None, widths=None, group=None):
+                 placement=None, widths=None, group=None, exchange: str = "nccl",
+                 timeout_s: float = 2.0):
         import torch
         import torch.distributed as dist
 
+        if exchange not in ("nccl", "peer"):
+            raise RuntimeError(f"exchange must be 'nccl' or 'peer', got {exchange!r}")
         self.world, self.rank, self.device, self.group = world, rank, device, group
+        self.exchange = exchange if world > 1 else "nccl"
+        self.timeout_ns = int(timeout_s * 1e9)
+        self.step_no = 0
         hdr = torch.zeros(2 * world, dtype=torch.int64, device=device)
         if rank == 0:
             if placement is None or widths is None or len(widths) != world:
@@ -146,10 +190,13 @@ class DecodeShards:
             raise RuntimeError(f"page-table widths must be >= 1, got {self.widths}")
         self.n, self.width = self.counts[rank], self.widths[rank]
         self.q_off = [sum(self.counts[:r]) for r in range(world)]
-        self.meta_len = [c * (1 + w) for c, w in zip(self.counts, self.widths)]
+        # metadata segments padded to 16 bytes (four int32)
+        self.meta_len = [_align(c * (1 + w), 4) for c, w in zip(self.counts, self.widths)]
         self.meta_off = [sum(self.meta_len[:r]) for r in range(world)]
         S = sum(self.counts)
+        self.S = S
         qshape = (q_heads, head_dim)
+        self.row_bytes = q_heads * head_dim * torch.tensor([], dtype=dtype).element_size()
         if rank == 0:
             order = sorted(range(S), key=lambda i: (int(placement[i]), i))
             self.batch_index = order  # shard-order position -> batch index
@@ -158,20 +205,114 @@ class DecodeShards:
             for pos, i in enumerate(order):
                 inv[i] = pos
             self.inv = torch.tensor(inv, dtype=torch.int64, device=device)
+            self.out_batch = torch.empty((S,) + qshape, dtype=dtype, device=device)
+        self.exchange_status = torch.zeros(1, dtype=torch.int32, device=device)
+        self._own = self._p0 = None
+        self._peers = []
+        if self.exchange == "peer":
+            self._setup_peer(torch, dist, qshape, dtype)
+        elif rank == 0:
             self.q_perm = torch.empty((S,) + qshape, dtype=dtype, device=device)
             self.meta_all = torch.zeros(sum(self.meta_len), dtype=torch.int32, device=device)
             self.out_perm = torch.empty((S,) + qshape, dtype=dtype, device=device)
-            self.out_batch = torch.empty((S,) + qshape, dtype=dtype, device=device)
-            self.q = self.q_perm[:self.n]
-            meta = self.meta_all[:self.meta_len[0]]
-            self.out = self.out_perm[:self.n]
         else:
             self.q = torch.empty((self.n,) + qshape, dtype=dtype, device=device)
-            meta = torch.zeros(self.meta_len[rank], dtype=torch.int32, device=device)
+            self.meta = torch.zeros(self.meta_len[rank], dtype=torch.int32, device=device)
             self.out = torch.empty((self.n,) + qshape, dtype=dtype, device=device)
-        self.meta = meta
-        self.seq_lens = meta[:self.n]
-        self.page_table = meta[self.n:].view(self.n, self.width)
+        if rank == 0:
+            self.q = self.q_perm[:self.n]
+            self.meta = self.meta_all[:self.meta_len[0]]
+            self.out = self.out_perm[:self.n]
+        if self.out is not None:
+            self.out_ptr = self.out.data_ptr()
+        self.seq_lens = self.meta[:self.n]
+        self.page_table = self.meta[self.n:self.n * (1 + self.width)].view(self.n, self.width)
+
+    # -- the peer-memory exchange -------------------------------------------------------
+    def _layout(self):
+        """Byte offsets of rank 0's shared buffer: flags, queries, metadata, outputs."""
+        flags = _align(64 * (self.world + 1))
+        q = flags
+        meta = _align(q + self.S * self.row_bytes)
+        out = _align(meta + sum(self.meta_len) * 4)
+        return flags, q, meta, out, _align(out + self.S * self.row_bytes)
+
+    def _setup_peer(self, torch, dist, qshape, dtype):
+        import ctypes
+
+        from . import _native
+        from .kernels import _capi  # noqa: F401  (registers the exchange symbols)
+
+        lib = _native.lib()
+        flags, q_b, meta_b, out_b, total = self._layout()
+        own = ctypes.c_void_p()
+        _native.check(lib.ouro_ipc_alloc(total if self.rank == 0 else flags, ctypes.byref(own)),
+                      "ipc alloc")
+        self._own = own.value
+        h = (ctypes.c_uint8 * 64)()
+        _native.check(lib.ouro_ipc_handle(self._own, h), "ipc handle")
+        mine = torch.tensor(list(bytes(h)), dtype=torch.uint8, device=self.device)
+        handles = [torch.empty_like(mine) for _ in range(self.world)]
+        dist.all_gather(handles, mine, group=self.group)
+        handles = [bytes(x.cpu().tolist()) for x in handles]
+        dev = self.device
+        if self.rank == 0:
+            for r in range(1, self.world):
+                p = ctypes.c_void_p()
+                buf = (ctypes.c_uint8 * 64).from_buffer_copy(handles[r])
+                _native.check(lib.ouro_ipc_open(buf, ctypes.byref(p)), "ipc open")
+                self._peers.append(p.value)
+            # each worker's ready flag is the first word of its shared buffer
+            self._ready_ptrs = torch.tensor(self._peers, dtype=torch.int64, device=dev)
+            self.q_perm = _view(torch, self._own + q_b, (self.S,) + qshape, dtype, dev)
+            self.meta_all = _view(torch, self._own + meta_b, (sum(self.meta_len),), torch.int32,
+                                  dev)
+            self.out_perm = _view(torch, self._own + out_b, (self.S,) + qshape, dtype, dev)
+        else:
+            p = ctypes.c_void_p()
+            buf = (ctypes.c_uint8 * 64).from_buffer_copy(handles[0])
+            _native.check(lib.ouro_ipc_open(buf, ctypes.byref(p)), "ipc open")
+            self._p0 = p.value
+            r = self.rank
+            self.q = torch.empty((self.n,) + qshape, dtype=dtype, device=dev)
+            self.meta = torch.zeros(self.meta_len[r], dtype=torch.int32, device=dev)
+            # the decode writes this rank's rows straight into rank 0's buffer: a raw
+            # address (out_ptr), since the memory belongs to rank 0's GPU
+            self.out = None
+            self.out_ptr = self._p0 + out_b + self.q_off[r] * self.row_bytes
+            self._src_q = self._p0 + q_b + self.q_off[r] * self.row_bytes
+            self._src_meta = self._p0 + meta_b + self.meta_off[r] * 4
+            self._done_flag = self._p0 + 64 * r
+        torch.cuda.synchronize(dev)
+        dist.barrier(group=self.group)
+
+    def close(self) -> None:
+        """Collective: unmaps the peers' buffers, then frees this rank's shared buffer."""
+        if self.exchange != "peer" or self._own is None:
+            return
+        import torch
+        import torch.distributed as dist
+
+        from . import _native
+
+        lib = _native.lib()
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)
+        for ptr in self._peers + ([self._p0] if self._p0 else []):
+            _native.check(lib.ouro_ipc_close(ptr), "ipc close")
+        self._peers, self._p0 = [], None
+        dist.barrier(group=self.group)
+        _native.check(lib.ouro_ipc_free(self._own), "ipc free")
+        self._own = None
+        for name in ("q_perm", "meta_all", "out_perm", "q", "meta", "out", "seq_lens",
+                     "page_table"):
+            if hasattr(self, name):
+                setattr(self, name, None)
+
+    def _stream(self):
+        import torch
+
+        return torch.cuda.current_stream(self.device).cuda_stream
 
     def shard_of(self, r: int) -> list[int]:
         """Rank 0: the batch indices rank r holds, in its shard order."""
@@ -189,9 +330,10 @@ class DecodeShards:
             if ln.numel() != self.counts[r] or tuple(pt.shape) != (self.counts[r], self.widths[r]):
                 raise RuntimeError(f"rank {r}: lengths / page table do not match the shard "
                                    f"({self.counts[r]} sequences, width {self.widths[r]})")
+            c = self.counts[r]
             seg = self.meta_all[self.meta_off[r]:self.meta_off[r] + self.meta_len[r]]
-            seg[:self.counts[r]].copy_(ln, non_blocking=True)
-            seg[self.counts[r]:].copy_(pt.reshape(-1), non_blocking=True)
+            seg[:c].copy_(ln, non_blocking=True)
+            seg[c:c * (1 + self.widths[r])].copy_(pt.reshape(-1), non_blocking=True)
 
     def _exchange(self, ops) -> None:
         import torch.distributed as dist
@@ -205,6 +347,24 @@ class DecodeShards:
         import torch
         import torch.distributed as dist
 
+        self.step_no += 1
+        if self.exchange == "peer":
+            from . import _native
+
+            lib = _native.lib()
+            if self.rank == 0:
+                q_batch = q_batch.contiguous()
+                _native.check(lib.ouro_shard_publish(
+                    q_batch.data_ptr(), self.perm.data_ptr(), self.q_perm.data_ptr(), self.S,
+                    self.row_bytes, self._ready_ptrs.data_ptr(), self.world - 1, self.step_no,
+                    self._stream()), "shard publish")
+            else:
+                _native.check(lib.ouro_shard_fetch(
+                    self._own, self.step_no, self.timeout_ns, self._src_q, self.q.data_ptr(),
+                    self.n * self.row_bytes, self._src_meta, self.meta.data_ptr(),
+                    self.meta_len[self.rank] * 4, self.exchange_status.data_ptr(),
+                    self._stream()), "shard fetch")
+            return
         ops = []
         if self.rank == 0:
             torch.index_select(q_batch, 0, self.perm, out=self.q_perm)
@@ -225,6 +385,20 @@ class DecodeShards:
         import torch
         import torch.distributed as dist
 
+        dst = (self.out_batch if out is None else out) if self.rank == 0 else None
+        if self.exchange == "peer":
+            from . import _native
+
+            lib = _native.lib()
+            if self.rank != 0:
+                _native.check(lib.ouro_shard_signal(self._done_flag, self.step_no,
+                                                    self._stream()), "shard signal")
+                return None
+            _native.check(lib.ouro_shard_collect(
+                self._own + 64, self.world - 1, 8, self.step_no, self.timeout_ns,
+                self.out_perm.data_ptr(), self.inv.data_ptr(), dst.data_ptr(), self.S,
+                self.row_bytes, self.exchange_status.data_ptr(), self._stream()), "shard collect")
+            return dst
         ops = []
         if self.rank == 0:
             for r in range(1, self.world):
@@ -236,7 +410,6 @@ class DecodeShards:
             self._exchange(ops)
         if self.rank != 0:
             return None
-        dst = self.out_batch if out is None else out
         torch.index_select(self.out_perm, 0, self.inv, out=dst)
         return dst
 

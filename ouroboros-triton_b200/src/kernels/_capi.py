@@ -68,3 +68,18 @@ _native.register("ouro_kv_append", ctypes.c_int,
                  [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _i32, _i32,
                   _vp, _vp])
 _native.register("ouro_paged_decode_noalloc", ctypes.c_int, [ctypes.POINTER(DecodeArgs), _vp])
+
+# Peer-memory exchange of the sharded decode step (src.dist.DecodeShards, exchange="peer").
+_u64 = ctypes.c_uint64
+_native.register("ouro_ipc_alloc", ctypes.c_int, [ctypes.c_size_t, ctypes.POINTER(_vp)])
+_native.register("ouro_ipc_free", ctypes.c_int, [_vp])
+_native.register("ouro_ipc_handle", ctypes.c_int, [_vp, _vp])
+_native.register("ouro_ipc_open", ctypes.c_int, [_vp, ctypes.POINTER(_vp)])
+_native.register("ouro_ipc_close", ctypes.c_int, [_vp])
+_native.register("ouro_shard_publish", ctypes.c_int,
+                 [_vp, _vp, _vp, _i64, _i64, _vp, _i32, _u64, _vp])
+_native.register("ouro_shard_fetch", ctypes.c_int,
+                 [_vp, _u64, _u64, _vp, _vp, _i64, _vp, _vp, _i64, _vp, _vp])
+_native.register("ouro_shard_signal", ctypes.c_int, [_vp, _u64, _vp])
+_native.register("ouro_shard_collect", ctypes.c_int,
+                 [_vp, _i32, _i32, _u64, _u64, _vp, _vp, _vp, _i64, _i64, _vp, _vp])

@@ -257,8 +257,12 @@ def decode_plan(args: "_capi.DecodeArgs") -> dict:
     _native.check(_native.lib().ouro_decode_plan(ctypes.byref(args), ctypes.byref(split),
                                                  ctypes.byref(nsplit), ctypes.byref(ws),
                                                  ctypes.byref(tc)), "decode plan")
+    tc_used = bool(tc.value)
+    # the library takes the stream-K form when asked for it, or on auto without a fixed split
+    stream_k = tc_used and (args.kernel == 4 or (args.kernel == 0 and args.split_blocks == 0))
     return {"split_blocks": split.value, "max_splits": nsplit.value,
-            "workspace_bytes": ws.value, "tensor_cores": bool(tc.value)}
+            "workspace_bytes": ws.value, "tensor_cores": tc_used, "stream_k": stream_k,
+            "launches": 3 if stream_k else (2 if nsplit.value > 1 else 1)}
 
 
 class DecodeCall:
@@ -274,12 +278,17 @@ class DecodeCall:
     batch's real work and the workspace from its longest sequence instead of
     from the page-table width. Keys beyond ``max_seq_blocks * 64`` are not
     read and set status bit 1.
+
+    ``out_ptr`` (instead of ``out``) is the raw device address of a contiguous
+    [S, Hq, D] buffer in the cache dtype, for rows that live in memory torch does
+    not own (another GPU's buffer mapped by CUDA IPC); :meth:`launch` then
+    returns None.
     """
 
     def __init__(self, page_table, q, k_cache, v_cache, seq_lens, cos, sin, *, positions=None,
                  mask=None, scope=None, causal=False, softmax_scale=None, out=None,
                  validate=True, split_blocks=0, kernel="auto", workspace=None, status=None,
-                 total_blocks=0, max_seq_blocks=0):
+                 total_blocks=0, max_seq_blocks=0, out_ptr=None):
         _require_cuda()
         if kernel not in _KERNELS:
             raise RuntimeError(f"kernel must be one of {sorted(_KERNELS)}, got {kernel!r}")
@@ -334,7 +343,12 @@ class DecodeCall:
         scope_arg = _scope_tensors(scope, S, device) if scope is not None else None
         if validate:
             validate_page_table(page_table, seq_lens, n_phys)
-        if out is None:
+        if out_ptr is not None:
+            if out is not None:
+                raise RuntimeError("pass out or out_ptr, not both")
+            if int(out_ptr) % 16 != 0:
+                raise RuntimeError("out_ptr must be 16-byte aligned")
+        elif out is None:
             out = torch.empty((S, Hq, D), dtype=k_cache.dtype, device=device)
         elif out.shape != (S, Hq, D) or out.dtype != k_cache.dtype or not out.is_contiguous():
             raise RuntimeError(f"out must be a contiguous [S, Hq, D] {k_cache.dtype} tensor")
@@ -348,6 +362,8 @@ class DecodeCall:
         args = _decode_args(page_table, q, k_cache, v_cache, seq_lens, cos, sin, positions,
                             mask_arg, scope_arg, causal, softmax_scale, split_blocks, kernel, out,
                             None, status, total_blocks, max_seq_blocks)
+        if out_ptr is not None:
+            args.out = int(out_ptr)
         self.plan = decode_plan(args)
         if self.plan["workspace_bytes"]:
             need = self.plan["workspace_bytes"]
