@@ -1080,13 +1080,22 @@ __global__ void __launch_bounds__(128) decode_sk_combine_kernel(const DecodePara
   }
   const int64_t stride = p.Hq;  // between consecutive slots of one row
   const float* ml = w.ws_ml + (first * p.Hq + h) * 2;
+  // With more CTAs than blocks some CTAs between a sequence's first and last own
+  // no block at all and wrote no slot: their slots are skipped.
+  const int64_t c0 = first / kWph - s;
+  auto live_slot = [&](int i) {
+    const int64_t c = c0 + i / kWph;
+    return (c * T_all) / w.P < ((c + 1) * T_all) / w.P;
+  };
   float M = -INFINITY;
-  for (int i = lane; i < n; i += 32) M = fmaxf(M, ml[2 * stride * i]);
+  for (int i = lane; i < n; i += 32)
+    if (live_slot(i)) M = fmaxf(M, ml[2 * stride * i]);
 #pragma unroll
   for (int sh = 16; sh > 0; sh >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, sh));
   float L = 0.f;
   if (M != -INFINITY)
-    for (int i = lane; i < n; i += 32) L += ml[2 * stride * i + 1] * exp2f(ml[2 * stride * i] - M);
+    for (int i = lane; i < n; i += 32)
+      if (live_slot(i)) L += ml[2 * stride * i + 1] * exp2f(ml[2 * stride * i] - M);
 #pragma unroll
   for (int sh = 16; sh > 0; sh >>= 1) L += __shfl_xor_sync(0xffffffffu, L, sh);
   const float inv = L > 0.f ? 1.f / L : 0.f;
@@ -1099,11 +1108,12 @@ __global__ void __launch_bounds__(128) decode_sk_combine_kernel(const DecodePara
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
     for (int i0 = 0; i0 < n; i0 += 32) {
       const int il = i0 + lane;
-      const float wl = (M != -INFINITY && il < n) ? exp2f(ml[2 * stride * il] - M) : 0.f;
+      const float wl =
+          (M != -INFINITY && il < n && live_slot(il)) ? exp2f(ml[2 * stride * il] - M) : 0.f;
       const int cnt = min(32, n - i0);
       for (int k = 0; k < cnt; ++k) {
         const float wk = __shfl_sync(0xffffffffu, wl, k);
-        if (wk == 0.f) continue;  // warp-uniform; an empty slot's values are never read
+        if (wk == 0.f) continue;  // warp-uniform; an empty or skipped slot is never read
         const float* src = po + static_cast<int64_t>(i0 + k) * stride * p.D + d;
         if (act && vec) {
           const float4 v = *reinterpret_cast<const float4*>(src);

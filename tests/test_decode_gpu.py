@@ -357,8 +357,9 @@ def test_total_blocks_hint_plans_from_the_real_work(cuda):
     c = _random_case(41, lens, 64, 8, 128, torch.bfloat16)
     args = [torch.from_numpy(c[x]).cuda() if isinstance(c[x], np.ndarray) else c[x].cuda()
             for x in ("pt", "q", "k", "v", "lens", "cos", "sin")]
-    blind = ba.DecodeCall(*args)
+    blind = ba.DecodeCall(*args, kernel="tc")
     total = int(sum(-(-n // 64) for n in lens))
-    aware = ba.DecodeCall(*args, total_blocks=total, max_seq_blocks=c["pt"].shape[1])
+    aware = ba.DecodeCall(*args, total_blocks=total, max_seq_blocks=c["pt"].shape[1],
+                          kernel="tc")
     assert aware.plan["split_blocks"] < blind.plan["split_blocks"]
     _close_half(aware.launch(), _oracle(c), "planned from total_blocks")

@@ -139,3 +139,14 @@ def test_streamk_matches_split_k_on_the_workload_shape(cuda):
     err = (out.float() - ref.float()).abs()
     assert err.max().item() <= HALF_MAX and err.mean().item() <= HALF_MEAN
     _check(c, out, rows=[0, 17, 31])
+
+
+@pytest.mark.parametrize("hq,hkv,d,dtype", [(32, 8, 128, torch.float16),
+                                            (3, 1, 64, torch.bfloat16)])
+def test_streamk_fewer_blocks_than_ctas(cuda, hq, hkv, d, dtype):
+    """A batch of 76 blocks over 148 CTAs: CTAs between a sequence's first and last own
+    no block; the merge skips their slots."""
+    lens = [1, 63, 64, 65, 700, 2049, 1500, 129]
+    c = _case(lens, hq, hkv, d, dtype, seed=hq * 7 + d)
+    _check(c, _run(c))
+    _check(c, _run(c, split_blocks=100))
