@@ -745,7 +745,8 @@ def _prefill_measure(args, world: int, rank: int, device):
         calls.append(PrefillCall(pt_c, qc, k, v, starts, lens, cos, sin, causal=True,
                                  kernel=args.kernel if args.kernel != "auto" else "auto",
                                  status=status, workspace=workspace,
-                                 krot_valid=torch.full((S,), c * C, dtype=torch.int32)))
+                                 krot_valid=torch.full((S,), c * C, dtype=torch.int32),
+                                 launch_seq=c))
         workspace = calls[-1].workspace
     flops = 4.0 * d * hq * S * (T * (T + 1) / 2.0)
     steps = args.prefill_steps if args.prefill_steps > 0 else args.steps

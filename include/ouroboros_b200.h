@@ -231,6 +231,13 @@ typedef struct ouro_attention_args {
   const int32_t* scope_lo;    /* [S, scope_stride]: LOCAL span [lo, hi) of the token at each */
   const int32_t* scope_hi;    /* position; the query at position i keeps key j when tags[j]
                                  or lo[i] <= j < hi[i] (both NULL with scope_tags NULL) */
+  int32_t launch_seq;         /* tensor-core path: 0 starts a chain of launches on one
+                                 workspace (the library zeroes its counters first); k > 0
+                                 marks the k-th launch after it on the same stream (chunked
+                                 prefill: chunk k). A chained launch may start while the
+                                 previous one finishes (programmatic dependent launch) and
+                                 reads the keys that launch rotated once its rotations are
+                                 done; the launches of a chain must write distinct outputs. */
 } ouro_attention_args;
 
 /* Kernel choice and the workspace the tensor-core path needs

@@ -238,6 +238,8 @@ ouro::RowsParams to_rows(const ouro_attention_args* a) {
   p.workspace = a->workspace;
   p.workspace_bytes = static_cast<int64_t>(a->workspace_bytes);
   p.krot_valid = a->krot_valid;
+  if (a->launch_seq < 0) fail(OURO_EINVAL, "launch_seq must be >= 0");
+  p.launch_seq = a->launch_seq;
   if (a->scope_tags != nullptr) {
     if (a->scope_lo == nullptr || a->scope_hi == nullptr)
       fail(OURO_EINVAL, "scope_tags needs scope_lo and scope_hi");

@@ -39,14 +39,19 @@
 //   warps 12-15 first the key rotation: RoPE for the keys that no earlier
 //               call sharing the workspace rotated (each CTA a share, written
 //               to the scratch), then one arrival per CTA on a grid-wide
-//               counter the launcher zeroes (the launch is cooperative, so
-//               every CTA is resident). Then the epilogue, one TMEM lane
+//               counter (one word per launch parity of a chain, see
+//               kWarpChain). Then the epilogue, one TMEM lane
 //               quarter per warp (one row per thread): once
 //               O is final, O = (2^(m_0-m) O_0 + 2^(m_1-m) O_1) /
 //               (2^(m_0-m) l_0 + 2^(m_1-m) l_1), m = max(m_0, m_1), staged in
 //               the item's own (now unused) query buffer and stored coalesced;
 //               then O is released for the next item and the query tile of the
 //               item after next is rotated into the same buffer.
+//   warp 11     the launch chain: once the previous launch has completed it
+//               zeroes the counter word the next launch will use, then lets the
+//               next launch start (programmatic dependent launch), whose CTAs
+//               take SMs as this launch's CTAs finish and do their prologue,
+//               key rotation and first query tiles during this launch's tail.
 // TMEM columns: S/P buffers at 0 and 128, O_0 at 256, O_1 at 384 (512 allocated).
 // Registers: the block launches with 128 per thread (512 threads); the softmax
 // warpgroups raise theirs to 168, the producer/MMA warpgroup lowers to 56 and
@@ -75,6 +80,7 @@ constexpr int kTile = 2 * kAtom;  // 128 rows x 128 columns x 2 bytes
 constexpr int kSoftmaxWarps = 8;                   // 4 lane quarters x 2 tile parities
 constexpr int kSoftmaxThreads = kSoftmaxWarps * 32;
 constexpr int kWarpK = 8, kWarpMma = 9, kWarpV = 10;  // K loads, MMA / TMEM, V loads
+constexpr int kWarpChain = 11;                        // the launch chain's bookkeeping
 constexpr int kWarpEpi = 12;                          // first epilogue warp
 constexpr int kEpiThreads = 128;
 constexpr int kThreads = 16 * 32;
@@ -349,9 +355,10 @@ __device__ void rotate_new_keys(const RowsParams& p, T* krot, int bps, int t) {
   }
 }
 
-// Grid-wide arrival after a CTA's rotations on a word the launcher zeroes
-// before the launch; the K producers wait for it to reach gridDim.x. The launch
-// is cooperative, so every CTA that is waited for is resident.
+// Grid-wide arrival after a CTA's rotations on a word that is zero when the
+// launch starts; the K producers wait (bounded) for it to reach gridDim.x. The
+// grid has one CTA per SM and an SM holds one, so every CTA waited for becomes
+// resident once the previous kernel on the stream has finished.
 __device__ __forceinline__ void rotation_arrive(unsigned long long* word) {
   __threadfence();
   atomicAdd(word, 1ull);
@@ -444,6 +451,16 @@ __global__ void __launch_bounds__(kThreads, 1)
   Bars* bars = reinterpret_cast<Bars*>(smem + kOffBar);
   volatile int32_t* s_abort = &bars->abort;
 
+  // Rotation counters of a launch chain: launch k counts its CTAs' rotations on
+  // word k % 3 and publishes its grid size in word 3 + k % 3; launch k + 1 reads
+  // both before it loads keys of chunk k. Launch k zeroes word (k + 1) % 3 for
+  // the next launch once launch k - 1 is done (launches k - 2 and k - 1, its
+  // users, are then complete). The launcher zeroes all words at a chain's start.
+  const int seq3 = p.launch_seq % 3;
+  unsigned long long* const rot_cnt = rot_sync + seq3;
+  unsigned long long* const rot_next = rot_sync + (seq3 + 1) % 3;
+  unsigned long long* const rot_prev = rot_sync + (seq3 + 2) % 3;
+  unsigned long long* const grid_words = rot_sync + 3;
   const int G = p.G;
   const int ppt = kBM / G;  // positions per tile (G divides 128, so a power of 2)
   const int lppt = 31 - __clz(ppt);
@@ -506,6 +523,22 @@ __global__ void __launch_bounds__(kThreads, 1)
         // load at once).
         const unsigned long long rot_done = gridDim.x;
         bool rotated = !is_k;
+        // Keys rotated by earlier launches of the chain: launches up to k - 2 are
+        // complete when this one starts; launch k - 1 (maybe still running) has
+        // rotated its chunk's keys once its counter reaches its grid size.
+        if (is_k && p.launch_seq > 0) {
+          const uint64_t t0 = global_timer_ns();
+          for (;;) {
+            const unsigned long long want = ld_acquire_gpu(grid_words + (seq3 + 2) % 3);
+            if (want > 0 && ld_acquire_gpu(rot_prev) >= want) break;
+            __nanosleep(256);
+            if (global_timer_ns() - t0 > 2000000000ull) {
+              fail(kStatusWaitTimeout);
+              break;
+            }
+          }
+          fence_proxy_async_global();
+        }
         Item it;
         for (int L = next_item(p, blockIdx.x, n_items, n_qt, ppt, it); L < n_items && !*s_abort;
              L = next_item(p, L + gridDim.x, n_items, n_qt, ppt, it)) {
@@ -514,7 +547,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int j = 0; j < it.n_tiles; ++j, ++g) {
             if (!rotated && (j + 1) * kBN > kv) {
               const uint64_t t0 = global_timer_ns();
-              while (ld_acquire_gpu(rot_sync) < rot_done && !*s_abort) {
+              while (ld_acquire_gpu(rot_cnt) < rot_done && !*s_abort) {
                 __nanosleep(256);  // one polling thread per CTA, on one word
                 if (global_timer_ns() - t0 > 2000000000ull) {
                   fail(kStatusWaitTimeout);
@@ -552,6 +585,21 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           }
         }
+      }
+    } else if (warp == kWarpChain) {
+      // -------------------- launch chain: counter for the next launch --------------------
+      if (lane == 0) {
+        if (blockIdx.x == 0) {  // for the next launch: this launch's grid size
+          atomicExch(grid_words + seq3, static_cast<unsigned long long>(gridDim.x));
+          __threadfence();
+        }
+        griddep_wait();  // launch k - 1 (and so k - 2), the users of word (k + 1) % 3, is done
+        if (blockIdx.x == 0) {
+          atomicExch(rot_next, 0ull);
+          atomicExch(grid_words + (seq3 + 1) % 3, 0ull);
+          __threadfence();
+        }
+        griddep_launch_dependents();  // the next launch may start on SMs this one frees
       }
     } else if (warp == kWarpMma) {
       // ------------------------------ MMA issuer ------------------------------
@@ -664,7 +712,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       rotate_new_keys<T>(p, static_cast<T*>(p.workspace), krot_rows_per_head / kBlock, t);
       fence_proxy_async_global();
       named_barrier(kBarEpi, kEpiThreads);
-      if (t == 0) rotation_arrive(rot_sync);
+      if (t == 0) rotation_arrive(rot_cnt);
     }
     const int quarter = warp & 3;
     const int r = quarter * 32 + lane;  // TMEM lane == query row == staged output row
@@ -1054,8 +1102,8 @@ cudaError_t launch_prefill_tc(const RowsParams& p, int dtype, cudaStream_t strea
   if (!kv_map(&mk, p.workspace, dt, k_rows, kBN) || !kv_map(&mv, p.v, dt, v_rows, kBlock))
     return cudaErrorInvalidValue;
   // Persistent CTAs: one per SM (shared memory allows no second), each walking
-  // items c, c + grid, ... The launch is cooperative: the K producers wait for
-  // the key rotations of all CTAs, so all of them must be resident.
+  // items c, c + grid, ... The K producers wait for the key rotations of all
+  // CTAs: with one CTA per SM all of them are resident together.
   const int ppt = kBM / p.G;
   const int64_t n_items = static_cast<int64_t>((p.Lq + ppt - 1) / ppt) * p.Hkv * p.S;
   if (n_items >= (int64_t(1) << 31)) return cudaErrorInvalidValue;
@@ -1087,16 +1135,24 @@ cudaError_t launch_prefill_tc(const RowsParams& p, int dtype, cudaStream_t strea
   if (e != cudaSuccess) return e;
   unsigned long long* rot_sync =
       reinterpret_cast<unsigned long long*>(static_cast<uint8_t*>(p.workspace) + krot_bytes(p));
-  e = cudaMemsetAsync(rot_sync, 0, sizeof(*rot_sync), stream);
-  if (e != cudaSuccess) return e;
+  if (p.launch_seq == 0) {  // a chain starts: counter and grid-size words zero
+    e = cudaMemsetAsync(rot_sync, 0, 6 * sizeof(*rot_sync), stream);
+    if (e != cudaSuccess) return e;
+  }
+  // Programmatic stream serialization: this launch's CTAs may start on SMs the
+  // previous kernel frees, before it completes; every read of the previous
+  // launches' results waits (griddepcontrol.wait) for its completion. One CTA
+  // per SM, at most one per SM resident, so every CTA of the grid becomes
+  // resident once the previous kernel is done (the rotation counter's waits
+  // rely on it; they are bounded).
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = kSmemBytes;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeCooperative;
-  attr[0].val.cooperative = 1;
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   return cudaLaunchKernelEx(&cfg, kernel, mk, mv, p, rows_per_head, rot_sync);

@@ -226,6 +226,17 @@ __device__ __forceinline__ float max3f(float a, float b, float c) {
 }
 
 // Named barrier over `nthreads` threads (id 0 is __syncthreads).
+// Programmatic dependent launch: wait until the grids this one depends on (the
+// previous kernel on the stream, when launched with programmatic stream
+// serialization) have completed with their memory visible; allow the next
+// kernel on the stream to be scheduled once every CTA of this grid has done so.
+__device__ __forceinline__ void griddep_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 __device__ __forceinline__ void named_barrier(uint32_t id, uint32_t nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }

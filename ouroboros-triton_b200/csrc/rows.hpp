@@ -35,6 +35,8 @@ struct RowsParams {
   int64_t scope_stride;
   const int32_t* scope_lo;    // [S, scope_stride]: span [lo, hi) of the token at each position
   const int32_t* scope_hi;
+  int32_t launch_seq;         // tensor-core path: position in a chain of launches sharing the
+                              // workspace (0 = chain start)
 };
 
 cudaError_t launch_attend_rows_simt(const RowsParams& p, int dtype, cudaStream_t stream);

@@ -56,7 +56,7 @@ class AttentionArgs(ctypes.Structure):
         ("softmax_scale", ctypes.c_float),
         ("workspace", _vp), ("workspace_bytes", ctypes.c_size_t), ("krot_valid", _vp),
         ("scope_tags", _vp), ("scope_stride", ctypes.c_int64), ("scope_lo", _vp),
-        ("scope_hi", _vp),
+        ("scope_hi", _vp), ("launch_seq", _i32),
     ]
 
 

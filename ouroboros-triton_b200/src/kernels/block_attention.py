@@ -549,7 +549,7 @@ class PrefillCall:
     def __init__(self, page_table, q, k_cache, v_cache, q_start, seq_lens, cos, sin, *,
                  causal: bool = True, softmax_scale=None, out=None, validate: bool = True,
                  kernel: str = "auto", status=None, workspace=None, krot_valid=None,
-                 scope=None):
+                 scope=None, launch_seq: int = 0):
         """``scope`` (optional) is the batch's token scope ``(tags, lo, hi)``, each
         [S, W] with W a multiple of 16 covering seq_lens (from
         :func:`src.scoping_mask.prefill_scope`): the query at position i keeps
@@ -560,7 +560,12 @@ class PrefillCall:
         prefill together with ``krot_valid`` ([S] int32: keys [0, krot_valid[s])
         already rotated there by an earlier call with the same caches, page-table
         width and RoPE tables) and each key is rotated once instead of once per
-        chunk."""
+        chunk.
+
+        ``launch_seq``: the call's position in a chain of launches that share
+        ``workspace`` and follow each other on one stream (chunk k of a chunked
+        prefill: k). A follow-up launch (k > 0) overlaps the previous one's tail
+        and must not share its ``out``; 0 (the default) starts a chain."""
         _require_cuda()
         if kernel not in _KERNELS:
             raise RuntimeError(f"kernel must be one of {sorted(_KERNELS)}, got {kernel!r}")
@@ -600,6 +605,9 @@ class PrefillCall:
         self.device = device
         self.args = _rows_args(q, False, k_cache, v_cache, pt, lens, starts, cos, sin, None, None,
                                out, status, Hq, L, causal, softmax_scale, kernel)
+        if launch_seq < 0:
+            raise RuntimeError("launch_seq must be >= 0")
+        self.args.launch_seq = int(launch_seq)
         scope_keep = None
         if scope is not None:
             tags, lo, hi = scope

@@ -70,7 +70,7 @@ def _worker(rank, world, port, result_q):
     torch.cuda.set_device(rank)
     device = torch.device("cuda", rank)
     dist.init_process_group("nccl", rank=rank, world_size=world,
-                            timeout=datetime.timedelta(seconds=60), device_id=device)
+                            timeout=datetime.timedelta(seconds=300), device_id=device)
     try:
         _, _, _, k_cpu, v_cpu, _ = _pool(rank)
         k, v = k_cpu.to(device), v_cpu.to(device)
@@ -118,7 +118,7 @@ def test_sharded_decode_two_gpus_nccl():
     for p in procs:
         p.start()
     for p in procs:
-        p.join(timeout=240)
+        p.join(timeout=600)
     assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
     msgs = []
     while not q.empty():
@@ -147,7 +147,7 @@ def _peer_worker(rank, world, port, result_q):
     torch.cuda.set_device(rank)
     device = torch.device("cuda", rank)
     dist.init_process_group("nccl", rank=rank, world_size=world,
-                            timeout=datetime.timedelta(seconds=60), device_id=device)
+                            timeout=datetime.timedelta(seconds=300), device_id=device)
     sh = None
     try:
         # one batch of 11 sequences placed on the ranks by LPT; every rank's pool from _pool
@@ -224,7 +224,7 @@ def test_decode_shards_peer_exchange_two_gpus():
     for p in procs:
         p.start()
     for p in procs:
-        p.join(timeout=240)
+        p.join(timeout=600)
     assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
     msgs = []
     while not q.empty():

@@ -242,3 +242,37 @@ def test_two_chunk_prefill_through_kv_append(cuda):
                                 causal=True)
     err = np.abs(got - want)
     assert err.max() <= 2e-2 and err.mean() <= 2e-3, (err.max(), err.mean())
+
+
+@pytest.mark.parametrize("chunks", [2, 6])
+def test_chained_chunk_launches_vs_oracle(cuda, chunks):
+    """The chunks of a prefill launched back to back as one chain (launch_seq = chunk):
+    each launch may start during the previous one's tail; it reads the previous launch's
+    keys once that launch's rotation counter is complete and earlier keys at once. Two
+    passes of the chain in a row: the second starts a new chain on the same workspace."""
+    hq, hkv, d, L = 32, 8, 128, 256
+    totals = [L * chunks] * 4
+    pt, q_all, k, v, cos, sin = _case(77, totals, hq, hkv, L * chunks, torch.bfloat16)
+    want = ao.prefill_attention(pt, q_all.float().cpu().numpy(), k.float().cpu().numpy(),
+                                v.float().cpu().numpy(), [0] * 4, totals, cos, sin, causal=True)
+    ptd = torch.from_numpy(pt).cuda()
+    cos_d, sin_d = torch.from_numpy(cos).cuda(), torch.from_numpy(sin).cuda()
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    calls, ws = [], None
+    for c in range(chunks):
+        starts = torch.full((4,), c * L, dtype=torch.int32, device="cuda")
+        lens = torch.full((4,), (c + 1) * L, dtype=torch.int32, device="cuda")
+        pt_c = ptd.clone()
+        pt_c[:, (c + 1) * L // 64:] = -1
+        calls.append(ba.PrefillCall(pt_c, q_all[:, :, c * L:(c + 1) * L].contiguous(), k, v,
+                                    starts, lens, cos_d, sin_d, kernel="tc", status=status,
+                                    workspace=ws,
+                                    krot_valid=torch.full((4,), c * L, dtype=torch.int32),
+                                    launch_seq=c))
+        ws = calls[-1].workspace
+    for _ in range(2):
+        results = [cl.launch() for cl in calls]   # no synchronisation between the launches
+        torch.cuda.synchronize()
+        assert int(status.item()) == 0
+        for c in range(chunks):
+            _check(results[c], want[:, :, c * L:(c + 1) * L], f"chunk {c}")
