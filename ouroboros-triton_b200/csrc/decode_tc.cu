@@ -42,6 +42,7 @@
 #include <mutex>
 
 #include "attention.hpp"
+#include "pdl.cuh"
 #include "ptx.cuh"
 
 namespace ouro {
@@ -842,6 +843,11 @@ __global__ void __launch_bounds__(HPC * kWph * 32, 1)
   const int c = blockIdx.x;
   const int kvh0 = blockIdx.y * HPC;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // Launched programmatically after the prep kernel: its block sums (and everything
+  // before it on the stream) are complete and visible past this wait. The merge
+  // kernel may then be scheduled on SMs as this grid's CTAs exit.
+  griddep_wait();
+  griddep_launch_dependents();
   const int64_t T_all = w.cum[p.S];
   const int64_t flat_lo = static_cast<int64_t>(c) * T_all / w.P;
   const int64_t flat_hi = static_cast<int64_t>(c + 1) * T_all / w.P;
@@ -1013,6 +1019,8 @@ __global__ void __launch_bounds__(1024) decode_sk_prep_kernel(const DecodeParams
   __shared__ int32_t warp_sum[32];
   __shared__ int32_t carry;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  griddep_wait();  // the lengths and tables written by earlier work on the stream
+  griddep_launch_dependents();
   if (tid == 0) {
     carry = 0;
     cum[0] = 0;
@@ -1064,6 +1072,8 @@ template <typename T>
 __global__ void __launch_bounds__(128) decode_sk_combine_kernel(const DecodeParams p,
                                                                 const SkWork w) {
   const int lane = threadIdx.x & 31;
+  griddep_wait();  // every piece's partials are written
+  griddep_launch_dependents();
   const int64_t row = static_cast<int64_t>(blockIdx.x) * 4 + (threadIdx.x >> 5);
   if (row >= static_cast<int64_t>(p.S) * p.Hq) return;  // warp-uniform
   const int s = static_cast<int>(row / p.Hq), h = static_cast<int>(row % p.Hq);
@@ -1081,21 +1091,31 @@ __global__ void __launch_bounds__(128) decode_sk_combine_kernel(const DecodePara
   const int64_t stride = p.Hq;  // between consecutive slots of one row
   const float* ml = w.ws_ml + (first * p.Hq + h) * 2;
   // With more CTAs than blocks some CTAs between a sequence's first and last own
-  // no block at all and wrote no slot: their slots are skipped.
+  // no block at all and wrote no slot: their slots are skipped (weight 0, never read).
   const int64_t c0 = first / kWph - s;
   auto live_slot = [&](int i) {
     const int64_t c = c0 + i / kWph;
     return (c * T_all) / w.P < ((c + 1) * T_all) / w.P;
   };
-  float M = -INFINITY;
-  for (int i = lane; i < n; i += 32)
-    if (live_slot(i)) M = fmaxf(M, ml[2 * stride * i]);
+  // (m, l) of slot i sits in lane i % 32's registers for the first 32 slots; a row
+  // with more slots reads the rest in further rounds. All loads of a round are
+  // issued before their values are used.
+  auto slot_ml = [&](int i) -> float2 {
+    return (i < n && live_slot(i)) ? *reinterpret_cast<const float2*>(ml + 2 * stride * i)
+                                   : make_float2(-INFINITY, 0.f);
+  };
+  const float2 ml0 = slot_ml(lane);
+  float M = ml0.x;
+  for (int i = lane + 32; i < n; i += 32) M = fmaxf(M, slot_ml(i).x);
 #pragma unroll
   for (int sh = 16; sh > 0; sh >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, sh));
-  float L = 0.f;
-  if (M != -INFINITY)
-    for (int i = lane; i < n; i += 32)
-      if (live_slot(i)) L += ml[2 * stride * i + 1] * exp2f(ml[2 * stride * i] - M);
+  auto weight = [&](float2 v) { return (M != -INFINITY && v.x != -INFINITY) ? exp2f(v.x - M) : 0.f; };
+  const float w0 = weight(ml0);
+  float L = w0 * ml0.y;
+  for (int i = lane + 32; i < n; i += 32) {
+    const float2 v = slot_ml(i);
+    L += weight(v) * v.y;
+  }
 #pragma unroll
   for (int sh = 16; sh > 0; sh >>= 1) L += __shfl_xor_sync(0xffffffffu, L, sh);
   const float inv = L > 0.f ? 1.f / L : 0.f;
@@ -1107,23 +1127,22 @@ __global__ void __launch_bounds__(128) decode_sk_combine_kernel(const DecodePara
     const bool act = d < p.D;
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
     for (int i0 = 0; i0 < n; i0 += 32) {
-      const int il = i0 + lane;
-      const float wl =
-          (M != -INFINITY && il < n && live_slot(il)) ? exp2f(ml[2 * stride * il] - M) : 0.f;
+      const float wl = i0 == 0 ? w0 : weight(slot_ml(i0 + lane));
       const int cnt = min(32, n - i0);
+      // Eight slots per round: their (predicated) loads are in flight together.
+#pragma unroll 8
       for (int k = 0; k < cnt; ++k) {
         const float wk = __shfl_sync(0xffffffffu, wl, k);
-        if (wk == 0.f) continue;  // warp-uniform; an empty or skipped slot is never read
         const float* src = po + static_cast<int64_t>(i0 + k) * stride * p.D + d;
-        if (act && vec) {
-          const float4 v = *reinterpret_cast<const float4*>(src);
-          acc.x += wk * v.x;
-          acc.y += wk * v.y;
-          acc.z += wk * v.z;
-          acc.w += wk * v.w;
-        } else if (act) {
-          acc.x += wk * src[0];
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (act && wk != 0.f) {  // an empty or skipped slot is never read
+          if (vec) v = *reinterpret_cast<const float4*>(src);
+          else v.x = src[0];
         }
+        acc.x += wk * v.x;
+        acc.y += wk * v.y;
+        acc.z += wk * v.z;
+        acc.w += wk * v.w;
       }
     }
     if (act) {
@@ -1248,20 +1267,22 @@ cudaError_t launch_sk_typed(const DecodeParams& p, CUtensorMapDataType dt, cudaS
       p.ws_ml + static_cast<size_t>(p.S + w.P) * kWph * p.Hq * 2);
   w.cum = ints;
   w.first_seq = ints + p.S + 1;
-  decode_sk_prep_kernel<<<1, 1024, 0, stream>>>(p, ints, ints + p.S + 1, w.P);
-  cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) return e;
+  // The three kernels are chained with programmatic dependent launch: each one's
+  // CTAs are scheduled while its predecessor runs and wait (griddepcontrol.wait)
+  // for the predecessor's results before touching them.
   const size_t smem = sk_smem_bytes<D, HPC>();
   auto kernel = decode_sk_kernel<T, D, HPC>;
-  e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           static_cast<int>(smem));
+  cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(smem));
   if (e != cudaSuccess) return e;
-  kernel<<<dim3(w.P, p.Hkv / HPC), HPC * kWph * 32, smem, stream>>>(mk, mv, mc, ms, p, w);
-  e = cudaGetLastError();
+  e = launch_pdl(decode_sk_prep_kernel, dim3(1), dim3(1024), 0, stream, p, ints, ints + p.S + 1,
+                 w.P);
+  if (e != cudaSuccess) return e;
+  e = launch_pdl(kernel, dim3(w.P, p.Hkv / HPC), dim3(HPC * kWph * 32), smem, stream, mk, mv, mc,
+                 ms, p, w);
   if (e != cudaSuccess) return e;
   const dim3 cgrid(static_cast<unsigned>((static_cast<int64_t>(p.S) * p.Hq + 3) / 4));
-  decode_sk_combine_kernel<T><<<cgrid, 128, 0, stream>>>(p, w);
-  return cudaGetLastError();
+  return launch_pdl(decode_sk_combine_kernel<T>, cgrid, dim3(128), 0, stream, p, w);
 }
 
 template <typename T>

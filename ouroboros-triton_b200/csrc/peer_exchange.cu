@@ -20,6 +20,9 @@
 // when it runs out the kernel sets status bit 2 (wait timeout), does no copy
 // and returns, so a rank that never arrives surfaces as an error, not a hang.
 // No TMA and no multicast touch peer memory: plain 16-byte loads and stores.
+// Each kernel is launched with programmatic stream serialization and waits
+// (griddepcontrol.wait) for the previous kernel on its stream before it touches
+// memory, so its launch overlaps that kernel's tail.
 #include <cuda_runtime.h>
 
 #include <cstdint>
@@ -28,6 +31,7 @@
 
 #include "block_table.hpp"
 #include "capi_common.hpp"
+#include "pdl.cuh"
 #include "ptx.cuh"
 
 using ouro::fail;
@@ -71,6 +75,8 @@ __device__ bool block_wait_flags(const uint64_t* flags, int n, int stride, uint6
 // out row i = src row idx[i] (rows of row_bytes, a multiple of 16).
 __global__ void gather_rows_kernel(const uint8_t* src, const int64_t* idx, uint8_t* out,
                                    int64_t rows, int64_t row_bytes) {
+  ouro::griddep_wait();
+  ouro::griddep_launch_dependents();
   const int64_t vec = row_bytes / 16;
   const int64_t total = rows * vec;
   for (int64_t t = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; t < total;
@@ -82,6 +88,8 @@ __global__ void gather_rows_kernel(const uint8_t* src, const int64_t* idx, uint8
 }
 
 __global__ void raise_flags_kernel(uint64_t* const* flags, int n, uint64_t step) {
+  ouro::griddep_wait();
+  ouro::griddep_launch_dependents();
   __threadfence_system();
   for (int i = threadIdx.x; i < n; i += blockDim.x) st_release_sys(flags[i], step);
 }
@@ -89,6 +97,8 @@ __global__ void raise_flags_kernel(uint64_t* const* flags, int n, uint64_t step)
 __global__ void fetch_kernel(const uint64_t* ready, uint64_t step, uint64_t limit_ns,
                              const uint8_t* src0, uint8_t* dst0, int64_t bytes0,
                              const uint8_t* src1, uint8_t* dst1, int64_t bytes1, int32_t* status) {
+  ouro::griddep_wait();
+  ouro::griddep_launch_dependents();
   if (!block_wait_flags(ready, 1, 1, step, limit_ns, status)) return;
   const int64_t v0 = bytes0 / 16, v1 = bytes1 / 16;
   for (int64_t t = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; t < v0 + v1;
@@ -99,6 +109,8 @@ __global__ void fetch_kernel(const uint64_t* ready, uint64_t step, uint64_t limi
 }
 
 __global__ void signal_kernel(uint64_t* flag, uint64_t step) {
+  ouro::griddep_wait();
+  ouro::griddep_launch_dependents();
   __threadfence_system();
   st_release_sys(flag, step);
 }
@@ -106,6 +118,8 @@ __global__ void signal_kernel(uint64_t* flag, uint64_t step) {
 __global__ void collect_kernel(const uint64_t* done, int n, int stride, uint64_t step,
                                uint64_t limit_ns, const uint8_t* src, const int64_t* idx,
                                uint8_t* out, int64_t rows, int64_t row_bytes, int32_t* status) {
+  ouro::griddep_wait();
+  ouro::griddep_launch_dependents();
   if (!block_wait_flags(done, n, stride, step, limit_ns, status)) return;
   const int64_t vec = row_bytes / 16;
   const int64_t total = rows * vec;
@@ -193,13 +207,15 @@ int ouro_shard_publish(const void* q, const int64_t* perm, void* q_perm, int64_t
     if (n_peers > 0 && peer_ready == nullptr) fail(OURO_EINVAL, "publish: null flag array");
     auto st = static_cast<cudaStream_t>(stream);
     if (rows > 0) {
-      gather_rows_kernel<<<grid_for(rows * row_bytes / 16), 256, 0, st>>>(
-          static_cast<const uint8_t*>(q), perm, static_cast<uint8_t*>(q_perm), rows, row_bytes);
-      check(cudaGetLastError(), "publish (gather)");
+      check(ouro::launch_pdl(gather_rows_kernel, dim3(grid_for(rows * row_bytes / 16)), dim3(256),
+                             0, st, static_cast<const uint8_t*>(q), perm,
+                             static_cast<uint8_t*>(q_perm), rows, row_bytes),
+            "publish (gather)");
     }
     if (n_peers > 0) {
-      raise_flags_kernel<<<1, 32, 0, st>>>(peer_ready, n_peers, step);
-      check(cudaGetLastError(), "publish (flags)");
+      check(ouro::launch_pdl(raise_flags_kernel, dim3(1), dim3(32), 0, st, peer_ready, n_peers,
+                             step),
+            "publish (flags)");
     }
   })
 }
@@ -215,18 +231,21 @@ int ouro_shard_fetch(const uint64_t* ready, uint64_t step, uint64_t timeout_ns, 
         (bytes1 > 0 && (!src1 || !dst1 || !aligned16(src1) || !aligned16(dst1))))
       fail(OURO_EINVAL, "fetch: null or unaligned buffer");
     auto st = static_cast<cudaStream_t>(stream);
-    fetch_kernel<<<grid_for((bytes0 + bytes1) / 16), 256, 0, st>>>(
-        ready, step, timeout_ns, static_cast<const uint8_t*>(src0), static_cast<uint8_t*>(dst0),
-        bytes0, static_cast<const uint8_t*>(src1), static_cast<uint8_t*>(dst1), bytes1, status);
-    check(cudaGetLastError(), "fetch");
+    check(ouro::launch_pdl(fetch_kernel, dim3(grid_for((bytes0 + bytes1) / 16)), dim3(256), 0, st,
+                           ready, step, timeout_ns, static_cast<const uint8_t*>(src0),
+                           static_cast<uint8_t*>(dst0), bytes0,
+                           static_cast<const uint8_t*>(src1), static_cast<uint8_t*>(dst1), bytes1,
+                           status),
+          "fetch");
   })
 }
 
 int ouro_shard_signal(uint64_t* flag, uint64_t step, void* stream) {
   OURO_CAPI_GUARD({
     if (flag == nullptr) fail(OURO_EINVAL, "signal: null flag");
-    signal_kernel<<<1, 1, 0, static_cast<cudaStream_t>(stream)>>>(flag, step);
-    check(cudaGetLastError(), "signal");
+    check(ouro::launch_pdl(signal_kernel, dim3(1), dim3(1), 0, static_cast<cudaStream_t>(stream),
+                           flag, step),
+          "signal");
   })
 }
 
@@ -241,10 +260,11 @@ int ouro_shard_collect(const uint64_t* done, int32_t n_flags, int32_t flag_strid
     if (rows > 0 && (!src || !inv || !out || !aligned16(src) || !aligned16(out)))
       fail(OURO_EINVAL, "collect: null or unaligned row buffer");
     auto st = static_cast<cudaStream_t>(stream);
-    collect_kernel<<<grid_for(rows * row_bytes / 16), 256, 0, st>>>(
-        done, n_flags, flag_stride, step, timeout_ns, static_cast<const uint8_t*>(src), inv,
-        static_cast<uint8_t*>(out), rows, row_bytes, status);
-    check(cudaGetLastError(), "collect");
+    check(ouro::launch_pdl(collect_kernel, dim3(grid_for(rows * row_bytes / 16)), dim3(256), 0,
+                           st, done, n_flags, flag_stride, step, timeout_ns,
+                           static_cast<const uint8_t*>(src), inv, static_cast<uint8_t*>(out),
+                           rows, row_bytes, status),
+          "collect");
   })
 }
 

@@ -22,7 +22,6 @@
 //               j % 2, then O_{j%2} += P_j V_j with P_j read from TMEM (V as an
 //               MN-major operand), tcgen05.commit to mbarriers; after an item's
 //               last PV one commit tells the epilogue that O is final
-//   warp 11     idle (completes the third warpgroup)
 //   warps 0-7   softmax. Warp w owns TMEM lanes 32 (w % 4) .. +31 (one query
 //               row per thread) and the tiles of parity w / 4: each parity keeps
 //               its own running max m, row sum l and accumulator O, so the two
@@ -39,7 +38,7 @@
 //   warps 12-15 first the key rotation: RoPE for the keys that no earlier
 //               call sharing the workspace rotated (each CTA a share, written
 //               to the scratch), then one arrival per CTA on a grid-wide
-//               counter (one word per launch parity of a chain, see
+//               counter (one word per launch of a chain, modulo 3, see
 //               kWarpChain). Then the epilogue, one TMEM lane
 //               quarter per warp (one row per thread): once
 //               O is final, O = (2^(m_0-m) O_0 + 2^(m_1-m) O_1) /
@@ -47,11 +46,13 @@
 //               the item's own (now unused) query buffer and stored coalesced;
 //               then O is released for the next item and the query tile of the
 //               item after next is rotated into the same buffer.
-//   warp 11     the launch chain: once the previous launch has completed it
-//               zeroes the counter word the next launch will use, then lets the
-//               next launch start (programmatic dependent launch), whose CTAs
-//               take SMs as this launch's CTAs finish and do their prologue,
-//               key rotation and first query tiles during this launch's tail.
+//   warp 11     the launch chain: zeroes the counter word the next launch
+//               will use, then lets the next kernel be scheduled (programmatic
+//               dependent launch): its CTAs take SMs as this launch's CTAs exit,
+//               set up their barriers and TMEM, and wait for this launch to
+//               complete before they touch global memory.
+// Every thread waits (griddepcontrol.wait) for the previous kernel on the stream
+// before its first global access.
 // TMEM columns: S/P buffers at 0 and 128, O_0 at 256, O_1 at 384 (512 allocated).
 // Registers: the block launches with 128 per thread (512 threads); the softmax
 // warpgroups raise theirs to 168, the producer/MMA warpgroup lowers to 56 and
@@ -370,11 +371,13 @@ __device__ __forceinline__ void rotation_arrive(unsigned long long* word) {
 // q0 + R % ppt; unit (R, c) covers the pairs (d, d + 64), d in [8c, 8c+8).
 // The caller passes rows R0, R0 + dR, R0 + 2 dR, R0 + 3 dR and one c; eight
 // consecutive threads take the 8 units of one row, so a warp-wide load reads 4
-// contiguous row segments.
-template <typename T, bool kPaged>
+// contiguous row segments. kOnePos: the four rows are at one position (dR a
+// multiple of ppt), so their cos/sin are read once.
+template <typename T, bool kPaged, bool kOnePos = false>
 struct QTile {
+  static constexpr int kPos = kOnePos ? 1 : 4;  // cos/sin sets held
   uint4 lo[4], hi[4];
-  float4 cs[8], sn[8];
+  float4 cs[2 * kPos], sn[2 * kPos];
 
   __device__ __forceinline__ void load(const RowsParams& p, const Item& it, int ppt, int R0,
                                        int dR, int c) {
@@ -384,9 +387,12 @@ struct QTile {
     for (int k = 0; k < 4; ++k) {
       const int R = R0 + dR * k;
       const int iR = R & (ppt - 1), posR = it.q0 + iR;  // ppt = 128 / G is a power of 2
+      const int kc = kOnePos ? 0 : k;  // this row's cos/sin set
       lo[k] = hi[k] = make_uint4(0, 0, 0, 0);
-      cs[2 * k] = cs[2 * k + 1] = make_float4(1.f, 1.f, 1.f, 1.f);
-      sn[2 * k] = sn[2 * k + 1] = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (!kOnePos || k == 0) {
+        cs[2 * kc] = cs[2 * kc + 1] = make_float4(1.f, 1.f, 1.f, 1.f);
+        sn[2 * kc] = sn[2 * kc + 1] = make_float4(0.f, 0.f, 0.f, 0.f);
+      }
       if (iR < it.rows_valid) {
         const int head = it.kvh * p.G + (R >> lppt);
         const T* qrow = nullptr;
@@ -411,13 +417,13 @@ struct QTile {
           lo[k] = *reinterpret_cast<const uint4*>(qrow + 8 * c);
           hi[k] = *reinterpret_cast<const uint4*>(qrow + half + 8 * c);
         }
-        if (posR < p.max_pos) {
+        if ((!kOnePos || k == 0) && posR < p.max_pos) {
           const float4* cr = reinterpret_cast<const float4*>(p.cos + static_cast<int64_t>(posR) * half + 8 * c);
           const float4* sr = reinterpret_cast<const float4*>(p.sin + static_cast<int64_t>(posR) * half + 8 * c);
-          cs[2 * k] = cr[0];
-          cs[2 * k + 1] = cr[1];
-          sn[2 * k] = sr[0];
-          sn[2 * k + 1] = sr[1];
+          cs[2 * kc] = cr[0];
+          cs[2 * kc + 1] = cr[1];
+          sn[2 * kc] = sr[0];
+          sn[2 * kc + 1] = sr[1];
         }
       }
     }
@@ -426,8 +432,9 @@ struct QTile {
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
       const int R = R0 + dR * k;
-      rope8<T>(lo[k], hi[k], reinterpret_cast<const float*>(&cs[2 * k]),
-               reinterpret_cast<const float*>(&sn[2 * k]), scale);
+      const int kc = kOnePos ? 0 : k;
+      rope8<T>(lo[k], hi[k], reinterpret_cast<const float*>(&cs[2 * kc]),
+               reinterpret_cast<const float*>(&sn[2 * kc]), scale);
       *reinterpret_cast<uint4*>(qs + sw_off(R, c)) = lo[k];
       *reinterpret_cast<uint4*>(qs + kAtom + sw_off(R, c)) = hi[k];
     }
@@ -451,16 +458,15 @@ __global__ void __launch_bounds__(kThreads, 1)
   Bars* bars = reinterpret_cast<Bars*>(smem + kOffBar);
   volatile int32_t* s_abort = &bars->abort;
 
-  // Rotation counters of a launch chain: launch k counts its CTAs' rotations on
-  // word k % 3 and publishes its grid size in word 3 + k % 3; launch k + 1 reads
-  // both before it loads keys of chunk k. Launch k zeroes word (k + 1) % 3 for
-  // the next launch once launch k - 1 is done (launches k - 2 and k - 1, its
-  // users, are then complete). The launcher zeroes all words at a chain's start.
+  // Rotation counter of a launch chain: launch k counts its CTAs' rotations on
+  // word k % 3. Every CTA waits (griddepcontrol.wait) for the previous kernel on
+  // the stream before it touches global memory, so launch k - 1 is complete when
+  // launch k starts its work; CTA 0 of launch k then zeroes word (k + 1) % 3 for
+  // launch k + 1 (its last user, launch k - 2, is long done) before it lets that
+  // launch be scheduled. The launcher zeroes the words at a chain's start.
   const int seq3 = p.launch_seq % 3;
   unsigned long long* const rot_cnt = rot_sync + seq3;
   unsigned long long* const rot_next = rot_sync + (seq3 + 1) % 3;
-  unsigned long long* const rot_prev = rot_sync + (seq3 + 2) % 3;
-  unsigned long long* const grid_words = rot_sync + 3;
   const int G = p.G;
   const int ppt = kBM / G;  // positions per tile (G divides 128, so a power of 2)
   const int lppt = 31 - __clz(ppt);
@@ -496,6 +502,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = bars->tmem_base;
+  // Programmatic launch: the previous kernel on the stream (whatever it is) is
+  // complete and its writes are visible past this point; nothing global is
+  // touched before it.
+  griddep_wait();
 
   auto fail = [&](int bit) {
     if (p.status) atomicOr(p.status, bit);
@@ -523,22 +533,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         // load at once).
         const unsigned long long rot_done = gridDim.x;
         bool rotated = !is_k;
-        // Keys rotated by earlier launches of the chain: launches up to k - 2 are
-        // complete when this one starts; launch k - 1 (maybe still running) has
-        // rotated its chunk's keys once its counter reaches its grid size.
-        if (is_k && p.launch_seq > 0) {
-          const uint64_t t0 = global_timer_ns();
-          for (;;) {
-            const unsigned long long want = ld_acquire_gpu(grid_words + (seq3 + 2) % 3);
-            if (want > 0 && ld_acquire_gpu(rot_prev) >= want) break;
-            __nanosleep(256);
-            if (global_timer_ns() - t0 > 2000000000ull) {
-              fail(kStatusWaitTimeout);
-              break;
-            }
-          }
-          fence_proxy_async_global();
-        }
         Item it;
         for (int L = next_item(p, blockIdx.x, n_items, n_qt, ppt, it); L < n_items && !*s_abort;
              L = next_item(p, L + gridDim.x, n_items, n_qt, ppt, it)) {
@@ -589,17 +583,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else if (warp == kWarpChain) {
       // -------------------- launch chain: counter for the next launch --------------------
       if (lane == 0) {
-        if (blockIdx.x == 0) {  // for the next launch: this launch's grid size
-          atomicExch(grid_words + seq3, static_cast<unsigned long long>(gridDim.x));
-          __threadfence();
-        }
-        griddep_wait();  // launch k - 1 (and so k - 2), the users of word (k + 1) % 3, is done
         if (blockIdx.x == 0) {
           atomicExch(rot_next, 0ull);
-          atomicExch(grid_words + (seq3 + 1) % 3, 0ull);
           __threadfence();
         }
-        griddep_launch_dependents();  // the next launch may start on SMs this one frees
+        griddep_launch_dependents();  // the next launch may be scheduled on SMs this one frees
       }
     } else if (warp == kWarpMma) {
       // ------------------------------ MMA issuer ------------------------------
@@ -728,8 +716,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (Lq < n_items) Lq = next_item(p, Lq + gridDim.x, n_items, n_qt, ppt, iq);
     while (L < n_items) {
       // Sleeping waits: these warps share schedulers with the softmax warps.
+      // o_full follows ml_ready by the last PV: that wait polls without sleeping.
       if (!__all_sync(0xffffffffu, mbar_wait_sleep(&bars->ml_ready, done & 1, 128)) ||
-          !__all_sync(0xffffffffu, mbar_wait_sleep(&bars->o_full, done & 1, 128))) {
+          !__all_sync(0xffffffffu, mbar_wait(&bars->o_full, done & 1))) {
         ok = false;
         break;
       }
@@ -749,19 +738,26 @@ __global__ void __launch_bounds__(kThreads, 1)
       // buffer: columns 0..63 in atom 0, 64..127 in atom 1, 16-byte chunks XOR
       // swizzled by the row.
       uint8_t* qbuf = smem + ((done & 1) ? kOffQ1 : kOffQ0);
+      // 16 columns of each accumulator per step; the loads of step c + 1 are in
+      // flight while step c is merged and staged (one wait::ld per step).
+      uint32_t oa[2][16], ob[2][16];
+      tmem_ld16(lane_addr + 256, oa[0]);
+      tmem_ld16(lane_addr + 384, ob[0]);
+      tmem_wait_ld();
 #pragma unroll
-      for (int c2 = 0; c2 < 4; ++c2) {
-        uint32_t o0[32], o1[32];
-        tmem_ld32(lane_addr + 256 + 32 * c2, o0);
-        tmem_ld32(lane_addr + 384 + 32 * c2, o1);
-        tmem_wait_ld();
+      for (int c2 = 0; c2 < 8; ++c2) {
+        const int cur = c2 & 1;
+        if (c2 + 1 < 8) {
+          tmem_ld16(lane_addr + 256 + 16 * (c2 + 1), oa[cur ^ 1]);
+          tmem_ld16(lane_addr + 384 + 16 * (c2 + 1), ob[cur ^ 1]);
+        }
 #pragma unroll
-        for (int e8 = 0; e8 < 4; ++e8) {
+        for (int e8 = 0; e8 < 2; ++e8) {
           float o[8];
 #pragma unroll
           for (int e = 0; e < 8; ++e) {
-            const float v0 = has0 ? __uint_as_float(o0[e8 * 8 + e]) * s0 : 0.f;
-            const float v1 = has1 ? __uint_as_float(o1[e8 * 8 + e]) * s1 : 0.f;
+            const float v0 = has0 ? __uint_as_float(oa[cur][e8 * 8 + e]) * s0 : 0.f;
+            const float v1 = has1 ? __uint_as_float(ob[cur][e8 * 8 + e]) * s1 : 0.f;
             o[e] = v0 + v1;
           }
           uint4 w;
@@ -769,9 +765,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           w.y = Elem<T>::from2(o[2], o[3]);
           w.z = Elem<T>::from2(o[4], o[5]);
           w.w = Elem<T>::from2(o[6], o[7]);
-          const int ch = c2 * 4 + e8;  // 16-byte chunk of the row, 0..15
+          const int ch = c2 * 2 + e8;  // 16-byte chunk of the row, 0..15
           *reinterpret_cast<uint4*>(qbuf + (ch >> 3) * kAtom + sw_off(r, ch & 7)) = w;
         }
+        if (c2 + 1 < 8) tmem_wait_ld();
       }
       tc_fence_before();
       mbar_arrive(&bars->o_free);  // O may take the next item's first PV
@@ -789,16 +786,29 @@ __global__ void __launch_bounds__(kThreads, 1)
               *reinterpret_cast<const uint4*>(qbuf + (ch >> 3) * kAtom + sw_off(R, ch & 7));
         }
       }
-      __syncwarp();
-      // Item done + 2's query tile into the same buffer: this warp writes rows
-      // 32 quarter .. +31 (the rows it staged), in two rounds of 16 rows.
+      // Item done + 2's query tile into the same buffer, once every warp has
+      // stored its staged rows. Thread t takes rows t / 8 + 32 k (and + 16): with
+      // G >= 4 (ppt <= 32) the four rows of a unit are one position, whose
+      // cos/sin are read once, and both halves' loads are issued together.
       if (Lq < n_items) {
-        QTile<T, kPaged> qn;
+        named_barrier(kBarEpi, kEpiThreads);
+        const int t = threadIdx.x - kWarpEpi * 32;
+        if (ppt <= 32) {
+          QTile<T, kPaged, true> qn;
 #pragma unroll 1
-        for (int rnd = 0; rnd < 2; ++rnd) {
-          const int R0 = quarter * 32 + 16 * rnd + (lane >> 3);
-          qn.load(p, iq, ppt, R0, 4, lane & 7);
-          qn.store(qbuf, p.scale_log2, R0, 4, lane & 7);
+          for (int rnd = 0; rnd < 2; ++rnd) {
+            const int R0 = 16 * rnd + (t >> 3);
+            qn.load(p, iq, ppt, R0, 32, t & 7);
+            qn.store(qbuf, p.scale_log2, R0, 32, t & 7);
+          }
+        } else {
+          QTile<T, kPaged> qn;
+#pragma unroll 1
+          for (int rnd = 0; rnd < 2; ++rnd) {
+            const int R0 = 16 * rnd + (t >> 3);
+            qn.load(p, iq, ppt, R0, 32, t & 7);
+            qn.store(qbuf, p.scale_log2, R0, 32, t & 7);
+          }
         }
         fence_proxy_async_smem();
         named_barrier(kBarEpi, kEpiThreads);
@@ -830,10 +840,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       int Lq = L;
 #pragma unroll 1
       for (int b = 0; b < 2 && Lq < n_items; ++b) {
-        QTile<T, kPaged> qn;
         const int R0 = tid >> 3;
-        qn.load(p, iq, ppt, R0, 32, tid & 7);
-        qn.store(smem + (b ? kOffQ1 : kOffQ0), p.scale_log2, R0, 32, tid & 7);
+        if (ppt <= 32) {  // rows R0 + 32 k share a position
+          QTile<T, kPaged, true> qn;
+          qn.load(p, iq, ppt, R0, 32, tid & 7);
+          qn.store(smem + (b ? kOffQ1 : kOffQ0), p.scale_log2, R0, 32, tid & 7);
+        } else {
+          QTile<T, kPaged> qn;
+          qn.load(p, iq, ppt, R0, 32, tid & 7);
+          qn.store(smem + (b ? kOffQ1 : kOffQ0), p.scale_log2, R0, 32, tid & 7);
+        }
         fence_proxy_async_smem();
         named_barrier(kBarSoftmax, kSoftmaxThreads);
         if (tid == 0) mbar_arrive(&bars->q_ready[b]);
@@ -1135,16 +1151,16 @@ cudaError_t launch_prefill_tc(const RowsParams& p, int dtype, cudaStream_t strea
   if (e != cudaSuccess) return e;
   unsigned long long* rot_sync =
       reinterpret_cast<unsigned long long*>(static_cast<uint8_t*>(p.workspace) + krot_bytes(p));
-  if (p.launch_seq == 0) {  // a chain starts: counter and grid-size words zero
-    e = cudaMemsetAsync(rot_sync, 0, 6 * sizeof(*rot_sync), stream);
+  if (p.launch_seq == 0) {  // a chain starts: its three counter words zero
+    e = cudaMemsetAsync(rot_sync, 0, 3 * sizeof(*rot_sync), stream);
     if (e != cudaSuccess) return e;
   }
-  // Programmatic stream serialization: this launch's CTAs may start on SMs the
-  // previous kernel frees, before it completes; every read of the previous
-  // launches' results waits (griddepcontrol.wait) for its completion. One CTA
-  // per SM, at most one per SM resident, so every CTA of the grid becomes
-  // resident once the previous kernel is done (the rotation counter's waits
-  // rely on it; they are bounded).
+  // Programmatic stream serialization: this launch's CTAs may be scheduled (and
+  // set up their barriers and TMEM) on SMs the previous kernel frees; each then
+  // waits (griddepcontrol.wait) for that kernel's completion before it touches
+  // global memory. One CTA per SM and at most one resident per SM, so every CTA
+  // of the grid is resident once the previous kernel is done (the rotation
+  // counter's waits rely on it; they are bounded).
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = dim3(kThreads);
