@@ -674,6 +674,7 @@ __global__ void __launch_bounds__(HPC * kWph * 32, MINB)
 // window boundary keeps its warps' state in registers into the next window.
 constexpr int kSkMaxList = 768;
 constexpr int kSkMaxSeg = 48;
+constexpr int kSkFastSlots = 16;  // merge rows with at most this many slots load them in one round
 
 struct SkWork {
   const int32_t* cum;        // [S + 1]: blocks before sequence s (cum[S] = T)
@@ -1104,6 +1105,43 @@ __global__ void __launch_bounds__(128) decode_sk_combine_kernel(const DecodePara
     return (i < n && live_slot(i)) ? *reinterpret_cast<const float2*>(ml + 2 * stride * i)
                                    : make_float2(-INFINITY, 0.f);
   };
+  const float* po = w.ws_o + (first * p.Hq + h) * p.D;
+  if (p.D == 128 && n <= kSkFastSlots) {
+    // One round of loads: every slot's (m, l) (lane i: slot i) and this lane's four
+    // columns of every slot's partial, all in flight together; then the weights.
+    float4 v[kSkFastSlots];
+#pragma unroll
+    for (int i = 0; i < kSkFastSlots; ++i) {
+      v[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (i < n && live_slot(i))
+        v[i] = *reinterpret_cast<const float4*>(po + static_cast<int64_t>(i) * stride * 128 +
+                                                4 * lane);
+    }
+    const float2 mi = slot_ml(lane);
+    float M = mi.x;
+#pragma unroll
+    for (int sh = 16; sh > 0; sh >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, sh));
+    const float wi = (M != -INFINITY && mi.x != -INFINITY) ? exp2f(mi.x - M) : 0.f;
+    float L = wi * mi.y;
+#pragma unroll
+    for (int sh = 16; sh > 0; sh >>= 1) L += __shfl_xor_sync(0xffffffffu, L, sh);
+    const float inv = L > 0.f ? 1.f / L : 0.f;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int i = 0; i < kSkFastSlots; ++i) {
+      const float wk = __shfl_sync(0xffffffffu, wi, i);  // 0 for slots past n or skipped
+      acc.x += wk * v[i].x;
+      acc.y += wk * v[i].y;
+      acc.z += wk * v[i].z;
+      acc.w += wk * v[i].w;
+    }
+    T* o4 = out + 4 * lane;
+    o4[0] = static_cast<T>(acc.x * inv);
+    o4[1] = static_cast<T>(acc.y * inv);
+    o4[2] = static_cast<T>(acc.z * inv);
+    o4[3] = static_cast<T>(acc.w * inv);
+    return;
+  }
   const float2 ml0 = slot_ml(lane);
   float M = ml0.x;
   for (int i = lane + 32; i < n; i += 32) M = fmaxf(M, slot_ml(i).x);
@@ -1119,7 +1157,6 @@ __global__ void __launch_bounds__(128) decode_sk_combine_kernel(const DecodePara
 #pragma unroll
   for (int sh = 16; sh > 0; sh >>= 1) L += __shfl_xor_sync(0xffffffffu, L, sh);
   const float inv = L > 0.f ? 1.f / L : 0.f;
-  const float* po = w.ws_o + (first * p.Hq + h) * p.D;
   const bool vec = (p.D & 3) == 0;
   const int per_pass = vec ? 128 : 32;
   for (int d0 = 0; d0 < p.D; d0 += per_pass) {
