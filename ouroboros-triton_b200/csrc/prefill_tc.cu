@@ -734,10 +734,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float den = w0 * a0.y + w1 * a1.y;
       const float inv = den > 0.f ? 1.f / den : 0.f;
       const float s0 = w0 * inv, s1 = w1 * inv;
-      // Rows whose two parities both hold keys take the packed path (warp-uniform);
-      // otherwise a parity without keys is not read (its TMEM may hold anything).
-      const bool both = __all_sync(0xffffffffu, has0 && has1);
-      const uint64_t s0x2 = f2pack(s0, s0), s1x2 = f2pack(s1, s1);
       // Output row r (128 columns, 256 B) staged over query row r of this item's
       // buffer: columns 0..63 in atom 0, 64..127 in atom 1, 16-byte chunks XOR
       // swizzled by the row.
@@ -754,34 +750,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (c2 + 1 < 8) {
           tmem_ld16(lane_addr + 256 + 16 * (c2 + 1), oa[cur ^ 1]);
           tmem_ld16(lane_addr + 384 + 16 * (c2 + 1), ob[cur ^ 1]);
-        } else {
-          // Every load of O has completed (the last wait::ld): O may take the next
-          // item's first PV while the last 16 columns are merged and staged.
-          tc_fence_before();
-          mbar_arrive(&bars->o_free);
         }
 #pragma unroll
         for (int e8 = 0; e8 < 2; ++e8) {
           float o[8];
-          if (both) {
-            // s0 O_0 + s1 O_1 on packed pairs: a multiply and an FMA per two columns
 #pragma unroll
-            for (int e = 0; e < 8; e += 2) {
-              const uint64_t a = f2pack(__uint_as_float(oa[cur][e8 * 8 + e]),
-                                        __uint_as_float(oa[cur][e8 * 8 + e + 1]));
-              const uint64_t b = f2pack(__uint_as_float(ob[cur][e8 * 8 + e]),
-                                        __uint_as_float(ob[cur][e8 * 8 + e + 1]));
-              const float2 v = f2unpack(f2fma(b, s1x2, f2mul(a, s0x2)));
-              o[e] = v.x;
-              o[e + 1] = v.y;
-            }
-          } else {
-#pragma unroll
-            for (int e = 0; e < 8; ++e) {
-              const float v0 = has0 ? __uint_as_float(oa[cur][e8 * 8 + e]) * s0 : 0.f;
-              const float v1 = has1 ? __uint_as_float(ob[cur][e8 * 8 + e]) * s1 : 0.f;
-              o[e] = v0 + v1;
-            }
+          for (int e = 0; e < 8; ++e) {
+            const float v0 = has0 ? __uint_as_float(oa[cur][e8 * 8 + e]) * s0 : 0.f;
+            const float v1 = has1 ? __uint_as_float(ob[cur][e8 * 8 + e]) * s1 : 0.f;
+            o[e] = v0 + v1;
           }
           uint4 w;
           w.x = Elem<T>::from2(o[0], o[1]);
@@ -793,6 +770,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (c2 + 1 < 8) tmem_wait_ld();
       }
+      tc_fence_before();
+      mbar_arrive(&bars->o_free);  // O may take the next item's first PV
       __syncwarp();
       // Two rows per warp-wide store (16 lanes x 16 B each).
 #pragma unroll 4
