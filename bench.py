@@ -437,6 +437,8 @@ def run_ours(args):
         if args.serving_rate <= 0:
             args.serving_rate = 4096.0
         serv = _serving_leg(args, world, rank, device)
+    sapi = (_supervisor_api_leg(args, device)
+            if (world == 1 and not args.no_supervisor_api) else None)
     refk = (_reference_kernel_leg(args, device)
             if (rank == 0 and world == 1 and not args.no_reference_kernel) else None)
     cpu = _cpu_baseline_leg() if (rank == 0 and world == 1 and not args.no_cpu) else None
@@ -490,6 +492,8 @@ def run_ours(args):
             line["prefill"] = pre
         if serv is not None:
             line["serving"] = serv
+        if sapi is not None:
+            line["supervisor_api"] = sapi
         if refk is not None:
             line["reference_kernel"] = refk
         print(json.dumps(line), flush=True)
@@ -701,6 +705,76 @@ def _traffic_from_profile(world: int = 1):
 PREFILL = dict(workload="chunked_prefill_llama3_8b_attention", prompts=8, prompt_len=4096,
                chunk=512, q_heads=32, kv_heads=8, head_dim=128, dtype="bf16", rope_base=500000.0,
                causal=True)
+
+
+def _supervisor_api_leg(args, device):
+    """The Supervisor's single-process API (``Supervisor.decode_step``) on the headline batch.
+
+    One KVPool on this GPU; ``admit_many`` places the 256 sequences (LPT, one pool), the
+    pool's caches hold seeded synthetic K/V and each sequence's length is set as if its
+    tokens had been appended (20 GB through the append kernel would need as much staging).
+    Each step is one ``decode_step(rids, q)`` call: device page tables kept between calls,
+    lengths uploaded, the shard launched through the pool's stateless worker and the rows
+    returned in request order. CUDA events around the calls (host work included); two rows
+    checked against the oracle.
+    """
+    import numpy as np
+    import torch
+
+    from oracle import attention_oracle as ao
+    from src.serving import KVPool, Supervisor
+
+    W = WORKLOAD
+    S = args.seqs if args.seqs > 0 else W["seqs_per_gpu"]
+    lens = _lens(1234, S)
+    max_b = -(-W["ctx_max"] // 64)
+    pool = KVPool(device=device, num_blocks=_pool_blocks(lens), kv_heads=W["kv_heads"],
+                  head_dim=W["head_dim"], dtype=torch.bfloat16, max_positions=max_b * 64,
+                  rope_base=W["rope_base"])
+    g = torch.Generator(device=device).manual_seed(321)
+    pool.k_cache.normal_(0.0, 0.5, generator=g)
+    pool.v_cache.normal_(0.0, 0.5, generator=g)
+    sup = Supervisor(pools=[pool])
+    rids = sup.admit_many(lens)
+    for r, n in zip(rids, lens):
+        sup.seqs[r].length = n
+    q = (torch.randn((S, W["q_heads"], W["head_dim"]), generator=g, device=device) * 0.5
+         ).to(torch.bfloat16)
+    for _ in range(max(args.warmup, 3)):
+        out = sup.decode_step(rids, q)
+    torch.cuda.synchronize(device)
+    stream = torch.cuda.current_stream(device)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        out = sup.decode_step(rids, q)
+    e1.record(stream)
+    torch.cuda.synchronize(device)
+    ms = e0.elapsed_time(e1) / args.steps
+    errs = []
+    cos_np, sin_np = pool.cos.cpu().numpy(), pool.sin.cpu().numpy()
+    for i in sorted(range(S), key=lambda j: (lens[j], j))[:2]:
+        st = sup.seqs[rids[i]]
+        nb = -(-lens[i] // 64)
+        ids = torch.tensor(pool.table.page_table_row(st.head)[:nb], dtype=torch.int64,
+                           device=device)
+        kn = pool.k_cache.index_select(0, ids).float().cpu().numpy()
+        vn = pool.v_cache.index_select(0, ids).float().cpu().numpy()
+        want = ao.decode_attention(np.arange(nb, dtype=np.int32)[None], q[i:i + 1].float().cpu()
+                                   .numpy(), kn, vn, [lens[i]], cos_np, sin_np)
+        errs.append(np.abs(out[i:i + 1].float().cpu().numpy() - want))
+    err = np.concatenate([e.ravel() for e in errs])
+    del sup, pool, q, out
+    torch.cuda.empty_cache()
+    return {
+        "metric": "paged-decode attn tokens/s through Supervisor.decode_step (one process, "
+                  "one pool)",
+        "value": S / (ms / 1000.0), "unit": "tokens/s", "ms_per_step": ms,
+        "steps": args.steps,
+        "check": {"rows": 2, "max_abs": float(err.max()), "mean_abs": float(err.mean()),
+                  "tolerance": {"max_abs": 2e-2, "mean_abs": 2e-3},
+                  "ok": bool(err.max() <= 2e-2 and err.mean() <= 2e-3)},
+    }
 
 
 def _prefill_measure(args, world: int, rank: int, device):
@@ -1170,6 +1244,8 @@ def main() -> int:
                          "within ~0.13 s, so the engine, not the arrivals, sets the time)")
     ap.add_argument("--no-serving", action="store_true",
                     help="skip the serving-trace sub-object of the decode line")
+    ap.add_argument("--no-supervisor-api", action="store_true",
+                    help="skip the Supervisor.decode_step sub-measurement (N = 1)")
     ap.add_argument("--no-reference-kernel", action="store_true",
                     help="skip the reference Triton kernel comparison (N = 1 only)")
     ap.add_argument("--prefill-steps", type=int, default=0,

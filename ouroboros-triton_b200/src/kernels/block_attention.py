@@ -164,16 +164,30 @@ def validate_page_table(page_table, seq_lens, num_phys_blocks: int) -> None:
     (block_attention.py:445-466); here one device pass finds the lowest bad
     entry and 8 bytes come back. Same message texts.
     """
+    _validate_page_table(page_table, seq_lens, num_phys_blocks)
+
+
+def _validate_page_table(page_table, seq_lens, num_phys_blocks: int, with_max_len=False):
+    """validate_page_table; with ``with_max_len`` also returns max(seq_lens), read back
+    in the same transfer as the check's verdict (one synchronisation per call)."""
     _require_cuda()
     S, max_b = page_table.shape
     device = page_table.device
-    report = torch.empty(1, dtype=torch.int64, device=device)
+    report = torch.empty(2, dtype=torch.int64, device=device)
     _native.check(_native.lib().ouro_validate_page_table(
         _ptr(page_table), _ptr(seq_lens), S, max_b, int(num_phys_blocks), _ptr(report),
         _stream_handle(device)), "validate_page_table")
-    key = int(report.item()) & 0xFFFFFFFFFFFFFFFF
+    if with_max_len:
+        if S:
+            report[1:].copy_(seq_lens.max().reshape(1))
+        else:
+            report[1:].zero_()
+        key, max_len = report.tolist()
+    else:
+        key, max_len = int(report[0].item()), 0
+    key &= 0xFFFFFFFFFFFFFFFF
     if key == 0xFFFFFFFFFFFFFFFF:
-        return
+        return max_len
     idx, code = key >> 2, key & 3
     s, n = divmod(idx, max_b) if max_b else (idx, 0)
     if code == 3:
@@ -505,8 +519,7 @@ def block_attention(page_table, q_cache, k_cache, v_cache, seq_lens, cos, sin, b
         raise RuntimeError(f"seq_lens must have shape [{S}], got {tuple(seq_lens.shape)}")
     pt = _as_int32(page_table, "page_table")
     lens = _as_int32(seq_lens, "seq_lens")
-    validate_page_table(pt, lens, n_phys)
-    max_len = int(lens.max().item()) if S else 0
+    max_len = _validate_page_table(pt, lens, n_phys, with_max_len=True)
     if max_len == 0:
         raise RuntimeError("all sequences are empty")
     if cos.shape[0] < max_b * BLOCK_SIZE or sin.shape[0] < max_b * BLOCK_SIZE:

@@ -114,6 +114,7 @@ class SeqState:
     pool: int
     head: int
     length: int  # tokens whose K/V are in the cache
+    blocks: int = 0  # the chain's length in blocks
 
 
 def lpt_placement(lengths, loads) -> list[int]:
@@ -149,6 +150,8 @@ class Supervisor:
         self.device = device if device is not None else (
             self.pools[0].device if self.pools else None)
         self._gpu_workers: dict[int, Worker] = {}
+        # decode_step's device page tables per (pool, rids): rows refreshed when a chain grows
+        self._tables: dict = {}
 
     @property
     def last_request_id(self) -> int:
@@ -267,7 +270,7 @@ class Supervisor:
         head = self.pools[pool].table.allocate_chain(nb)
         self._request_counter += 1
         rid = self._request_counter
-        self.seqs[rid] = SeqState(pool=pool, head=head, length=0)
+        self.seqs[rid] = SeqState(pool=pool, head=head, length=0, blocks=nb)
         return rid
 
     def admit_many(self, lengths) -> list[int]:
@@ -292,11 +295,44 @@ class Supervisor:
             tail = table.chain_tail(st.head)
             for _ in range(-(-(need - have) // BLOCK_SIZE)):
                 tail = table.expand_chain(tail)
+            st.blocks = table.chain_len(st.head)
 
     def finish(self, rid: int) -> None:
         """Frees a sequence's chain and forgets it."""
         st = self.seqs.pop(rid)
         self.pools[st.pool].table.free_chain(st.head)
+        self._tables.clear()  # cached tables may name the freed chain
+
+    def _device_table(self, p: int, rs):
+        """Pool p's page table for ``rs`` on its device, kept between calls.
+
+        The first call exports every row; later calls with the same sequences upload
+        only the rows whose chain grew, and the whole table again only when the
+        longest chain outgrows the kept width (kept in steps of 32 blocks).
+        """
+        import torch
+
+        pool = self.pools[p]
+        heads = tuple(self.seqs[r].head for r in rs)
+        blocks = tuple(self.seqs[r].blocks for r in rs)
+        need = max(blocks)
+        key = (p, tuple(rs))
+        ent = self._tables.get(key)
+        if ent is None or ent["width"] < need or ent["heads"] != heads:
+            width = -(-need // 32) * 32
+            pt = pool.table.export_page_table(list(heads), width)
+            if len(self._tables) >= 64:
+                self._tables.clear()
+            ent = {"width": width, "heads": heads, "blocks": blocks,
+                   "pt": torch.from_numpy(pt).to(pool.device)}
+            self._tables[key] = ent
+        elif ent["blocks"] != blocks:
+            rows = [i for i, (a, b) in enumerate(zip(ent["blocks"], blocks)) if a != b]
+            fresh = pool.table.export_page_table([heads[i] for i in rows], ent["width"])
+            idx = torch.tensor(rows, dtype=torch.long, device=pool.device)
+            ent["pt"].index_copy_(0, idx, torch.from_numpy(fresh).to(pool.device))
+            ent["blocks"] = blocks
+        return ent["pt"], need
 
     def shard(self, rids) -> dict[int, tuple[list[int], object, object]]:
         """Per pool: (rids in order, page table [n, max_b] int32 numpy, lengths)."""
@@ -363,19 +399,27 @@ class Supervisor:
 
         out = torch.empty_like(q)
         index = {r: i for i, r in enumerate(rids)}
+        by_pool: dict[int, list[int]] = {}
+        for r in rids:
+            by_pool.setdefault(self.seqs[r].pool, []).append(r)
         pending = []
-        for p, (rs, pt, lens) in self.shard(rids).items():
+        for p, rs in by_pool.items():
             pool = self.pools[p]
+            pt, _ = self._device_table(p, rs)
+            lens = torch.tensor([self.seqs[r].length for r in rs], dtype=torch.int32)
             sel = torch.tensor([index[r] for r in rs], device=q.device)
+            kw_p = dict(kw)
+            nbs = [-(-self.seqs[r].length // BLOCK_SIZE) for r in rs]
+            kw_p.setdefault("total_blocks", sum(nbs))
+            kw_p.setdefault("max_seq_blocks", max(nbs))
             args = (pool.k_cache, pool.v_cache, pool.cos, pool.sin,
-                    q.index_select(0, sel).to(pool.device),
-                    torch.from_numpy(pt).to(pool.device),
-                    torch.from_numpy(lens).to(pool.device))
+                    q.index_select(0, sel).to(pool.device), pt,
+                    lens.to(pool.device, non_blocking=True))
             for attempt in range(2):
                 worker = self._gpu_worker(p)
                 try:
                     with torch.cuda.device(pool.device):
-                        res = worker.decode(*args, **kw)
+                        res = worker.decode(*args, **kw_p)
                     break
                 except WorkerCrash:
                     worker.kill()

@@ -87,3 +87,30 @@ def test_finish_returns_every_block(cuda):
     for r in rids:
         sup.finish(r)
     assert [p.table.num_free for p in sup.pools] == [40, 40]
+
+
+def test_decode_loop_across_block_boundaries_matches_oracle(cuda):
+    """decode_step keeps each pool's page table on the device between calls and refreshes
+    only the rows whose chain grew (and the whole table when the longest chain outgrows
+    the kept width, 32 blocks): a few decode steps whose appended tokens cross block
+    boundaries, each checked against the oracle."""
+    sup = Supervisor(pools=_pools(2, blocks=160))
+    lens = [63, 127, 2045, 64, 300]
+    rids = sup.admit_many(lens)
+    g = torch.Generator(device="cuda").manual_seed(7)
+    L = max(lens)
+    k_new = (torch.randn(len(lens), 2, L, 128, generator=g, device="cuda") * 0.5).bfloat16()
+    v_new = (torch.randn(len(lens), 2, L, 128, generator=g, device="cuda") * 0.5).bfloat16()
+    sup.append_kv(rids, k_new, v_new, counts=lens)
+    for step in range(4):
+        n_new = 1 if step < 3 else 5     # the last step takes the 2045-token chain past 32 blocks
+        k1 = (torch.randn(len(lens), 2, n_new, 128, generator=g, device="cuda") * 0.5).bfloat16()
+        v1 = (torch.randn(len(lens), 2, n_new, 128, generator=g, device="cuda") * 0.5).bfloat16()
+        sup.append_kv(rids, k1, v1)
+        q = (torch.randn(len(lens), 16, 128, generator=g, device="cuda") * 0.5).bfloat16()
+        out = sup.decode_step(rids, q)
+        want = _oracle_rows(sup, rids, q)
+        err = np.abs(out.float().cpu().numpy() - want)
+        assert err.max() < 2e-2 and err.mean() < 2e-3, (step, err.max(), err.mean())
+    assert sup.seqs[rids[2]].length == 2045 + 3 + 5 and sup.seqs[rids[2]].blocks == 33
+    assert sup.seqs[rids[0]].blocks == 2 and sup.seqs[rids[3]].blocks == 2
