@@ -389,19 +389,30 @@ def run_ours(args):
             k1[i].record(stream)
         return run
 
+    # The step time comes from steps with nothing but the work on the stream; the decode
+    # kernels' own time from the same K steps again with events around the decode launches
+    # (an event between two kernels keeps the second from starting early, as the
+    # programmatic launch chain of the exchange and decode kernels otherwise lets it).
     with ClockSampler(device.index) as clk:
         barrier()
         start.record(stream)
         for i in range(args.steps):
-            sh.step(launch_timed(i), q_batch)
+            sh.step(call.launch, q_batch)
         stop.record(stream)
+        barrier()
+        start2, stop2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start2.record(stream)
+        for i in range(args.steps):
+            sh.step(launch_timed(i), q_batch)
+        stop2.record(stream)
         barrier()
     ms = start.elapsed_time(stop)
     kern_ms = sum(a.elapsed_time(b) for a, b in zip(k0, k1)) / args.steps
-    t = torch.tensor([ms, kern_ms], dtype=torch.float64, device=device)
+    ev_step_ms = start2.elapsed_time(stop2) / args.steps
+    t = torch.tensor([ms, kern_ms, ev_step_ms], dtype=torch.float64, device=device)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms_max, kern_max = float(t[0]), float(t[1])
+    ms_max, kern_max, ev_step_max = float(t[0]), float(t[1]), float(t[2])
     step_ms = ms_max / args.steps
     value = S * args.steps / (ms_max / 1000.0)
     kv_bytes_all = sum(lens) * hkv * d * 2 * 2
@@ -474,12 +485,15 @@ def run_ours(args):
                          "peak_source": peak_kind,
                          "algorithmic_bytes_per_launch": kv_bytes_all // world,
                          "per_rank_GB/s": rates,
-                         "note": "decode + combine launches timed with CUDA events inside the "
-                                 "timed region; K+V bytes once per KV head; achieved = the "
-                                 "batch's bytes / N over the slowest rank's kernel time"},
-            "step_breakdown_ms": {"decode_kernels_max_rank": kern_max,
-                                  "step": step_ms,
-                                  "outside_kernels": step_ms - kern_max},
+                         "note": "prep + decode + merge launches timed with CUDA events "
+                                 "around them in K more steps right after the timed ones "
+                                 "(same clocks record); K+V bytes once per KV head; "
+                                 "achieved = the batch's bytes / N over the slowest rank's "
+                                 "kernel time"},
+            "step_breakdown_ms": {"step": step_ms,
+                                  "step_with_kernel_events": ev_step_max,
+                                  "decode_kernels_max_rank": kern_max,
+                                  "outside_kernels": ev_step_max - kern_max},
             "cpu_baseline": cpu,
             "e2e": e2e,
             "gpu_launches": launches,
@@ -1152,9 +1166,28 @@ def _serving_measure(args, world: int, rank: int, device, rate: float):
                  slots=1024)
     if world > 1:
         dist.barrier()
+    class _DeviceTimer:
+        """Token times from CUDA events recorded after each step (no per-step sync)."""
+
+        def start(self):
+            self.e0 = torch.cuda.Event(enable_timing=True)
+            self.e0.record()
+
+        def mark(self):
+            ev = torch.cuda.Event(enable_timing=True)
+            ev.record()
+            return ev
+
+        def sync(self):
+            torch.cuda.synchronize(device)
+
+        def seconds(self, ev):
+            return self.e0.elapsed_time(ev) / 1000.0
+
     with ClockSampler(device.index) as clk:
-        # one synchronize per step: token times are completion times
-        st = eng.run(mine, sync=lambda: torch.cuda.synchronize(device))
+        # the host runs ahead of the device; token times are the device completion times of
+        # the steps that produced them (events), read once at the end
+        st = eng.run(mine, timer=_DeviceTimer())
         torch.cuda.synchronize(device)
     dec_ms, pre_ms = be.attn_ms("decode"), be.attn_ms("prefill")
     vals = torch.tensor([st["generated_tokens"], st["wall_s"], be.kv_bytes, dec_ms],

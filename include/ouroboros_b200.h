@@ -232,12 +232,13 @@ typedef struct ouro_attention_args {
   const int32_t* scope_hi;    /* position; the query at position i keeps key j when tags[j]
                                  or lo[i] <= j < hi[i] (both NULL with scope_tags NULL) */
   int32_t launch_seq;         /* tensor-core path: 0 starts a chain of launches on one
-                                 workspace (the library zeroes its counters first); k > 0
-                                 marks the k-th launch after it on the same stream (chunked
-                                 prefill: chunk k). A chained launch may start while the
-                                 previous one finishes (programmatic dependent launch) and
-                                 reads the keys that launch rotated once its rotations are
-                                 done; the launches of a chain must write distinct outputs. */
+                                 workspace (the library zeroes its counter words first);
+                                 k > 0 marks the k-th launch after it on the same workspace
+                                 and stream (chunked prefill: chunk k), whose counter word
+                                 the previous launch of the chain zeroed. Every launch is
+                                 programmatic (its CTAs may be scheduled while the previous
+                                 kernel on the stream finishes) and touches no global memory
+                                 before that kernel has completed. */
 } ouro_attention_args;
 
 /* Kernel choice and the workspace the tensor-core path needs

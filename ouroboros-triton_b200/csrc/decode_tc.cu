@@ -1019,12 +1019,18 @@ __global__ void __launch_bounds__(1024) decode_sk_prep_kernel(const DecodeParams
                                                               int32_t P) {
   __shared__ int32_t warp_sum[32];
   __shared__ int32_t carry;
+  // A copy of cum for the CTAs' binary searches when the batch fits (dependent
+  // loads from shared memory instead of global).
+  constexpr int kCumSmem = 4096;
+  __shared__ int32_t s_cum[kCumSmem + 1];
+  const bool cum_in_smem = p.S <= kCumSmem;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   griddep_wait();  // the lengths and tables written by earlier work on the stream
   griddep_launch_dependents();
   if (tid == 0) {
     carry = 0;
     cum[0] = 0;
+    s_cum[0] = 0;
   }
   __syncthreads();
   for (int base = 0; base < p.S; base += 1024) {
@@ -1048,18 +1054,22 @@ __global__ void __launch_bounds__(1024) decode_sk_prep_kernel(const DecodeParams
     }
     __syncthreads();
     const int incl = v + (warp > 0 ? warp_sum[warp - 1] : 0) + carry;
-    if (s < p.S) cum[s + 1] = incl;
+    if (s < p.S) {
+      cum[s + 1] = incl;
+      if (cum_in_smem) s_cum[s + 1] = incl;
+    }
     __syncthreads();
     if (tid == 1023) carry = incl;
     __syncthreads();
   }
   const int64_t T_all = carry;
+  const int32_t* cs = cum_in_smem ? s_cum : cum;
   for (int c = tid; c < P; c += 1024) {
     const int64_t x = static_cast<int64_t>(c) * T_all / P;
     int lo_s = 0, hi_s = p.S > 0 ? p.S - 1 : 0;
     while (lo_s < hi_s) {  // largest s with cum[s] <= x
       const int mid = (lo_s + hi_s + 1) >> 1;
-      if (cum[mid] <= x) lo_s = mid;
+      if (cs[mid] <= x) lo_s = mid;
       else hi_s = mid - 1;
     }
     first_seq[c] = lo_s;

@@ -60,6 +60,8 @@ class Request:
     admit_time: float | None = None
     first_token_time: float | None = None
     finish_time: float | None = None
+    first_token_step: int | None = None  # the step that produced the first token
+    finish_step: int | None = None       # the step that produced the last one
     tags: np.ndarray | None = field(default=None, repr=False)   # uint8 [total], 1 = GLOBAL
     span_start: np.ndarray | None = field(default=None, repr=False)
     span_end: np.ndarray | None = field(default=None, repr=False)
@@ -169,6 +171,7 @@ class Engine:
                         r.last_token = int(tokens[i])
                     r.generated = 1
                     r.first_token_time = now
+                    r.first_token_step = self.steps
         if dec:
             pos = np.asarray([r.prompt_len + r.generated - 1 for r in dec], np.int32)
             tokens = self.backend.decode(dec, pos)
@@ -185,7 +188,9 @@ class Engine:
             if r.generated >= r.max_new:
                 if r.first_token_time is None:
                     r.first_token_time = now
+                    r.first_token_step = self.steps - 1
                 r.finish_time = now
+                r.finish_step = self.steps - 1
                 self.table.free_chain(r.head)
                 self.backend.release(r)
                 self.free_slots.append(r.slot)
@@ -196,20 +201,38 @@ class Engine:
         self.running = keep
 
     def run(self, reqs, *, clock=time.perf_counter, sleep=time.sleep, sync=None,
-            max_steps: int = 10 ** 9) -> dict:
+            timer=None, max_steps: int = 10 ** 9) -> dict:
         """Serves ``reqs`` with arrivals on ``clock`` (seconds since the call) and
-        returns the trace's statistics; ``sync`` (optional) waits for the
-        device before a timestamp is taken."""
+        returns the trace's statistics. ``sync`` (optional) waits for the device
+        after every step, so host timestamps follow the device. ``timer``
+        (optional, instead) keeps the host free to run ahead: ``timer.start()``
+        at the start, ``timer.mark()`` after every step that did work (a device
+        marker, e.g. a CUDA event), ``timer.sync()`` once at the end and
+        ``timer.seconds(marker)`` since the start; first-token and finish times
+        are then those of the steps that produced the tokens."""
         self.submit(reqs)
+        marks = []
+        if timer is not None:
+            timer.start()
         t0 = clock()
         while not self.idle and self.steps < max_steps:
             now = clock() - t0
             if not self.running and self.waiting and self.waiting[0].arrival > now:
                 sleep(min(0.001, self.waiting[0].arrival - now))
                 continue
+            before = self.steps
             self.step(now)
+            if timer is not None and self.steps > before:
+                marks.append(timer.mark())
             if sync is not None:
                 sync()
+        if timer is not None:
+            timer.sync()
+            for r in self.finished:
+                if r.first_token_step is not None:
+                    r.first_token_time = timer.seconds(marks[r.first_token_step])
+                if r.finish_step is not None:
+                    r.finish_time = timer.seconds(marks[r.finish_step])
         wall = clock() - t0
         return self.stats(wall)
 

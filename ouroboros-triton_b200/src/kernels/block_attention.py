@@ -577,8 +577,9 @@ class PrefillCall:
 
         ``launch_seq``: the call's position in a chain of launches that share
         ``workspace`` and follow each other on one stream (chunk k of a chunked
-        prefill: k). A follow-up launch (k > 0) overlaps the previous one's tail
-        and must not share its ``out``; 0 (the default) starts a chain."""
+        prefill: k); 0 (the default) starts a chain. A launch's CTAs may be
+        scheduled while the previous kernel on the stream finishes, and wait for
+        it before they touch memory."""
         _require_cuda()
         if kernel not in _KERNELS:
             raise RuntimeError(f"kernel must be one of {sorted(_KERNELS)}, got {kernel!r}")

@@ -111,6 +111,43 @@ def test_engine_serves_every_request_and_frees_every_block(pool_blocks, chunk, b
     assert st["peak_blocks"] <= pool_blocks
 
 
+def test_engine_timer_gives_token_times_of_the_producing_steps():
+    """With a timer (no per-step sync) first-token and finish times are the marks of the
+    steps that produced those tokens, read after the run."""
+    tr = make_trace(12, rate=500.0, median=200, sigma=0.5, lo=16, hi=800, max_new=5, seed=9)
+    table = BlockTable(400)
+    be = RecordingBackend(table)
+    eng = Engine(table, be, chunk=128, prefill_tokens=256, slots=32)
+    be.engine = eng
+
+    class StepTimer:                      # mark i resolves to 10 + i seconds
+        def __init__(self):
+            self.marks, self.synced = 0, False
+
+        def start(self):
+            self.marks = 0
+
+        def mark(self):
+            self.marks += 1
+            return self.marks - 1
+
+        def sync(self):
+            self.synced = True
+
+        def seconds(self, m):
+            return 10.0 + m
+
+    timer = StepTimer()
+    clock = FakeClock(0.001)
+    st = eng.run(tr, clock=clock, sleep=clock.sleep, timer=timer)
+    assert timer.synced and timer.marks == eng.steps == st["steps"]
+    for r in tr:
+        assert r.first_token_time == 10.0 + r.first_token_step
+        assert r.finish_time == 10.0 + r.finish_step
+        # prefill completes at one step; the remaining max_new - 1 tokens take one step each
+        assert r.finish_step - r.first_token_step >= r.max_new - 1
+
+
 def test_engine_prefill_respects_chunk_and_budget():
     tr = [Request(i, 0.0, L, 3, random_segments(random.Random(i), L + 3))
           for i, L in enumerate([1000, 70, 2500, 5])]
