@@ -694,10 +694,15 @@ static_assert(sizeof(SkSeg) == 32, "segment record");
 // Lists one window of CTA c's share, starting at sequence *walk_s, flat block
 // *walk_flat, into segs / list_b (piece index << 24 | block) / list_p; called by
 // all 32 lanes of warp 0. Returns the number of pieces; *n_items the entries.
+// on_listed(n, s) runs on all lanes after each group of up to 32 entries is
+// listed (entries [0, n) are visible to the warp; the latest ones belong to
+// sequence s), so the first stages can be issued while the rest is listed.
+template <typename OnListed>
 __device__ __forceinline__ int sk_build_window(const DecodeParams& p, const SkWork& w, int c,
                                                int64_t flat_hi, bool carry_in, SkSeg* segs,
                                                int32_t* list_b, int32_t* list_p, int* walk_s,
-                                               int64_t* walk_flat, int* n_items, bool* carry_out) {
+                                               int64_t* walk_flat, int* n_items, bool* carry_out,
+                                               OnListed&& on_listed) {
   const int lane = threadIdx.x & 31;
   int s = *walk_s;
   int64_t flat = *walk_flat;
@@ -776,6 +781,8 @@ __device__ __forceinline__ int sk_build_window(const DecodeParams& p, const SkWo
         }
         n += __popc(bal);
         b += cnt;
+        __syncwarp();
+        on_listed(n, sj);
       }
       if (lane == 0) {
         SkSeg sg;
@@ -890,8 +897,24 @@ __global__ void __launch_bounds__(HPC * kWph * 32, 1)
       int64_t wf = s_walk_flat;
       int nitems = 0;
       bool carry = false;
+      // In the first window the first stages go out as soon as their blocks are
+      // listed (the ring is empty); later windows issue after the listing.
+      int early = 0;
+      const bool first_window = it_base == 0;
+      auto on_listed = [&](int n_listed, int s_cur) {
+        if (!first_window || lane != 0) return;
+        for (; early < S_ && (early >> 2) < n_listed; ++early) {
+          const int e = early >> 2;
+          issue_stage<D, HPC>(&tm_k, &tm_v, &tm_cos, &tm_sin, p,
+                              stages + (early % S_) * L::kStage, &full[early % S_],
+                              tags + (early % S_) * 16, &s_use[early % S_], early / S_, s_cur,
+                              kvh0, list_b[e] & 0xffffff, list_p[e], early & 3, pol_stream,
+                              pol_keep);
+          s_issued = early + 1;
+        }
+      };
       const int nseg = sk_build_window(p, w, c, flat_hi, s_carry != 0, segs, list_b, list_p, &ws,
-                                       &wf, &nitems, &carry);
+                                       &wf, &nitems, &carry, on_listed);
       if (lane == 0) {
         s_nseg = nseg;
         s_nitems = nitems;
@@ -899,7 +922,7 @@ __global__ void __launch_bounds__(HPC * kWph * 32, 1)
         s_walk_flat = wf;
         s_carry = carry ? 1 : 0;
         const int total = nitems * 4;
-        for (int i = 0; i < S_ && i < total; ++i) {
+        for (int i = early; i < S_ && i < total; ++i) {
           const int git = it_base + i;
           const int e = i >> 2;
           issue_stage<D, HPC>(&tm_k, &tm_v, &tm_cos, &tm_sin, p, stages + (git % S_) * L::kStage,
