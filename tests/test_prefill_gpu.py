@@ -276,3 +276,50 @@ def test_chained_chunk_launches_vs_oracle(cuda, chunks):
         assert int(status.item()) == 0
         for c in range(chunks):
             _check(results[c], want[:, :, c * L:(c + 1) * L], f"chunk {c}")
+
+
+def test_chained_launches_with_kv_append_between_them(cuda):
+    """Serving-style chunked prefill with nothing synchronised: before each chunk's launch
+    (launch_seq = chunk, one shared workspace) a kv-append kernel writes that chunk's K/V
+    into the cache. Every prefill thread waits for the previous kernel on the stream before
+    it touches memory, so each launch reads the keys and values just appended."""
+    hq, hkv, d, L, chunks, S = 32, 8, 128, 256, 4, 3
+    total = L * chunks
+    bt = BlockTable(S * total // 64 + 8)
+    heads = [bt.allocate_chain(total // 64) for _ in range(S)]
+    ptd = torch.from_numpy(build_page_table_array(bt, heads, pad_to=total // 64)).cuda()
+    g = torch.Generator(device="cuda").manual_seed(11)
+    kc = torch.zeros(S * total // 64 + 8, hkv, 64, d, dtype=torch.bfloat16, device="cuda")
+    vc = torch.zeros_like(kc)
+    cos, sin = ao.rope_tables(total, d, 500000.0)
+    cos_d, sin_d = torch.from_numpy(cos).cuda(), torch.from_numpy(sin).cuda()
+    q_all = (torch.randn(S, hq, total, d, generator=g, device="cuda") * 0.5).bfloat16()
+    k_all = (torch.randn(S, hkv, total, d, generator=g, device="cuda") * 0.5).bfloat16()
+    v_all = (torch.randn(S, hkv, total, d, generator=g, device="cuda") * 0.5).bfloat16()
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    calls, ws = [], None
+    for c in range(chunks):                     # checked and prepared before any launch
+        pt_c = ptd.clone()
+        pt_c[:, (c + 1) * L // 64:] = -1
+        calls.append(ba.PrefillCall(
+            pt_c, q_all[:, :, c * L:(c + 1) * L].contiguous(), kc, vc,
+            torch.full((S,), c * L, dtype=torch.int32, device="cuda"),
+            torch.full((S,), (c + 1) * L, dtype=torch.int32, device="cuda"), cos_d, sin_d,
+            kernel="tc", status=status, workspace=ws,
+            krot_valid=torch.full((S,), c * L, dtype=torch.int32), launch_seq=c))
+        ws = calls[-1].workspace
+    start = [torch.full((S,), c * L, dtype=torch.int32, device="cuda") for c in range(chunks)]
+    cnt = torch.full((S,), L, dtype=torch.int32, device="cuda")
+    outs = []
+    for c in range(chunks):                     # append, attend, append, attend, ... unsynchronised
+        ba.paged_kv_append(k_all[:, :, c * L:(c + 1) * L].contiguous(),
+                           v_all[:, :, c * L:(c + 1) * L].contiguous(), ptd, start[c], cnt, kc, vc)
+        outs.append(calls[c].launch())
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    pt_np = build_page_table_array(bt, heads, pad_to=total // 64)
+    want = ao.prefill_attention(pt_np, q_all.float().cpu().numpy(), kc.float().cpu().numpy(),
+                                vc.float().cpu().numpy(), [0] * S, [total] * S, cos, sin,
+                                causal=True)
+    for c in range(chunks):
+        _check(outs[c], want[:, :, c * L:(c + 1) * L], f"chunk {c}")
