@@ -311,6 +311,14 @@ class StandInBackend:
         self._stage = [torch.empty(8 * slots, dtype=torch.int32, pin_memory=True) for _ in range(2)]
         self._stage_done = [None, None]
         self._flip = 0
+        # decode inputs gathered per step into fixed buffers, and one prepared decode call per
+        # batch size over their first n rows (checks, plan and workspace done once per size)
+        self._dec = {"pt": torch.full((slots, self.max_blocks), -1, dtype=torch.int32, device=dev),
+                     "q": torch.empty(slots, self.hq, self.d, dtype=dt, device=dev),
+                     "lens": torch.zeros(slots, dtype=torch.int32, device=dev),
+                     "tags": torch.zeros(slots, width, dtype=torch.uint8, device=dev),
+                     "span": torch.zeros(slots, 2, dtype=torch.int32, device=dev)}
+        self._dec_calls = {}
         self.kv_bytes = 0
         self.attn_events = {"prefill": [], "decode": []}  # (start, end) CUDA event pairs
         self.last_prefill = self.last_decode = None        # inputs / outputs of the last call
@@ -404,8 +412,21 @@ class StandInBackend:
                                   torch.where(fin != 0, nxt, self.last_tok.index_select(0, slots)))
         return None
 
+    def _decode_call(self, n):
+        """The prepared decode launch over the first n rows of the decode buffers."""
+        call = self._dec_calls.get(n)
+        if call is None:
+            from .kernels.block_attention import DecodeCall
+
+            b = self._dec
+            call = DecodeCall(b["pt"][:n], b["q"][:n], self.pool.k_cache, self.pool.v_cache,
+                              b["lens"][:n], self.pool.cos, self.pool.sin,
+                              scope=(b["tags"][:n], b["span"][:n]), validate=False)
+            self._dec_calls[n] = call
+        return call
+
     def decode(self, reqs, pos):
-        from .kernels.block_attention import block_attention_decode, paged_kv_append
+        from .kernels.block_attention import paged_kv_append
 
         torch = self.torch
         dev = self.device
@@ -414,17 +435,20 @@ class StandInBackend:
         idx = self._upload([[r.slot for r in reqs], pos, [a for a, _ in spans],
                             [b for _, b in spans]])
         slots, start = idx[0], idx[1]
-        span = idx[2:4].t().contiguous()
+        b = self._dec
+        pt, lens, tags, span = b["pt"][:n], b["lens"][:n], b["tags"][:n], b["span"][:n]
+        torch.index_select(self.pt, 0, slots, out=pt)
+        torch.index_select(self.tags, 0, slots, out=tags)
+        span.copy_(idx[2:4].t())
+        torch.add(start, 1, out=lens)
         q, k, v = self._qkv(self.last_tok.index_select(0, slots))   # [n, H, D]
-        pt = self.pt.index_select(0, slots)
+        b["q"][:n].copy_(q)
+        q = b["q"][:n]
         paged_kv_append(k[:, :, None].contiguous(), v[:, :, None].contiguous(), pt, start,
                         torch.ones(n, dtype=torch.int32, device=dev), self.pool.k_cache,
                         self.pool.v_cache)
-        lens = start + 1
-        tags = self.tags.index_select(0, slots)
-        out = self._timed("decode", lambda: block_attention_decode(
-            pt, q.contiguous(), self.pool.k_cache, self.pool.v_cache, lens, self.pool.cos,
-            self.pool.sin, scope=(tags, span), validate=False))
+        call = self._decode_call(n)
+        out = self._timed("decode", call.launch)
         self.kv_bytes += int(pos.astype(np.int64).sum() + n) * self.hkv * self.d * 2 * \
             self.pool.k_cache.element_size()
         self.last_decode = (pt, q, lens, tags, span, out)

@@ -219,9 +219,14 @@ def _scope_tensors(scope, S: int, device):
     if tags.dim() != 2 or tags.shape[0] != S:
         raise RuntimeError(f"scope tags must be [S={S}, L], got {tuple(tags.shape)}")
     L = tags.shape[1]
-    W = max(_SM_SCOPE_ALIGN, -(-L // _SM_SCOPE_ALIGN) * _SM_SCOPE_ALIGN)
-    padded = torch.zeros((S, W), dtype=torch.uint8, device=device)
-    padded[:, :L] = tags.to(device=device, dtype=torch.uint8)
+    if (tags.dtype == torch.uint8 and tags.device == torch.device(device) and L > 0
+            and L % _SM_SCOPE_ALIGN == 0 and tags.is_contiguous()
+            and tags.data_ptr() % _SM_SCOPE_ALIGN == 0):
+        padded = tags  # already in the kernel's layout: used in place
+    else:
+        W = max(_SM_SCOPE_ALIGN, -(-L // _SM_SCOPE_ALIGN) * _SM_SCOPE_ALIGN)
+        padded = torch.zeros((S, W), dtype=torch.uint8, device=device)
+        padded[:, :L] = tags.to(device=device, dtype=torch.uint8)
     span = _on(span, device, torch.int32)
     if span is None or tuple(span.shape) != (S, 2):
         raise RuntimeError(f"scope span must be [S={S}, 2]")
