@@ -23,7 +23,7 @@ by ``cases.py``:
 * ``alloc_scripts.json`` op-by-op results of the reference Python BlockTable
 * ``scope_masks.json`` block_sparse_mask for seeded span sets
 
-The GPU box never runs this script; tests read only the recorded files.
+Only this script needs the reference checkout; the tests read the recorded files.
 """
 
 from __future__ import annotations
