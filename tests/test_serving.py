@@ -131,6 +131,37 @@ def test_admit_reserve_shard_finish_bookkeeping():
     assert [p.table.num_free for p in sup.pools] == [64, 64] and sum(free) < 128
 
 
+def test_decode_tables_kept_between_calls_and_refreshed_by_row():
+    """decode_step's per-pool page tables: exported once, then only the rows whose chain
+    grew are rewritten; a chain longer than the kept width (steps of 32 blocks) brings a
+    full export; a finished sequence drops the kept tables."""
+    sup = Supervisor(pools=_cpu_pools(1, blocks=256))
+    rids = sup.admit_many([100, 64, 1900])
+    for r, n in zip(rids, [100, 64, 1900]):
+        sup.seqs[r].length = n
+
+    def rows_ok(pt):
+        table = sup.pools[0].table
+        for row, r in zip(pt, rids):
+            chain = list(table.walk(sup.seqs[r].head))
+            assert row[:len(chain)].tolist() == chain
+            assert (row[len(chain):] == -1).all()
+
+    pt, widest = sup._device_table(0, rids)
+    assert tuple(pt.shape) == (3, 32) and widest == 30
+    rows_ok(pt)
+    sup.reserve(rids[1], 10)                      # 64 -> 74 tokens: one more block
+    pt2, _ = sup._device_table(0, rids)
+    assert pt2.data_ptr() == pt.data_ptr()        # same kept table, one row rewritten
+    rows_ok(pt2)
+    sup.reserve(rids[2], 200)                     # 1900 -> 2100 tokens: 33 blocks > 32
+    pt3, widest = sup._device_table(0, rids)
+    assert tuple(pt3.shape) == (3, 64) and widest == 33
+    rows_ok(pt3)
+    sup.finish(rids[0])
+    assert sup._tables == {}
+
+
 def test_admission_refuses_when_no_pool_has_room():
     sup = Supervisor(pools=_cpu_pools(2, blocks=4))
     sup.admit(4 * 64)
