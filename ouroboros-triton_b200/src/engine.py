@@ -413,16 +413,21 @@ class StandInBackend:
         return None
 
     def _decode_call(self, n):
-        """The prepared decode launch over the first n rows of the decode buffers."""
-        call = self._dec_calls.get(n)
+        """The prepared decode launch over the first m >= n rows of the decode buffers, m
+        rounded up to a multiple of 8 (rows n .. m - 1 get length 0: no keys, zero output),
+        so a run keeps at most slots / 8 prepared calls."""
+        m = min(-(-n // 8) * 8, self._dec["lens"].shape[0])
+        if m > n:
+            self._dec["lens"][n:m].zero_()
+        call = self._dec_calls.get(m)
         if call is None:
             from .kernels.block_attention import DecodeCall
 
             b = self._dec
-            call = DecodeCall(b["pt"][:n], b["q"][:n], self.pool.k_cache, self.pool.v_cache,
-                              b["lens"][:n], self.pool.cos, self.pool.sin,
-                              scope=(b["tags"][:n], b["span"][:n]), validate=False)
-            self._dec_calls[n] = call
+            call = DecodeCall(b["pt"][:m], b["q"][:m], self.pool.k_cache, self.pool.v_cache,
+                              b["lens"][:m], self.pool.cos, self.pool.sin,
+                              scope=(b["tags"][:m], b["span"][:m]), validate=False)
+            self._dec_calls[m] = call
         return call
 
     def decode(self, reqs, pos):
@@ -448,7 +453,7 @@ class StandInBackend:
                         torch.ones(n, dtype=torch.int32, device=dev), self.pool.k_cache,
                         self.pool.v_cache)
         call = self._decode_call(n)
-        out = self._timed("decode", call.launch)
+        out = self._timed("decode", call.launch)[:n]
         self.kv_bytes += int(pos.astype(np.int64).sum() + n) * self.hkv * self.d * 2 * \
             self.pool.k_cache.element_size()
         self.last_decode = (pt, q, lens, tags, span, out)
