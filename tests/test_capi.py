@@ -160,3 +160,24 @@ def test_rows_argument_builder_marshals_every_field():
                           None, H, 128, True, None, "auto")
     assert lib.ouro_attention_plan(ctypes.byref(dense), ctypes.byref(need),
                                    ctypes.byref(tc)) == 0
+
+
+def test_scope_tags_in_kernel_layout_are_used_in_place():
+    """Decode's token scope: uint8 tags whose rows are a multiple of 16 bytes, contiguous
+    and 16-byte aligned are handed to the kernel as they are (the serving engine's per-slot
+    tags); anything else is copied into a zero-padded [S, 16 k] buffer."""
+    import torch
+
+    from src.kernels.block_attention import _scope_tensors
+
+    dev = torch.device("cpu")
+    tags = torch.zeros(4, 32, dtype=torch.uint8)
+    span = torch.zeros(4, 2, dtype=torch.int32)
+    t, s = _scope_tensors((tags, span), 4, dev)
+    assert t.data_ptr() == tags.data_ptr() and s.data_ptr() == span.data_ptr()
+    ragged = torch.ones(4, 20, dtype=torch.bool)
+    t2, _ = _scope_tensors((ragged, span), 4, dev)
+    assert tuple(t2.shape) == (4, 32) and t2.dtype == torch.uint8
+    assert t2[:, :20].all() and not t2[:, 20:].any()
+    t3, _ = _scope_tensors((tags[:, :16], span), 4, dev)   # rows not contiguous: copied
+    assert t3.data_ptr() != tags.data_ptr() and tuple(t3.shape) == (4, 16)
